@@ -1,0 +1,305 @@
+"""Benchmark of the Q4_K decode GEMV (TinyLlama-1.1B
+ffn_up, W = 5632 x 2048 Q4_K, x = f32[2048]).
+
+One step = one GEMV over each of N_COPIES distinct, seeded copies of W
+(415 MB in total, > 3x the 126 MB L2, so every timed launch streams its
+weights from HBM), launched back to back with programmatic dependent launch
+and replayed as one CUDA graph.  `value` is algorithmic bytes (W + x + y per
+GEMV) per second with inputs resident in HBM; `e2e` is the same metric
+through the C-ABI context API with host buffers (x copied H2D from pinned
+memory, every y read back D2H, inside the timed region).
+
+`--impl reference` times the reference's CPU algorithm (the oracle port in
+oracle/; the Zig reference cannot be compiled here) on all host threads.
+Multi-GPU (torchrun): every rank runs an independent replica (the GEMV
+shards by rows with no exchange), value = all ranks' bytes / max rank time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, K = 5632, 2048
+N_COPIES = 64
+Q4_K = 12
+W_BYTES = M * (K // 256) * 144
+ALG_BYTES = W_BYTES + 4 * K + 4 * M  # per GEMV (6,518,784 B)
+METRIC = "Q4_K GEMV HBM GB/s (TinyLlama ffn_up 5632x2048, batch 1)"
+CONFIG = {"workload": "q4_k_gemv_5632x2048", "m": M, "k": K, "quant": "Q4_K", "weight_copies": N_COPIES,
+          "l2": "inputs > L2: 64 distinct weight copies = 415 MB per step"}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    return int(os.environ.get("RANK", "0")), ws, int(os.environ.get("LOCAL_RANK", "0"))
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index = index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.p:
+            time.sleep(0.15)
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            f = [s.strip() for s in line.split(",")]
+            if len(f) >= 8:
+                try:
+                    rows.append((float(f[1]), float(f[2]), f[4:8]))
+                except ValueError:
+                    pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": rows[0][1], "reasons": reasons,
+                "samples": len(rows)}
+
+
+def make_weights(rank: int):
+    from vantablack_b200 import synth as S
+    rng = np.random.default_rng(1000 + rank)
+    ws = [S.quant_tensor(rng, S.Q4_K, M, K) for _ in range(N_COPIES)]
+    x = S.activations(rng, K)
+    return ws, x
+
+
+def cpu_gemv_rate(ws, x, budget_s: float, threads: int):
+    """Oracle (reference algorithm, row-striped pool) GB/s on a bounded sample."""
+    import oracle as O
+    O.set_threads(threads)
+    O.matmul(Q4_K, ws[0], x, M, K)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.matmul(Q4_K, ws[n % len(ws)], x, M, K)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return n * ALG_BYTES / el / 1e9, n
+
+
+def run_reference(args):
+    rank, ws_, _ = dist_env()
+    if ws_ > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", init_method="env://")
+        if rank != 0:
+            dist.destroy_process_group()
+            return
+    import oracle as O
+    ws, x = make_weights(0)
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    per_step = 4  # bounded sample: 4 GEMVs (distinct copies) per step
+    for s in range(args.warmup):
+        for i in range(per_step):
+            O.matmul(Q4_K, ws[(s * per_step + i) % N_COPIES], x, M, K)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        for i in range(per_step):
+            O.matmul(Q4_K, ws[(s * per_step + i) % N_COPIES], x, M, K)
+    el = time.perf_counter() - t0
+    v = args.steps * per_step * ALG_BYTES / el / 1e9
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(CONFIG, per_step_sample=f"{per_step} GEMVs"),
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"{per_step} GEMVs of 5632x2048 Q4_K per step, oracle port of "
+                                       "simd.zig matmul_q4_k with pool.zig row striping"},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    if ws_ > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from vantablack_b200 import _lib, ops
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", device_id=dev)
+    lib = _lib.load()
+
+    ws, x = make_weights(rank)
+    dws = [torch.from_numpy(w).to(dev) for w in ws]
+    dx = torch.from_numpy(x).to(dev)
+    dys = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(N_COPIES)]
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for i in range(N_COPIES):
+            ops.gemv(Q4_K, dws[i], dx, M, K, out=dys[i], pdl=True)
+
+    with torch.cuda.stream(stream):
+        step()
+        stream.synchronize()
+        ops.check_device_error()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+        stream.synchronize()
+
+        # Device-timed region (CUDA events on the launching stream).
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        smi_idx = int(vis.split(",")[local]) if vis else local
+        with ClockSampler(smi_idx) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = e0.elapsed_time(e1)
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+        ops.check_device_error()
+
+        # Correctness spot check of the timed outputs (one copy) vs the oracle.
+        import oracle as O
+        if rank == 0:
+            ref = O.matmul(Q4_K, ws[0], x, M, K)
+            err = float(np.abs(dys[0].cpu().numpy() - ref).max() / np.abs(ref).max())
+        else:
+            err = None
+
+    # End-to-end through the C-ABI context API with host buffers.
+    ctx = lib.vtb_cuda_init(local)
+    wbufs = [lib.vtb_cuda_upload(ctx, w.ctypes.data, w.nbytes) for w in ws]
+    xb = lib.vtb_cuda_alloc(ctx, K * 4, None)
+    ybufs = [lib.vtb_cuda_alloc(ctx, M * 4, None) for _ in range(N_COPIES)]
+    hx = torch.from_numpy(x).pin_memory()
+    hy = torch.empty(N_COPIES, M, dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 200))
+
+    def e2e_step():
+        _lib.check(lib.vtb_cuda_copy_h2d(ctx, xb, 0, hx.data_ptr(), K * 4), "h2d")
+        for i in range(N_COPIES):
+            _lib.check(lib.vtb_cuda_matmul_q4_k(ctx, ybufs[i], wbufs[i], 0, xb, M, K), "matmul")
+        for i in range(N_COPIES):
+            _lib.check(lib.vtb_cuda_copy_d2h(ctx, hy[i].data_ptr(), ybufs[i], 0, M * 4), "d2h")
+
+    for _ in range(3):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = time.perf_counter() - t0
+    tt = torch.tensor([e2e_s], device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    e2e_s = float(tt.item())
+    for b in wbufs + ybufs + [xb]:
+        lib.vtb_cuda_release(b)
+    lib.vtb_cuda_destroy(ctx)
+
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        launches = args.steps * N_COPIES
+        value = world * launches * ALG_BYTES / (ms_max / 1e3) / 1e9
+        per_launch_ms = ms / launches
+        achieved = ALG_BYTES / (per_launch_ms / 1e3) / 1e9
+        cpu_v, cpu_n = cpu_gemv_rate(ws, x, args.cpu_budget, os.cpu_count() or 1) if world == 1 else (None, 0)
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF Q4_K bytes)",
+            "config": dict(CONFIG, parallelism=f"replicas x{world}"),
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": peak_kind,
+                         "traffic": ALG_BYTES_TRAFFIC if ALG_BYTES_TRAFFIC else None},
+            "e2e": {"value": world * e2e_steps * N_COPIES * ALG_BYTES / e2e_s / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": K * 4, "d2h_bytes_per_step": N_COPIES * M * 4},
+            "clocks": clk.summary(),
+            "max_rel_err_vs_oracle": err,
+        }
+        if cpu_v is not None:
+            line["cpu_baseline"] = {"value": cpu_v, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+                                    "sample": f"{cpu_n} GEMVs of 5632x2048 Q4_K over {args.cpu_budget:.0f} s, "
+                                              "oracle port of simd.zig matmul_q4_k + pool.zig row striping"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# dram bytes per launch from the committed ncu capture (profiles/), or None.
+ALG_BYTES_TRAFFIC = None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,149 @@
+/*
+ * vtb_cuda.h -- C ABI of the vantablack B200 (sm_100a) CUDA backend.
+ *
+ * This is the flat shim a `backend_cuda.zig` binds with `extern "c"`
+ * declarations, the way the reference binds its Metal bridge
+ * (src/metal/bridge.h:25-228 declared in src/metal/bridge.zig:16-60).
+ * Every signature uses plain pointers, sizes and opaque handles only.
+ *
+ * Conventions
+ *  - Every function returning int returns VTB_CUDA_OK (0) on success and a
+ *    negative status on failure (the reference's bridge returns nonzero on
+ *    failure, bridge.h:47; the codes reuse include/vantablack.h:25-33 values
+ *    so the Zig side can map them straight through mapStreamErr,
+ *    src/c_api.zig:332-340).
+ *  - Quant types are ggml type ids (src/core/parser.zig GgmlType):
+ *    VTB_CUDA_Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14.
+ *  - "Device pointer" arguments are CUDA global-memory addresses on the
+ *    current device.  `stream` is a cudaStream_t passed as void* (NULL = the
+ *    legacy default stream).  Launches are asynchronous on that stream.
+ *  - Weight tensors are row-major packed blocks (m rows of k/elems blocks).
+ *    Their base must be 16-byte aligned and the allocation readable up to
+ *    the next 16-byte boundary past its end (cudaMalloc and the context
+ *    allocator below guarantee both).
+ */
+#ifndef VTB_CUDA_H
+#define VTB_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VTB_CUDA_OK 0
+#define VTB_CUDA_ERR_INVALID_ARG (-1)
+#define VTB_CUDA_ERR_OOM (-4)
+#define VTB_CUDA_ERR_DEVICE (-5)
+#define VTB_CUDA_ERR_DISPATCH (-6)
+#define VTB_CUDA_ERR_UNSUPPORTED (-8)
+#define VTB_CUDA_ERR_TIMEOUT (-9)
+#define VTB_CUDA_ERR_COMM (-10)
+
+#define VTB_CUDA_F32 0
+#define VTB_CUDA_Q8_0 8
+#define VTB_CUDA_Q4_K 12
+#define VTB_CUDA_Q5_K 13
+#define VTB_CUDA_Q6_K 14
+
+/* ------------------------------------------------------------------ */
+/* Introspection                                                        */
+/* ------------------------------------------------------------------ */
+
+/* Static version string (cf. vtb_version_string, include/vantablack.h:128). */
+const char *vtb_cuda_version_string(void);
+/* 1 when a CUDA device of compute capability 10.x is visible (cf. vtb_has_metal,
+ * include/vantablack.h:131). */
+int vtb_cuda_available(void);
+/* Human-readable text for a status code. */
+const char *vtb_cuda_status_string(int status);
+/* Text of the last CUDA error this thread saw inside the library. */
+const char *vtb_cuda_last_error(void);
+/* Bytes per row of k weights in `quant` format (forward.zig rowBytes :629-641);
+ * -1 if unsupported or k is not a whole number of blocks. */
+int64_t vtb_cuda_row_bytes(int quant, int64_t k);
+/* Reads and clears the device error word that bounded waits in the kernels
+ * set when they give up (then VTB_CUDA_ERR_TIMEOUT); synchronizes the device. */
+int vtb_cuda_check_device_error(void);
+
+/* ------------------------------------------------------------------ */
+/* Stream-level kernels (device pointers)                               */
+/* ------------------------------------------------------------------ */
+
+/* y[m] = W[m,k] . x[k], f32 activations, fp32 accumulation.  Replaces the
+ * per-quant CPU kernels matmul_q8_0 / q4_k / q5_k / q6_k
+ * (src/kernels/simd.zig:159, 245, 321, 406) behind comptime_gen.zig:44-58
+ * dispatch, and the Metal one-shots vtb_metal_matmul_* (bridge.h:48-70).
+ * `pdl` != 0 launches with programmatic dependent launch, so the weight
+ * stream starts before the previous kernel on `stream` has finished. */
+int vtb_cuda_gemv(int quant, const void *w, const float *x, float *y, int64_t m, int64_t k,
+                  void *stream, int pdl);
+
+/* Dequantize n elements (whole blocks) to f32, bit-exact with
+ * dequantBlockQ*_* (simd.zig:153, 221, 290, 366) / dequantToF32
+ * (src/runtime/forward.zig:654-736). */
+int vtb_cuda_dequant(int quant, const void *w, float *out, int64_t n, void *stream);
+
+/* out[t, :] = dequantized row ids[t] of a [rows, dim] table
+ * (gatherEmbedding, forward.zig:738-845). */
+int vtb_cuda_embed(int quant, const void *table, const int32_t *ids, float *out, int64_t dim,
+                   int64_t n_tokens, void *stream);
+
+/* Q8_0 activation quantizer for the Q8_0 x Q8_0 path: per 32-block
+ * d = max|x| / 127, q = round-half-away(x * (1/d)).  The reference has no
+ * quantizer (only dot_i8, simd.zig:31-62); this rule is the backend's own. */
+int vtb_cuda_quantize_q8_0(const float *x, int64_t k, int8_t *qs, float *d, void *stream);
+
+/* dots[i, b] = dot_i8(W_qs[i, b, :], xq[b, :]) as int32 (simd.zig:40-62). */
+int vtb_cuda_q8_0_block_dots(const void *w, const int8_t *xq, int32_t *dots, int64_t m, int64_t k,
+                             void *stream);
+
+/* Q8_0 x Q8_0 GEMV: quantizes x into caller scratch (xq_scratch: k bytes,
+ * dx_scratch: k/32 floats), then y[i] = sum_b (d_w * d_x) * float(int32 dot). */
+int vtb_cuda_gemv_q8_0_q8_0(const void *w, const float *x, float *y, int64_t m, int64_t k,
+                            int8_t *xq_scratch, float *dx_scratch, void *stream, int pdl);
+
+/* ------------------------------------------------------------------ */
+/* Context / buffers (mirrors the Metal bridge, bridge.h:25-46)         */
+/* ------------------------------------------------------------------ */
+
+typedef struct VtbCudaCtx VtbCudaCtx;
+typedef struct VtbCudaBuf VtbCudaBuf;
+
+/* Bind device `device_ordinal`, create the context's stream (vtb_metal_init). */
+VtbCudaCtx *vtb_cuda_init(int device_ordinal);
+void vtb_cuda_destroy(VtbCudaCtx *ctx);
+/* The context's cudaStream_t, as void*. */
+void *vtb_cuda_stream(VtbCudaCtx *ctx);
+/* Device allocation (vtb_metal_alloc); *dev_ptr_out receives the address. */
+VtbCudaBuf *vtb_cuda_alloc(VtbCudaCtx *ctx, size_t bytes, void **dev_ptr_out);
+/* Copy `len` host bytes (e.g. the GGUF mmap) into a new device buffer.
+ * Replaces the no-copy vtb_metal_wrap (bridge.h:36-39): a discrete GPU
+ * cannot alias host pages, so weights are uploaded once. */
+VtbCudaBuf *vtb_cuda_upload(VtbCudaCtx *ctx, const void *host, size_t len);
+void vtb_cuda_release(VtbCudaBuf *buf);
+void *vtb_cuda_buf_ptr(VtbCudaBuf *buf);
+size_t vtb_cuda_buf_size(VtbCudaBuf *buf);
+int vtb_cuda_copy_h2d(VtbCudaCtx *ctx, VtbCudaBuf *dst, size_t dst_off, const void *src, size_t bytes);
+/* Waits for the context stream, then copies. */
+int vtb_cuda_copy_d2h(VtbCudaCtx *ctx, void *dst, VtbCudaBuf *src, size_t src_off, size_t bytes);
+/* Block until all work on the context stream is done (vtb_metal_wait_idle). */
+int vtb_cuda_wait_idle(VtbCudaCtx *ctx);
+
+/* One-shot matmuls with the Metal bridge's signature (bridge.h:48-70):
+ * out_buf[m] = W(w_buf + w_offset)[m,k] . acts_buf[k].  Enqueued on the
+ * context stream; results are visible to vtb_cuda_copy_d2h. */
+int vtb_cuda_matmul_q8_0(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                         VtbCudaBuf *acts_buf, size_t m, size_t k);
+int vtb_cuda_matmul_q4_k(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                         VtbCudaBuf *acts_buf, size_t m, size_t k);
+int vtb_cuda_matmul_q5_k(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                         VtbCudaBuf *acts_buf, size_t m, size_t k);
+int vtb_cuda_matmul_q6_k(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                         VtbCudaBuf *acts_buf, size_t m, size_t k);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VTB_CUDA_H */

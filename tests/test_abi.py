@@ -1,0 +1,51 @@
+"""The C-ABI library loads without a GPU and exports every symbol that
+include/vtb_cuda.h declares; host-side argument checks reject bad calls
+before any launch."""
+import ctypes
+
+import pytest
+
+from vantablack_b200 import _lib, build
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_exports_every_header_symbol(lib):
+    syms = _lib.header_symbols()
+    assert len(syms) >= 20
+    for s in syms:
+        assert hasattr(lib, s), f"libvtbcuda.so does not export {s}"
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
+
+
+def test_no_torch_in_abi():
+    text = open(_lib.HEADER).read()
+    for bad in ("torch", "at::", "Tensor", "c10"):
+        assert bad not in text
+
+
+def test_introspection(lib):
+    assert b"sm_100a" in lib.vtb_cuda_version_string()
+    assert lib.vtb_cuda_row_bytes(12, 2048) == 1152
+    assert lib.vtb_cuda_row_bytes(14, 5632) == 4620
+    assert lib.vtb_cuda_row_bytes(8, 4096) == 4352
+    assert lib.vtb_cuda_row_bytes(12, 100) == -1
+    assert lib.vtb_cuda_status_string(-9) == b"device-side bounded wait timed out"
+
+
+def test_argument_checks_without_launch(lib):
+    buf = ctypes.create_string_buffer(64)
+    p = (ctypes.addressof(buf) + 15) & ~15
+    # unsupported quant, k not a whole number of blocks, misaligned weights, null x
+    assert lib.vtb_cuda_gemv(3, p, p, p, 4, 256, None, 0) == -8
+    assert lib.vtb_cuda_gemv(12, p, p, p, 4, 100, None, 0) == -1
+    assert lib.vtb_cuda_gemv(12, p + 1, p, p, 4, 256, None, 0) == -1
+    assert lib.vtb_cuda_gemv(12, p, None, p, 4, 256, None, 0) == -1
+    assert lib.vtb_cuda_gemv(12, p, p, p, 0, 256, None, 0) == -1
+    assert b"aligned" in lib.vtb_cuda_last_error() or lib.vtb_cuda_last_error()
+    assert lib.vtb_cuda_dequant(14, p, p, 100, None) == -1
+    assert lib.vtb_cuda_quantize_q8_0(p, 33, p, p, None) == -1

@@ -1,0 +1,132 @@
+"""GPU parity of the decode GEMV, dequantizer and Q8_0 x Q8_0 path against
+the CPU oracle, through the C ABI.  Tolerances (north star): dequantized
+values and int32 block dots bit-exact; fp32 GEMV outputs
+max|y - y_ref| / max|y_ref| <= 1e-4."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from vantablack_b200 import synth as S
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+O.set_threads(8)
+
+
+def ops():
+    from vantablack_b200 import ops as _ops
+    return _ops
+
+
+def rel_err(got, ref):
+    return float(np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+@pytest.mark.parametrize("q", [S.Q8_0, S.Q4_K, S.Q5_K, S.Q6_K])
+def test_dequant_bit_exact(q):
+    rng = np.random.default_rng(100 + q)
+    m, k = 33, 2048
+    w = S.quant_tensor(rng, q, m, k)
+    got = ops().dequant(q, torch.from_numpy(w).cuda(), m * k).cpu().numpy()
+    exp = O.dequant(q, w, m * k)
+    assert np.array_equal(got.view(np.uint32), exp.view(np.uint32))
+
+
+GEMV_SHAPES = [
+    (S.Q4_K, 5632, 2048),   # config 1 (TinyLlama ffn_up)
+    (S.Q4_K, 1024, 4096), (S.Q4_K, 14336, 4096),
+    (S.Q6_K, 4096, 4096), (S.Q6_K, 4096, 14336), (S.Q6_K, 2048, 5632),  # ragged Q6_K rows (4620 B)
+    (S.Q8_0, 4096, 4096), (S.Q8_0, 14336, 4096), (S.Q8_0, 4096, 14336),
+    (S.Q5_K, 4096, 4096), (S.Q5_K, 1000, 2304),
+    (S.Q4_K, 1, 256), (S.Q6_K, 3, 256), (S.Q8_0, 5, 32), (S.Q4_K, 7, 2560),  # tiny / ragged tails
+]
+
+
+@pytest.mark.parametrize("q,m,k", GEMV_SHAPES)
+def test_gemv_matches_oracle(q, m, k):
+    rng = np.random.default_rng(m * 7 + k + q)
+    w = S.quant_tensor(rng, q, m, k)
+    x = S.activations(rng, k)
+    y = ops().gemv(q, torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda(), m, k).cpu().numpy()
+    ops().check_device_error()
+    ref = O.matmul(q, w, x, m, k)
+    assert rel_err(y, ref) <= TOL
+
+
+def test_gemv_pdl_chain_matches():
+    """Back-to-back PDL launches where each GEMV reads the previous output."""
+    rng = np.random.default_rng(11)
+    k = 2048
+    ws = [S.quant_tensor(rng, S.Q4_K, k, k) for _ in range(3)]
+    x = S.activations(rng, k)
+    dws = [torch.from_numpy(w).cuda() for w in ws]
+    cur = torch.from_numpy(x).cuda()
+    for dw in dws:
+        cur = ops().gemv(S.Q4_K, dw, cur, k, k, pdl=True)
+    got = cur.cpu().numpy()
+    ref = x
+    for w in ws:
+        ref = O.matmul(S.Q4_K, w, ref, k, k)
+    assert rel_err(got, ref) <= 1e-3  # three chained roundings
+
+
+def test_q8_0_quantizer_and_block_dots_bit_exact():
+    rng = np.random.default_rng(21)
+    m, k = 257, 4096
+    w = S.quant_tensor(rng, S.Q8_0, m, k)
+    x = S.activations(rng, k)
+    x[64:96] = 0.0
+    qs, d = ops().quantize_q8_0(torch.from_numpy(x).cuda())
+    eqs, ed = O.quantize_q8_0(x)
+    assert np.array_equal(qs.cpu().numpy(), eqs)
+    assert np.array_equal(d.cpu().numpy().view(np.uint32), ed.view(np.uint32))
+    dots = ops().q8_0_block_dots(torch.from_numpy(w).cuda(), qs, m, k).cpu().numpy()
+    assert np.array_equal(dots, O.q8_0_block_dots(w, eqs, m, k))
+
+
+@pytest.mark.parametrize("m,k", [(4096, 4096), (14336, 4096), (333, 1024)])
+def test_gemv_q8_0_q8_0_matches_oracle(m, k):
+    rng = np.random.default_rng(m + k)
+    w = S.quant_tensor(rng, S.Q8_0, m, k)
+    x = S.activations(rng, k)
+    y = ops().gemv_q8_0_q8_0(torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda(), m, k).cpu().numpy()
+    assert rel_err(y, O.matmul_q8_0_q8_0(w, x, m, k)) <= TOL
+
+
+def test_embed_rows_bit_exact():
+    rng = np.random.default_rng(4)
+    vocab, dim = 100, 2048
+    t = S.quant_tensor(rng, S.Q4_K, vocab, dim)
+    ids = np.array([0, 99, 3, 3, 57], np.int32)
+    got = ops().embed(S.Q4_K, torch.from_numpy(t).cuda(), torch.from_numpy(ids).cuda(), dim).cpu().numpy()
+    rb = S.row_bytes(S.Q4_K, dim)
+    for i, r in enumerate(ids):
+        exp = O.dequant(S.Q4_K, t[r * rb:(r + 1) * rb], dim)
+        assert np.array_equal(got[i].view(np.uint32), exp.view(np.uint32))
+
+
+def test_context_bridge_matmul():
+    """The Metal-bridge-shaped API: upload, one-shot matmul at an offset, copy back."""
+    import ctypes
+    from vantablack_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(8)
+    m, k = 300, 4096
+    w = S.quant_tensor(rng, S.Q6_K, m, k)
+    blob = np.concatenate([np.zeros(64, np.uint8), w])  # tensor at offset 64 inside a weight blob
+    x = S.activations(rng, k)
+    ctx = lib.vtb_cuda_init(0)
+    assert ctx
+    wb = lib.vtb_cuda_upload(ctx, blob.ctypes.data, blob.nbytes)
+    xb = lib.vtb_cuda_upload(ctx, x.ctypes.data, x.nbytes)
+    yb = lib.vtb_cuda_alloc(ctx, m * 4, None)
+    assert wb and xb and yb
+    _lib.check(lib.vtb_cuda_matmul_q6_k(ctx, yb, wb, 64, xb, m, k), "matmul")
+    y = np.empty(m, np.float32)
+    _lib.check(lib.vtb_cuda_copy_d2h(ctx, y.ctypes.data, yb, 0, m * 4), "d2h")
+    assert rel_err(y, O.matmul(S.Q6_K, w, x, m, k)) <= TOL
+    assert lib.vtb_cuda_matmul_q6_k(ctx, yb, wb, 64, xb, m + 1, k) == -1  # beyond the buffer
+    for b in (wb, xb, yb):
+        lib.vtb_cuda_release(b)
+    lib.vtb_cuda_destroy(ctx)

@@ -1,0 +1,149 @@
+"""Pins the CPU oracle to the reference's own known-answer tests
+(src/kernels/simd.zig:500-806, src/kernels/math.zig:205-254) and to
+gguf-py's independent dequantizers (tests/golden/kquant_golden.npz)."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from vantablack_b200 import synth as S
+
+GOLD = np.load(os.path.join(os.path.dirname(__file__), "golden", "kquant_golden.npz"))
+
+
+def test_dot_i8_div16():  # simd.zig:502-513
+    a = (np.arange(32) - 16).astype(np.int8)
+    b = (np.arange(32) * 3 - 47).astype(np.int8)
+    assert O.dot_i8(a, b) == int((a.astype(np.int32) * b.astype(np.int32)).sum())
+
+
+def test_dot_i8_tail():  # simd.zig:515-525
+    a = (np.arange(19) - 9).astype(np.int8)
+    b = (np.arange(19) + 1).astype(np.int8)
+    assert O.dot_i8(a, b) == int((a.astype(np.int32) * b.astype(np.int32)).sum())
+
+
+def test_dot_i8_saturation():  # simd.zig:527-531
+    a = np.full(32, -128, np.int8)
+    assert O.dot_i8(a, a) == 524288
+
+
+def test_dot_f32():  # simd.zig:533-543
+    a = np.arange(1, 20, dtype=np.float32)
+    b = a * 2
+    exp = np.float32(0)
+    for i in range(19):
+        exp = np.float32(exp + a[i] * b[i])
+    assert abs(O.dot_f32(a, b) - exp) <= 1e-4
+
+
+@pytest.mark.parametrize("name,q", [("q8_0", S.Q8_0), ("q4_k", S.Q4_K), ("q5_k", S.Q5_K), ("q6_k", S.Q6_K)])
+def test_dequant_bit_exact_vs_gguf(name, q):
+    blocks = GOLD[f"{name}_blocks"]
+    exp = GOLD[f"{name}_dequant"]
+    got = O.dequant(q, blocks, exp.size)
+    assert np.array_equal(got.view(np.uint32), exp.view(np.uint32))
+
+
+def test_q8_0_dequant_kat():  # simd.zig:586-599
+    blk = GOLD["q8_0_blocks"][:34]
+    qs = blk[2:].view(np.int8).astype(np.float32)
+    assert np.allclose(O.dequant(S.Q8_0, blk, 32), np.float32(0.125) * qs, atol=1e-4)
+
+
+def test_q4_k_kat_spots_and_matmul():  # simd.zig:601-651
+    blk = GOLD["q4_k_blocks"][:144]
+    dq = O.dequant(S.Q4_K, blk, 256)
+    d, dmin = np.float32(0.0078125), np.float32(0.0625)
+    e0 = d * np.float32(blk[4] & 63) * np.float32(blk[16] & 15) - dmin * np.float32(blk[8] & 63)
+    e32 = d * np.float32(blk[5] & 63) * np.float32(blk[16] >> 4) - dmin * np.float32(blk[9] & 63)
+    assert abs(dq[0] - e0) <= 1e-4 and abs(dq[32] - e32) <= 1e-4
+    x = (np.arange(256) % 7).astype(np.float32) * np.float32(0.1)
+    got = O.matmul_single(S.Q4_K, blk, x, 1, 256)[0]
+    assert abs(got - float(np.dot(dq.astype(np.float64), x))) <= 1e-3
+
+
+def test_q5_k_kat():  # simd.zig:653-697
+    blk = GOLD["q5_k_blocks"][:176]
+    dq = O.dequant(S.Q5_K, blk, 256)
+    d, dmin = np.float32(0.00390625), np.float32(0.03125)
+    w5 = (blk[48] & 15) + (16 if blk[16] & 1 else 0)
+    e0 = d * np.float32(blk[4] & 63) * np.float32(w5) - dmin * np.float32(blk[8] & 63)
+    assert abs(dq[0] - e0) <= 1e-4
+    x = (np.arange(256) % 9).astype(np.float32) * np.float32(0.1) - np.float32(0.4)
+    got = O.matmul_single(S.Q5_K, blk, x, 1, 256)[0]
+    assert abs(got - float(np.dot(dq.astype(np.float64), x))) <= 1e-3
+
+
+def test_q6_k_kat():  # simd.zig:699-732
+    blk = GOLD["q6_k_blocks"][:210]
+    dq = O.dequant(S.Q6_K, blk, 256)
+    q1 = int((blk[0] & 15) | ((blk[128] & 3) << 4)) - 32
+    e0 = np.float32(0.001953125) * np.float32(np.int8(blk[192].astype(np.int8))) * np.float32(q1)
+    assert abs(dq[0] - e0) <= 1e-4
+    x = (np.arange(256) % 11).astype(np.float32) * np.float32(0.05) - np.float32(0.25)
+    got = O.matmul_single(S.Q6_K, blk, x, 1, 256)[0]
+    assert abs(got - float(np.dot(dq.astype(np.float64), x))) <= 1e-3
+
+
+def test_matmul_q8_0_kat():  # simd.zig:770-806
+    got = O.matmul(S.Q8_0, GOLD["mm_q8_0_w"], GOLD["mm_q8_0_x"], 4, 64)
+    assert np.allclose(got, GOLD["mm_q8_0_y"], atol=1e-3)
+
+
+def test_math_kats():  # math.zig:205-254
+    x = np.arange(1, 9, dtype=np.float32)
+    ref = x / np.sqrt((x * x).sum() / 8)
+    assert np.allclose(O.rms_norm(x, np.ones(8, np.float32), 0.0), ref, atol=1e-4)
+    r = O.rope(np.array([1, 2, 3, 4], np.float32), 0, 10000.0)
+    assert abs(r[0] - 1) < 1e-5 and abs(r[1] - 2) < 1e-5
+    assert abs(O.softmax(np.array([0.5, 1.5, -0.5, 2.0], np.float32)).sum() - 1) < 1e-5
+    g = O.geglu(np.array([-2.0, -0.5, 0.0, 0.5, 1.0, 2.0], np.float32), np.ones(6, np.float32))
+    assert np.allclose(g, [-0.045402, -0.154286, 0.0, 0.345714, 0.841192, 1.954598], atol=1e-4)
+    gg = np.array([0.5, -1.0, 2.0, 0.0], np.float32)
+    u = np.array([1.0, 2.0, 0.5, 4.0], np.float32)
+    assert np.allclose(O.swiglu(gg, u), gg / (1 + np.exp(-gg)) * u, atol=1e-5)
+    assert O.argmax(np.array([0.1, 0.5, 1.5, 0.3], np.float32)) == 2
+
+
+@pytest.mark.parametrize("q", [S.Q8_0, S.Q4_K, S.Q5_K, S.Q6_K])
+def test_threaded_matmul_equals_single(q):
+    rng = np.random.default_rng(q)
+    m, k = 37, 512
+    w = S.quant_tensor(rng, q, m, k)
+    x = S.activations(rng, k)
+    O.set_threads(4)
+    a = O.matmul(q, w, x, m, k)
+    O.set_threads(1)
+    assert np.array_equal(a, O.matmul_single(q, w, x, m, k))
+    W = O.dequant(q, w, m * k).reshape(m, k).astype(np.float64)
+    assert np.abs(a - W @ x).max() <= 1e-4 * np.abs(W @ x).max()
+
+
+def test_batched_matmul_matches_dot_f32():
+    rng = np.random.default_rng(5)
+    m, k, B = 9, 512, 3
+    w = S.quant_tensor(rng, S.Q6_K, m, k)
+    acts = S.activations(rng, B, k)
+    out = O.matmul_batched(S.Q6_K, w, acts, m, k, B)
+    W = O.dequant(S.Q6_K, w, m * k).reshape(m, k)
+    for b in range(B):
+        for i in range(m):
+            assert out[b, i] == np.float32(O.dot_f32(W[i], acts[b]))
+
+
+def test_q8_0_quantizer_rule():
+    rng = np.random.default_rng(3)
+    x = S.activations(rng, 256)
+    x[32:64] = 0.0  # all-zero block: d = 0, q = 0
+    qs, d = O.quantize_q8_0(x)
+    xb = x.reshape(-1, 32)
+    dd = (np.abs(xb).max(1) / np.float32(127)).astype(np.float32)
+    assert np.array_equal(d, dd)
+    with np.errstate(divide="ignore"):
+        inv = np.where(dd != 0, np.float32(1) / dd, np.float32(0)).astype(np.float32)
+    v = (xb * inv[:, None]).astype(np.float32)
+    q = np.sign(v) * np.floor(np.abs(v) + np.float32(0.5))  # round half away from zero
+    assert np.array_equal(qs.reshape(-1, 32), q.astype(np.int8))
+    assert np.abs(qs).max() <= 127

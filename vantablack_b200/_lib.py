@@ -1,0 +1,92 @@
+"""ctypes binding of libvtbcuda.so (the C ABI in include/vtb_cuda.h).
+
+The library is the product: there is no CPU or PyTorch fallback.  Loading
+fails loudly if it has not been built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvtbcuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "vtb_cuda.h")
+
+OK = 0
+STATUS = {0: "ok", -1: "invalid argument", -4: "out of device memory", -5: "no usable CUDA device",
+          -6: "kernel dispatch failed", -8: "unsupported quant type", -9: "device-side wait timed out",
+          -10: "collective communication failed"}
+
+_vp, _i64, _i32, _int, _sz = C.c_void_p, C.c_int64, C.c_int32, C.c_int, C.c_size_t
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "vtb_cuda_version_string": (C.c_char_p, []),
+    "vtb_cuda_available": (_int, []),
+    "vtb_cuda_status_string": (C.c_char_p, [_int]),
+    "vtb_cuda_last_error": (C.c_char_p, []),
+    "vtb_cuda_row_bytes": (_i64, [_int, _i64]),
+    "vtb_cuda_check_device_error": (_int, []),
+    "vtb_cuda_gemv": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _int]),
+    "vtb_cuda_dequant": (_int, [_int, _vp, _vp, _i64, _vp]),
+    "vtb_cuda_embed": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "vtb_cuda_quantize_q8_0": (_int, [_vp, _i64, _vp, _vp, _vp]),
+    "vtb_cuda_q8_0_block_dots": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "vtb_cuda_gemv_q8_0_q8_0": (_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _int]),
+    "vtb_cuda_init": (_vp, [_int]),
+    "vtb_cuda_destroy": (None, [_vp]),
+    "vtb_cuda_stream": (_vp, [_vp]),
+    "vtb_cuda_alloc": (_vp, [_vp, _sz, C.POINTER(_vp)]),
+    "vtb_cuda_upload": (_vp, [_vp, _vp, _sz]),
+    "vtb_cuda_release": (None, [_vp]),
+    "vtb_cuda_buf_ptr": (_vp, [_vp]),
+    "vtb_cuda_buf_size": (_sz, [_vp]),
+    "vtb_cuda_copy_h2d": (_int, [_vp, _vp, _sz, _vp, _sz]),
+    "vtb_cuda_copy_d2h": (_int, [_vp, _vp, _vp, _sz, _sz]),
+    "vtb_cuda_wait_idle": (_int, [_vp]),
+    "vtb_cuda_matmul_q8_0": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_matmul_q4_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_matmul_q5_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_matmul_q6_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+}
+
+
+class VtbError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        detail = ""
+        if _lib is not None:
+            detail = (_lib.vtb_cuda_last_error() or b"").decode(errors="replace")
+        super().__init__(f"{where}: {STATUS.get(status, status)} ({status}) {detail}".rstrip())
+        self.status = status
+
+
+_lib = None
+
+
+def header_symbols(path: str = HEADER) -> list[str]:
+    """Function names declared in include/vtb_cuda.h."""
+    text = open(path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(vtb_cuda_\w+)\s*\(", text)))
+
+
+def load(path: str = LIB_PATH):
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing: build it with `python -m vantablack_b200.build` "
+                          "(there is no CPU fallback)")
+    lib = C.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int, where: str) -> None:
+    if status != OK:
+        raise VtbError(status, where)

@@ -1,0 +1,108 @@
+// common.cuh -- shared device helpers for the vantablack B200 backend.
+//
+// Block formats (ggml, as restated by the reference at src/kernels/simd.zig):
+//   Q8_0  34 B / 32 weights : f16 d | i8 qs[32]
+//   Q4_K 144 B / 256        : f16 d | f16 dmin | u8 scales[12] | u8 qs[128]
+//   Q5_K 176 B / 256        : f16 d | f16 dmin | u8 scales[12] | u8 qh[32] | u8 qs[128]
+//   Q6_K 210 B / 256        : u8 ql[128] | u8 qh[64] | i8 sc[16] | f16 d
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace vtb {
+
+enum Quant : int { F32 = 0, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14 };
+
+template <int Q> struct Fmt;
+template <> struct Fmt<Q8_0> { static constexpr int bytes = 34, elems = 32; };
+template <> struct Fmt<Q4_K> { static constexpr int bytes = 144, elems = 256; };
+template <> struct Fmt<Q5_K> { static constexpr int bytes = 176, elems = 256; };
+template <> struct Fmt<Q6_K> { static constexpr int bytes = 210, elems = 256; };
+
+inline int64_t host_row_bytes(int q, int64_t k) {
+  switch (q) {
+    case F32: return 4 * k;
+    case Q8_0: return (k / 32) * 34;
+    case Q4_K: return (k / 256) * 144;
+    case Q5_K: return (k / 256) * 176;
+    case Q6_K: return (k / 256) * 210;
+    default: return -1;
+  }
+}
+inline int host_block_elems(int q) { return q == Q8_0 ? 32 : (q == F32 ? 1 : 256); }
+inline bool host_quant_ok(int q) { return q == Q8_0 || q == Q4_K || q == Q5_K || q == Q6_K; }
+
+// Device-side error word.  Kernels that give up a bounded wait OR a code in
+// here and return; the host reads it with vtb_cuda_check_device_error().
+enum DevErr : unsigned { DEV_ERR_MBAR_TIMEOUT = 1u, DEV_ERR_BAD_ARG = 2u };
+__device__ unsigned g_dev_error = 0;  // one definition: the library is a single translation unit
+
+__device__ __forceinline__ void flag_error(unsigned code) { atomicOr(&g_dev_error, code); }
+
+__device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+
+// ---- packed f32x2 arithmetic (sm_100a) ----
+struct f2 { unsigned long long v; };
+__device__ __forceinline__ f2 pk(float a, float b) {
+  f2 r; asm("mov.b64 %0, {%1,%2};" : "=l"(r.v) : "f"(a), "f"(b)); return r;
+}
+__device__ __forceinline__ void unpk(f2 r, float& a, float& b) {
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(r.v));
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 r; asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v)); return r;
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 r; asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v)); return r;
+}
+__device__ __forceinline__ float hsum(f2 a) { float x, y; unpk(a, x, y); return x + y; }
+
+// Byte k of `v` as the float 2^23 + byte (exact): PRMT against 0x4B000000.
+template <int K>
+__device__ __forceinline__ float byte_magic(uint32_t v) {
+  return __uint_as_float(__byte_perm(v, 0x4B000000u, K | (4 << 4) | (5 << 8) | (7 << 12)));
+}
+
+// ---- mbarrier + bulk copy (TMA, non-multicast) ----
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after ~max_iter polls (each try_wait itself
+// suspends for a hardware-chosen time), flags DEV_ERR_MBAR_TIMEOUT.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity, unsigned max_iter = 1u << 22) {
+  for (unsigned i = 0; i < max_iter; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  flag_error(DEV_ERR_MBAR_TIMEOUT);
+  return false;
+}
+// 1-D bulk copy global -> shared (both 16 B aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace vtb

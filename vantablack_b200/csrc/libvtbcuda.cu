@@ -1,0 +1,6 @@
+// libvtbcuda.cu -- single translation unit of the backend library: the
+// kernels share device globals (the error word), so they are compiled
+// together without relocatable device code.
+#include "gemv.cu"
+#include "quant_aux.cu"
+#include "api.cu"

@@ -1,0 +1,90 @@
+"""Tensor-level front end of the CUDA kernels.
+
+Device memory and streams come from PyTorch (plumbing only); every call goes
+through the C ABI of libvtbcuda.so on torch's current stream.  Weight
+tensors are flat ``torch.uint8`` CUDA tensors of packed GGUF blocks.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .synth import BLOCK_ELEMS, F32, Q4_K, Q5_K, Q6_K, Q8_0, row_bytes  # noqa: F401
+
+lib = _lib.load()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dev(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def gemv(quant: int, w: torch.Tensor, x: torch.Tensor, m: int, k: int, out: torch.Tensor | None = None,
+         pdl: bool = False) -> torch.Tensor:
+    """y[m] = W[m, k] . x[k] (f32)."""
+    _dev(w, "w"); _dev(x, "x")
+    if x.dtype != torch.float32 or x.numel() != k:
+        raise ValueError("x must be f32[k]")
+    if w.numel() < m * row_bytes(quant, k):
+        raise ValueError("w is smaller than m rows")
+    y = torch.empty(m, dtype=torch.float32, device=x.device) if out is None else out
+    _lib.check(lib.vtb_cuda_gemv(quant, w.data_ptr(), x.data_ptr(), y.data_ptr(), m, k, _stream(), int(pdl)),
+               "vtb_cuda_gemv")
+    return y
+
+
+def dequant(quant: int, w: torch.Tensor, n: int) -> torch.Tensor:
+    _dev(w, "w")
+    out = torch.empty(n, dtype=torch.float32, device=w.device)
+    _lib.check(lib.vtb_cuda_dequant(quant, w.data_ptr(), out.data_ptr(), n, _stream()), "vtb_cuda_dequant")
+    return out
+
+
+def embed(quant: int, table: torch.Tensor, ids: torch.Tensor, dim: int) -> torch.Tensor:
+    _dev(table, "table"); _dev(ids, "ids")
+    ids = ids.to(torch.int32)
+    out = torch.empty(ids.numel(), dim, dtype=torch.float32, device=table.device)
+    _lib.check(lib.vtb_cuda_embed(quant, table.data_ptr(), ids.data_ptr(), out.data_ptr(), dim, ids.numel(),
+                                  _stream()), "vtb_cuda_embed")
+    return out
+
+
+def quantize_q8_0(x: torch.Tensor):
+    _dev(x, "x")
+    k = x.numel()
+    qs = torch.empty(k, dtype=torch.int8, device=x.device)
+    d = torch.empty(k // 32, dtype=torch.float32, device=x.device)
+    _lib.check(lib.vtb_cuda_quantize_q8_0(x.data_ptr(), k, qs.data_ptr(), d.data_ptr(), _stream()),
+               "vtb_cuda_quantize_q8_0")
+    return qs, d
+
+
+def q8_0_block_dots(w: torch.Tensor, xq: torch.Tensor, m: int, k: int) -> torch.Tensor:
+    _dev(w, "w"); _dev(xq, "xq")
+    dots = torch.empty(m, k // 32, dtype=torch.int32, device=w.device)
+    _lib.check(lib.vtb_cuda_q8_0_block_dots(w.data_ptr(), xq.data_ptr(), dots.data_ptr(), m, k, _stream()),
+               "vtb_cuda_q8_0_block_dots")
+    return dots
+
+
+def gemv_q8_0_q8_0(w: torch.Tensor, x: torch.Tensor, m: int, k: int, out=None, scratch=None,
+                   pdl: bool = False) -> torch.Tensor:
+    _dev(w, "w"); _dev(x, "x")
+    y = torch.empty(m, dtype=torch.float32, device=x.device) if out is None else out
+    if scratch is None:
+        scratch = (torch.empty(k, dtype=torch.int8, device=x.device),
+                   torch.empty(k // 32, dtype=torch.float32, device=x.device))
+    xq, dx = scratch
+    _lib.check(lib.vtb_cuda_gemv_q8_0_q8_0(w.data_ptr(), x.data_ptr(), y.data_ptr(), m, k, xq.data_ptr(),
+                                           dx.data_ptr(), _stream(), int(pdl)), "vtb_cuda_gemv_q8_0_q8_0")
+    return y
+
+
+def check_device_error() -> None:
+    _lib.check(lib.vtb_cuda_check_device_error(), "device error word")
