@@ -1,0 +1,302 @@
+// gemv_mma.cu -- tensor-core decode GEMV for Q4_K: y[m] = W[m,k] . x[k]
+// with f32 x and y (the reference's matmul_q4_k, src/kernels/simd.zig:245-273).
+//
+// Why tensor cores for a GEMV: a Q4_K weight costs 0.5625 B of HBM, so at
+// ~6.5 TB/s every SM must retire ~41 weights per clock.  SIMT dequant
+// (nibble -> f32, FMA) costs >2 instructions per weight and runs out of issue
+// slots at ~40% of the HBM roofline.  Here the nibble bytes go to the integer
+// tensor core unchanged: one AND extracts four weights.
+//
+// Arithmetic:
+//  * A (u8): the low nibbles q (AND 0x0F0F0F0F) of sub-block 2j, or the high
+//    nibbles kept in place, 16*q (AND 0xF0F0F0F0), of sub-block 2j+1.  One
+//    m16n8k32 MMA covers 16 rows x one 32-weight sub-block.
+//  * B (s8): per sub-block s, x is scaled by 2^-e_s so that max|x| lands in
+//    [32, 64), then split into two int8 limbs:  x/2^e_s ~ L0 + L1/254 with
+//    L0 = rint(x'), L1 = rint((x' - L0) * 254)  (|error| <= 1/508 in a block
+//    whose max is >= 32, i.e. < 2^-14 relative to the block max).
+//  * Block-diagonal B: the 8 columns hold (L0, L1) of 4 consecutive
+//    sub-blocks; the MMA of sub-block s only has its own column pair
+//    non-zero, so the int32 accumulator D[r, 2s'+c] = sum_k A[r,k] L_c[k]
+//    is an EXACT integer dot per (row, sub-block, limb).
+//  * Epilogue per (row, sub-block): sum_k q x = 2^e (D0 + D1/254) (/16 for
+//    high nibbles), and y += (d*sc) * sum q x - (dmin*mn) * sum x -- the
+//    reference's w = d1*q - m1 (simd.zig:221-243) distributed over the
+//    sub-block.  fp32 accumulation; tolerance-checked (<= 1e-4).
+//
+// Data movement: persistent CTAs; each warp streams tiles of 32 rows x CHB
+// super-blocks HBM -> shared with 1-D bulk copies (one per row, no
+// multicast) into an S-stage mbarrier ring; the copies for the first S tiles
+// are issued before griddepcontrol.wait, so with programmatic dependent
+// launch they overlap the kernel that produces x.
+#include "common.cuh"
+
+namespace vtb {
+
+__device__ __forceinline__ void imma16832(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared layout of the activation vector, written once per CTA:
+//   xq[s] : 64 bytes per sub-block s = [limb c][lane-quad t][8 bytes]; the 8
+//           bytes are the B-fragment registers b0 (k = 4t..4t+3) and b1
+//           (k = 16+4t..16+4t+3) of column limb c.
+//   xs[s] : {2^e_s, sum_k x_k}
+struct XShared {
+  int8_t* xq;
+  float2* xs;
+};
+
+// Each warp converts 4 sub-blocks per float4 load (8 lanes per sub-block) and
+// keeps up to 8 loads in flight, so the prologue costs about one L2 round trip.
+__device__ __forceinline__ void build_x_shared(const float* __restrict__ x, int K, XShared xsh, int warp, int lane,
+                                               int nwarps) {
+  const int n4 = K / 128;  // groups of 4 sub-blocks
+  const int sub = lane >> 3, part = lane & 7;
+  for (int base = warp; base < n4; base += nwarps * 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int gi = base + u * nwarps;
+      if (gi < n4) v[u] = __ldg(reinterpret_cast<const float4*>(x + gi * 128) + lane);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int gi = base + u * nwarps;
+      if (gi >= n4) break;
+      const float4 a = v[u];
+      float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
+      float sum = (a.x + a.y) + (a.z + a.w);
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      }
+      const int E = (int)((__float_as_uint(m) >> 23) & 0xffu);  // biased exponent of max|x|
+      // max|x| * 2^-e in [32, 64), so L0 = rint(x') fits int8 with room; zero /
+      // subnormal blocks keep e = 0 (their limbs round to 0)
+      const int e = (E == 0) ? 0 : (E - 127 - 5);
+      const float sx = __uint_as_float((uint32_t)(127 + e) << 23);
+      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+      const float xv[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};  // exact (power of two)
+      uint32_t l0w = 0, l1w = 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float l0 = rintf(xv[c]);
+        const float l1 = rintf((xv[c] - l0) * 254.f);
+        l0w |= ((uint32_t)(int)l0 & 0xffu) << (8 * c);
+        l1w |= ((uint32_t)(int)l1 & 0xffu) << (8 * c);
+      }
+      const int s = gi * 4 + sub;
+      // element l = 4*part + c sits at t = part & 3, half = part >> 2, byte c
+      int8_t* dst = xsh.xq + s * 64 + (part & 3) * 8 + (part >> 2) * 4;
+      *reinterpret_cast<uint32_t*>(dst) = l0w;
+      *reinterpret_cast<uint32_t*>(dst + 32) = l1w;
+      if (part == 0) xsh.xs[s] = make_float2(sx, sum);
+    }
+  }
+}
+
+template <int CHB>
+struct MmaQ4K {
+  static constexpr int ROWS = 32;            // two m16 MMA tiles per warp tile
+  static constexpr int BB = 144;
+  static constexpr int SLOT = CHB * BB + 16;  // +16 B: row stride = 12 (mod 32) words -> conflict-free LDS
+  static constexpr int STAGE = ROWS * SLOT;
+};
+
+template <int WARPS, int S, int CHB>
+__global__ void __launch_bounds__(WARPS * 32)
+gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
+                    int ksplit) {
+  using C = MmaQ4K<CHB>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  uint8_t* ring = smem + warp * S * C::STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + WARPS * S * C::STAGE) + warp * S;
+  float* red = reinterpret_cast<float*>(smem + WARPS * S * C::STAGE + WARPS * S * 8);  // [WARPS][32]
+  XShared xsh;
+  xsh.xq = reinterpret_cast<int8_t*>(red + WARPS * 32);
+  xsh.xs = reinterpret_cast<float2*>(xsh.xq + 2 * K);
+
+  // Work: 32-row units.  The CTA's warps form WARPS/ksplit slots; a slot's
+  // ksplit warps share one unit and split its K range by chunks of CHB
+  // super-blocks (chunk c goes to part c % ksplit).  Small M uses a large
+  // ksplit so every SM streams; large M uses ksplit = 1.
+  const int slots = WARPS / ksplit, slot = warp / ksplit, kpart = warp % ksplit;
+  const int nb = K / 256, nch = (nb + CHB - 1) / CHB;
+  const long long rb = (long long)nb * C::BB;
+  const int nunits = (M + C::ROWS - 1) / C::ROWS;
+  const int ngroups = (nunits + slots - 1) / slots;  // a group = `slots` consecutive units
+  const int my_groups = blockIdx.x < ngroups ? (ngroups - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int my_chunks = kpart < nch ? (nch - 1 - kpart) / ksplit + 1 : 0;
+  const int ntiles = my_groups * my_chunks;
+
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  // Tile tt = (group tt / my_chunks, chunk kpart + ksplit * (tt % my_chunks)).
+  // Each lane copies one row; lane 0 arms the barrier first.
+  auto issue = [&](int tt) {
+    const int u = (blockIdx.x + (tt / my_chunks) * gridDim.x) * slots + slot;
+    const int c = kpart + ksplit * (tt % my_chunks), st = tt % S;
+    const int b0 = c * CHB, nblk = min(CHB, nb - b0);
+    const int r0 = u * C::ROWS, nr = max(0, min(C::ROWS, M - r0));
+    const unsigned bytes = (unsigned)(nblk * C::BB);
+    if (lane == 0) mbar_expect_tx(&bars[st], bytes * (unsigned)nr);
+    __syncwarp();
+    if (lane < nr)
+      bulk_g2s(ring + st * C::STAGE + lane * C::SLOT, W + (long long)(r0 + lane) * rb + (long long)b0 * C::BB, bytes,
+               &bars[st]);
+  };
+  for (int tt = 0; tt < min(S, ntiles); ++tt) issue(tt);
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  build_x_shared(x, K, xsh, warp, lane, WARPS);
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  const int gs = g >> 1;                  // sub-block (within a group of 4) whose B columns this lane holds
+  const int boff = (g & 1) * 32 + t * 8;  // limb g&1, quad t
+  const float qscale = (t & 1) ? 0.0625f : 1.0f;  // odd sub-blocks are high nibbles, carried as 16*q
+  bool ok = true;
+
+  for (int ui = 0; ui < my_groups; ++ui) {
+    const int u = (blockIdx.x + ui * gridDim.x) * slots + slot;
+    const int r0 = u * C::ROWS, nr = max(0, min(C::ROWS, M - r0));
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24; this lane's sub-blocks t and 4+t
+    for (int ci = 0; ci < my_chunks && ok; ++ci) {
+      const int tt = ui * my_chunks + ci, st = tt % S;
+      const int c = kpart + ksplit * ci, b0 = c * CHB, nblk = min(CHB, nb - b0);
+      if (!mbar_wait_bounded(&bars[st], (unsigned)((tt / S) & 1))) { ok = false; break; }
+      const uint8_t* base = ring + st * C::STAGE + g * C::SLOT;  // row g + 8i at base + 8i*SLOT
+      for (int bi = 0; bi < nblk; ++bi) {
+        const int sb = b0 + bi;
+        const uint8_t* blk = base + bi * C::BB;
+        uint4 hd[4];
+        float dd[4], dm[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          hd[i] = *reinterpret_cast<const uint4*>(blk + 8 * i * C::SLOT);
+          dd[i] = h2f((uint16_t)(hd[i].x & 0xffffu));
+          dm[i] = h2f((uint16_t)(hd[i].x >> 16));
+        }
+#pragma unroll
+        for (int grp = 0; grp < 2; ++grp) {
+          const uint2 bx = *reinterpret_cast<const uint2*>(xsh.xq + (sb * 8 + 4 * grp + gs) * 64 + boff);
+          int D[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // [m-tile][frag]
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int p = 2 * grp + jj;  // nibble pair p: sub-blocks 2p (low), 2p+1 (high)
+            const bool mlo = gs == 2 * jj, mhi = gs == 2 * jj + 1;
+            const uint32_t bl0 = mlo ? bx.x : 0u, bl1 = mlo ? bx.y : 0u;
+            const uint32_t bh0 = mhi ? bx.x : 0u, bh1 = mhi ? bx.y : 0u;
+            const int q0 = 16 + 32 * p + 4 * t;
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+              const uint8_t* r = blk + 16 * mt * C::SLOT;
+              const uint32_t a0 = *reinterpret_cast<const uint32_t*>(r + q0);
+              const uint32_t a1 = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + q0);
+              const uint32_t a2 = *reinterpret_cast<const uint32_t*>(r + q0 + 16);
+              const uint32_t a3 = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + q0 + 16);
+              imma16832(D[mt], a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu, bl0, bl1);
+              imma16832(D[mt], a0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, a2 & 0xF0F0F0F0u, a3 & 0xF0F0F0F0u, bh0, bh1);
+            }
+          }
+          // D[mt][0..1]: row 16mt+g, limbs (L0, L1) of sub-block s = 4 grp + t; D[mt][2..3]: row 16mt+g+8.
+          const float2 xs = xsh.xs[sb * 8 + 4 * grp + t];
+          const float fx = xs.x * qscale;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int mt = i >> 1, e = (i & 1) * 2;
+            const float sq = ((float)D[mt][e] + (float)D[mt][e + 1] * (1.0f / 254.0f)) * fx;  // sum_k q_k x_k
+            const uint4 hh = hd[i];
+            const unsigned yb = (hh.y >> (8 * t)) & 0xffu, zb = (hh.z >> (8 * t)) & 0xffu;
+            unsigned sc, mn;
+            if (grp == 0) {  // q4kScaleMin, s < 4
+              sc = yb & 63u; mn = zb & 63u;
+            } else {         // s >= 4
+              const unsigned wb = (hh.w >> (8 * t)) & 0xffu;
+              sc = (wb & 15u) | ((yb >> 6) << 4); mn = (wb >> 4) | ((zb >> 6) << 4);
+            }
+            acc[i] += (dd[i] * (float)sc) * sq - (dm[i] * (float)mn) * xs.y;
+          }
+        }
+      }
+      __syncwarp();
+      if (tt + S < ntiles) issue(tt + S);
+    }
+    // CTA reduction of the K-split partial sums for this unit's 32 rows.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float v = acc[i];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if (t == 0) red[warp * 32 + 16 * (i >> 1) + 8 * (i & 1) + g] = v;
+    }
+    __syncthreads();
+    if (kpart == 0) {
+      float v = 0.f;
+      for (int w = 0; w < min(ksplit, nch); ++w) v += red[(warp + w) * 32 + lane];
+      if (lane < nr) y[r0 + lane] = v;
+    }
+    __syncthreads();
+  }
+}
+
+template <int WARPS, int S, int CHB>
+static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl) {
+  auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB>;
+  const int smem = WARPS * S * MmaQ4K<CHB>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 2 + (k / 32) * 8;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  static int set_for = 0, sms = 0, per_sm = 0;
+  if (smem > set_for) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    set_for = smem;
+  }
+  if (!sms) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  static int occ_smem = -1;
+  if (occ_smem != smem) {  // occupancy depends on k through the shared x buffer
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, smem);
+    if (per_sm < 1) per_sm = 1;
+    occ_smem = smem;
+  }
+  const int units = (m + MmaQ4K<CHB>::ROWS - 1) / MmaQ4K<CHB>::ROWS;
+  const int nch = (k / 256 + CHB - 1) / CHB;
+  const int cap = sms * per_sm;
+  int ksplit = 1;  // smallest power of two that gives every resident warp a unit
+  while (ksplit < WARPS && ksplit < nch && (long long)units * ksplit < (long long)cap * WARPS) ksplit *= 2;
+  const int groups = (units + WARPS / ksplit - 1) / (WARPS / ksplit);
+  const int grid = groups < cap ? groups : cap;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(WARPS * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, y, m, k, ksplit);
+}
+
+cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl) {
+  return launch_q4k_mma_t<8, 2, 2>(w, x, y, m, k, st, pdl);
+}
+
+}  // namespace vtb

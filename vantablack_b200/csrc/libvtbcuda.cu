@@ -2,5 +2,6 @@
 // kernels share device globals (the error word), so they are compiled
 // together without relocatable device code.
 #include "gemv.cu"
+#include "gemv_mma.cu"
 #include "quant_aux.cu"
 #include "api.cu"
