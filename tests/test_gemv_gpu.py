@@ -130,3 +130,24 @@ def test_context_bridge_matmul():
     for b in (wb, xb, yb):
         lib.vtb_cuda_release(b)
     lib.vtb_cuda_destroy(ctx)
+
+
+@pytest.mark.parametrize("q", [S.Q4_K, S.Q6_K, S.Q8_0, S.Q5_K])
+@pytest.mark.parametrize("kind", ["huge", "tiny", "outliers", "zeros"])
+def test_gemv_activation_ranges(q, kind):
+    """Activation magnitudes far from N(0,1): per-sub-block scaling must hold
+    the 1e-4 bound (huge/tiny values, one outlier per block, zero blocks)."""
+    rng = np.random.default_rng(77)
+    m, k = 512, 4096
+    w = S.quant_tensor(rng, q, m, k)
+    x = S.activations(rng, k)
+    if kind == "huge":
+        x *= np.float32(3e4)
+    elif kind == "tiny":
+        x *= np.float32(1e-6)
+    elif kind == "outliers":
+        x[::32] *= np.float32(1000.0)
+    else:
+        x[: k // 2] = 0.0
+    y = ops().gemv(q, torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda(), m, k).cpu().numpy()
+    assert rel_err(y, O.matmul(q, w, x, m, k)) <= TOL

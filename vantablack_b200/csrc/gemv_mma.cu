@@ -12,15 +12,16 @@
 //    nibbles kept in place, 16*q (AND 0xF0F0F0F0), of sub-block 2j+1.  One
 //    m16n8k32 MMA covers 16 rows x one 32-weight sub-block.
 //  * B (s8): per sub-block s, x is scaled by 2^-e_s so that max|x| lands in
-//    [32, 64), then split into two int8 limbs:  x/2^e_s ~ L0 + L1/254 with
-//    L0 = rint(x'), L1 = rint((x' - L0) * 254)  (|error| <= 1/508 in a block
-//    whose max is >= 32, i.e. < 2^-14 relative to the block max).
-//  * Block-diagonal B: the 8 columns hold (L0, L1) of 4 consecutive
+//    [32, 64), then split into four int8 limbs x/2^e_s ~ sum_c L_c 254^-c,
+//    L0 = rint(x'), L_c = rint(residual * 254) (|error| < 254^-3, about
+//    2^-29 relative to the block max).
+//  * Block-diagonal B: the 8 columns hold (L0, L1) -- and, in a second MMA
+//    pass over the same A registers, (L2, L3) -- of 4 consecutive
 //    sub-blocks; the MMA of sub-block s only has its own column pair
-//    non-zero, so the int32 accumulator D[r, 2s'+c] = sum_k A[r,k] L_c[k]
-//    is an EXACT integer dot per (row, sub-block, limb).
-//  * Epilogue per (row, sub-block): sum_k q x = 2^e (D0 + D1/254) (/16 for
-//    high nibbles), and y += (d*sc) * sum q x - (dmin*mn) * sum x -- the
+//    non-zero, so the int32 accumulators D[r, 2s'+c] = sum_k A[r,k] L_c[k]
+//    are EXACT integer dots per (row, sub-block, limb).
+//  * Epilogue per (row, sub-block): sum_k q x = 2^e sum_c D_c 254^-c (/16
+//    for high nibbles), and y += (d*sc) * sum q x - (dmin*mn) * sum x -- the
 //    reference's w = d1*q - m1 (simd.zig:221-243) distributed over the
 //    sub-block.  fp32 accumulation; tolerance-checked (<= 1e-4).
 //
@@ -42,7 +43,7 @@ __device__ __forceinline__ void imma16832(int* d, uint32_t a0, uint32_t a1, uint
 }
 
 // Shared layout of the activation vector, written once per CTA:
-//   xq[s] : 64 bytes per sub-block s = [limb c][lane-quad t][8 bytes]; the 8
+//   xq[s] : 128 bytes per sub-block s = [limb c][lane-quad t][8 bytes]; the 8
 //           bytes are the B-fragment registers b0 (k = 4t..4t+3) and b1
 //           (k = 16+4t..16+4t+3) of column limb c.
 //   xs[s] : {2^e_s, sum_k x_k}
@@ -83,19 +84,22 @@ __device__ __forceinline__ void build_x_shared(const float* __restrict__ x, int 
       const float sx = __uint_as_float((uint32_t)(127 + e) << 23);
       const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
       const float xv[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};  // exact (power of two)
-      uint32_t l0w = 0, l1w = 0;
+      uint32_t lw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const float l0 = rintf(xv[c]);
-        const float l1 = rintf((xv[c] - l0) * 254.f);
-        l0w |= ((uint32_t)(int)l0 & 0xffu) << (8 * c);
-        l1w |= ((uint32_t)(int)l1 & 0xffu) << (8 * c);
+        float r = xv[c];
+#pragma unroll
+        for (int li = 0; li < 4; ++li) {  // r - L is exact in f32; each step scales by 254
+          const float L = rintf(r);
+          lw[li] |= ((uint32_t)(int)L & 0xffu) << (8 * c);
+          r = (r - L) * 254.f;
+        }
       }
       const int s = gi * 4 + sub;
       // element l = 4*part + c sits at t = part & 3, half = part >> 2, byte c
-      int8_t* dst = xsh.xq + s * 64 + (part & 3) * 8 + (part >> 2) * 4;
-      *reinterpret_cast<uint32_t*>(dst) = l0w;
-      *reinterpret_cast<uint32_t*>(dst + 32) = l1w;
+      int8_t* dst = xsh.xq + s * 128 + (part & 3) * 8 + (part >> 2) * 4;
+#pragma unroll
+      for (int li = 0; li < 4; ++li) *reinterpret_cast<uint32_t*>(dst + 32 * li) = lw[li];
       if (part == 0) xsh.xs[s] = make_float2(sx, sum);
     }
   }
@@ -110,7 +114,7 @@ struct MmaQ4K {
 };
 
 template <int WARPS, int S, int CHB>
-__global__ void __launch_bounds__(WARPS * 32)
+__global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
                     int ksplit) {
   using C = MmaQ4K<CHB>;
@@ -123,7 +127,7 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
   float* red = reinterpret_cast<float*>(smem + WARPS * S * C::STAGE + WARPS * S * 8);  // [WARPS][32]
   XShared xsh;
   xsh.xq = reinterpret_cast<int8_t*>(red + WARPS * 32);
-  xsh.xs = reinterpret_cast<float2*>(xsh.xq + 2 * K);
+  xsh.xs = reinterpret_cast<float2*>(xsh.xq + 4 * K);
 
   // Work: 32-row units.  The CTA's warps form WARPS/ksplit slots; a slot's
   // ksplit warps share one unit and split its K range by chunks of CHB
@@ -192,14 +196,19 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
         }
 #pragma unroll
         for (int grp = 0; grp < 2; ++grp) {
-          const uint2 bx = *reinterpret_cast<const uint2*>(xsh.xq + (sb * 8 + 4 * grp + gs) * 64 + boff);
-          int D[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // [m-tile][frag]
+          const int8_t* xb = xsh.xq + (sb * 8 + 4 * grp + gs) * 128 + boff;
+          const uint2 bx = *reinterpret_cast<const uint2*>(xb);        // limb (g&1)
+          const uint2 bz = *reinterpret_cast<const uint2*>(xb + 64);   // limb 2 + (g&1)
+          int D[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // [m-tile][frag], limbs 0/1
+          int E[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // limbs 2/3
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {
             const int p = 2 * grp + jj;  // nibble pair p: sub-blocks 2p (low), 2p+1 (high)
             const bool mlo = gs == 2 * jj, mhi = gs == 2 * jj + 1;
             const uint32_t bl0 = mlo ? bx.x : 0u, bl1 = mlo ? bx.y : 0u;
             const uint32_t bh0 = mhi ? bx.x : 0u, bh1 = mhi ? bx.y : 0u;
+            const uint32_t zl0 = mlo ? bz.x : 0u, zl1 = mlo ? bz.y : 0u;
+            const uint32_t zh0 = mhi ? bz.x : 0u, zh1 = mhi ? bz.y : 0u;
             const int q0 = 16 + 32 * p + 4 * t;
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
@@ -208,8 +217,12 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
               const uint32_t a1 = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + q0);
               const uint32_t a2 = *reinterpret_cast<const uint32_t*>(r + q0 + 16);
               const uint32_t a3 = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + q0 + 16);
-              imma16832(D[mt], a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu, bl0, bl1);
-              imma16832(D[mt], a0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, a2 & 0xF0F0F0F0u, a3 & 0xF0F0F0F0u, bh0, bh1);
+              const uint32_t l0 = a0 & 0x0F0F0F0Fu, l1 = a1 & 0x0F0F0F0Fu, l2 = a2 & 0x0F0F0F0Fu, l3 = a3 & 0x0F0F0F0Fu;
+              const uint32_t h0 = a0 & 0xF0F0F0F0u, h1 = a1 & 0xF0F0F0F0u, h2 = a2 & 0xF0F0F0F0u, h3 = a3 & 0xF0F0F0F0u;
+              imma16832(D[mt], l0, l1, l2, l3, bl0, bl1);
+              imma16832(D[mt], h0, h1, h2, h3, bh0, bh1);
+              imma16832(E[mt], l0, l1, l2, l3, zl0, zl1);
+              imma16832(E[mt], h0, h1, h2, h3, zh0, zh1);
             }
           }
           // D[mt][0..1]: row 16mt+g, limbs (L0, L1) of sub-block s = 4 grp + t; D[mt][2..3]: row 16mt+g+8.
@@ -218,7 +231,8 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int mt = i >> 1, e = (i & 1) * 2;
-            const float sq = ((float)D[mt][e] + (float)D[mt][e + 1] * (1.0f / 254.0f)) * fx;  // sum_k q_k x_k
+            const float lo = (float)E[mt][e] * (1.0f / 254.0f) + (float)E[mt][e + 1] * (1.0f / 64516.0f);
+            const float sq = ((float)D[mt][e] + ((float)D[mt][e + 1] + lo) * (1.0f / 254.0f)) * fx;  // sum_k q_k x_k
             const uint4 hh = hd[i];
             const unsigned yb = (hh.y >> (8 * t)) & 0xffu, zb = (hh.z >> (8 * t)) & 0xffu;
             unsigned sc, mn;
@@ -256,7 +270,7 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
 template <int WARPS, int S, int CHB>
 static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl) {
   auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB>;
-  const int smem = WARPS * S * MmaQ4K<CHB>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 2 + (k / 32) * 8;
+  const int smem = WARPS * S * MmaQ4K<CHB>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   static int set_for = 0, sms = 0, per_sm = 0;
   if (smem > set_for) {
