@@ -37,6 +37,7 @@ extern "C" {
 #define VTB_CUDA_ERR_OOM (-4)
 #define VTB_CUDA_ERR_DEVICE (-5)
 #define VTB_CUDA_ERR_DISPATCH (-6)
+#define VTB_CUDA_ERR_STREAM_ABORTED (-7)
 #define VTB_CUDA_ERR_UNSUPPORTED (-8)
 #define VTB_CUDA_ERR_TIMEOUT (-9)
 #define VTB_CUDA_ERR_COMM (-10)
@@ -142,6 +143,69 @@ int vtb_cuda_matmul_q5_k(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf
                          VtbCudaBuf *acts_buf, size_t m, size_t k);
 int vtb_cuda_matmul_q6_k(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
                          VtbCudaBuf *acts_buf, size_t m, size_t k);
+
+/* ------------------------------------------------------------------ */
+/* Llama forward loop (the backend vtable, src/runtime/backend.zig:67-97) */
+/* ------------------------------------------------------------------ */
+
+/* LlamaConfig (src/runtime/model.zig:40-149), GGUF llama fields only. */
+typedef struct {
+  int32_t dim, n_layers, n_heads, n_kv_heads, head_dim, ffn_dim, vocab_size, max_seq;
+  float rope_base, rms_eps;
+} VtbCudaLlamaConfig;
+
+/* LayerWeights (model.zig:172-189): HOST pointers to each tensor's packed
+ * bytes (e.g. into the GGUF mmap) and ggml type ids; norms are f32. */
+typedef struct {
+  const void *attn_q, *attn_k, *attn_v, *attn_o, *ffn_gate, *ffn_up, *ffn_down;
+  const float *attn_norm, *ffn_norm;
+  int32_t q_attn_q, q_attn_k, q_attn_v, q_attn_o, q_ffn_gate, q_ffn_up, q_ffn_down;
+} VtbCudaLayerWeights;
+
+typedef struct VtbCudaModel VtbCudaModel;
+typedef struct VtbCudaState VtbCudaState;
+
+/* Upload every weight once to the context's device (Model.init + the Metal
+ * backend's initShards, model.zig:201-243, metal_backend.zig:134).  Q|K|V and
+ * gate|up are row-concatenated when their quant types match (the reference's
+ * -Dweight_fusion fuseRowConcat, model.zig:358-378).  Every projection must be
+ * Q8_0/Q4_K/Q5_K/Q6_K: anything else is refused with NULL (no CPU fallback;
+ * BackendUnsupportedQuant, backend.zig:61). */
+VtbCudaModel *vtb_cuda_model_create(VtbCudaCtx *ctx, const VtbCudaLlamaConfig *cfg,
+                                    const VtbCudaLayerWeights *layers, const void *token_embd,
+                                    int32_t q_token_embd, const float *output_norm, const void *output_w,
+                                    int32_t q_output);
+void vtb_cuda_model_destroy(VtbCudaModel *m);
+size_t vtb_cuda_model_weight_bytes(VtbCudaModel *m);
+
+/* Per-session device state (forward.zig State :33-113 + KvCache kv_cache.zig:20-73):
+ * n_seqs independent sequences decoded together (batch decode), and up to
+ * max_rows rows per step (prefill chunk size). */
+VtbCudaState *vtb_cuda_state_create(VtbCudaModel *m, int32_t n_seqs, int32_t max_rows);
+void vtb_cuda_state_destroy(VtbCudaState *s);
+/* KvCache.reset (kv_cache.zig:80). */
+int vtb_cuda_state_reset(VtbCudaState *s);
+/* KvCache.pos of sequence `seq` (host-authoritative). */
+int64_t vtb_cuda_state_pos(VtbCudaState *s, int32_t seq);
+
+/* The vtable, slot by slot.  begin_token is stepWithBackend's preamble
+ * (token checks + gatherEmbedding, forward.zig:158-163) for one token per
+ * sequence; layer_step / final_step / finalize_token are the VTable slots.
+ * finalize_token copies logits ([n_seqs][vocab], may be NULL) and the
+ * greedy argmax ([n_seqs], may be NULL) to the host and advances the cache. */
+int vtb_cuda_begin_token(VtbCudaState *s, const int32_t *tokens);
+int vtb_cuda_layer_step(VtbCudaState *s, int32_t layer);
+int vtb_cuda_final_step(VtbCudaState *s);
+int vtb_cuda_finalize_token(VtbCudaState *s, float *logits, int32_t *argmax);
+
+/* One whole decode step for all sequences (stepWithBackend), replayed as a
+ * CUDA graph captured on first use. */
+int vtb_cuda_step(VtbCudaState *s, const int32_t *tokens, float *logits, int32_t *argmax);
+
+/* Batched prompt prefill of one sequence (prefillCpu, src/runtime/prefill.zig:111-147):
+ * advances the sequence by n; logits/argmax of the last token. */
+int vtb_cuda_prefill(VtbCudaState *s, int32_t seq, const int32_t *tokens, int32_t n, float *logits,
+                     int32_t *argmax);
 
 #ifdef __cplusplus
 }

@@ -49,6 +49,19 @@ SIGNATURES = {
     "vtb_cuda_matmul_q4_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
     "vtb_cuda_matmul_q5_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
     "vtb_cuda_matmul_q6_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_model_create": (_vp, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _i32]),
+    "vtb_cuda_model_destroy": (None, [_vp]),
+    "vtb_cuda_model_weight_bytes": (_sz, [_vp]),
+    "vtb_cuda_state_create": (_vp, [_vp, _i32, _i32]),
+    "vtb_cuda_state_destroy": (None, [_vp]),
+    "vtb_cuda_state_reset": (_int, [_vp]),
+    "vtb_cuda_state_pos": (_i64, [_vp, _i32]),
+    "vtb_cuda_begin_token": (_int, [_vp, _vp]),
+    "vtb_cuda_layer_step": (_int, [_vp, _i32]),
+    "vtb_cuda_final_step": (_int, [_vp]),
+    "vtb_cuda_finalize_token": (_int, [_vp, _vp, _vp]),
+    "vtb_cuda_step": (_int, [_vp, _vp, _vp, _vp]),
+    "vtb_cuda_prefill": (_int, [_vp, _i32, _vp, _i32, _vp, _vp]),
 }
 
 

@@ -10,8 +10,10 @@
 #include "common.cuh"
 
 namespace vtb {
-cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl);
-cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl);
+cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                        int accumulate = 0);
+cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                                int accumulate = 0);
 cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* dx, float* y, int m, int k,
                                   cudaStream_t st, bool pdl);
 cudaError_t launch_dequant(int q, const void* w, float* out, long long n, cudaStream_t st);

@@ -271,7 +271,7 @@ __device__ __forceinline__ float lane_dot_q80_i8(const uint8_t* blk, const XQSli
 template <int Q, int R, int S, int WARPS, bool XQ>
 __global__ void __launch_bounds__(WARPS * 32)
 gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const float* __restrict__ dx,
-            float* __restrict__ y, int M, int K) {
+            float* __restrict__ y, int M, int K, int accumulate) {
   const float* x = static_cast<const float*>(xv);
   constexpr int CH = GemvCfg<Q>::CH, BB = Fmt<Q>::bytes, EL = Fmt<Q>::elems;
   constexpr int SLOT = Slot<Q>::BYTES, STAGE = R * SLOT;
@@ -374,7 +374,7 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const float s = warp_sum(acc[r]);
-        if (lane == r && r < nr) y[r0 + r] = s;
+        if (lane == r && r < nr) y[r0 + r] = accumulate ? y[r0 + r] + s : s;
         acc[r] = 0.f;
       }
     }
@@ -384,7 +384,7 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
 // ---------------- host launcher ----------------
 template <int Q, int R, int S, int WARPS, bool XQ = false>
 static cudaError_t launch_gemv_t(const void* w, const void* x, const float* dx, float* y, int m, int k,
-                                 cudaStream_t st, bool pdl) {
+                                 cudaStream_t st, bool pdl, int accumulate = 0) {
   auto kern = gemv_kernel<Q, R, S, WARPS, XQ>;
   constexpr int smem = WARPS * S * R * Slot<Q>::BYTES + WARPS * S * 8;
   static int max_ctas_per_sm = -1;
@@ -413,15 +413,16 @@ static cudaError_t launch_gemv_t(const void* w, const void* x, const float* dx, 
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, dx, y, m, k);
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, dx, y, m, k, accumulate);
 }
 
-cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl) {
+cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                        int accumulate) {
   switch (q) {
-    case Q4_K: return launch_gemv_t<Q4_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl);
-    case Q5_K: return launch_gemv_t<Q5_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl);
-    case Q6_K: return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl);
-    case Q8_0: return launch_gemv_t<Q8_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl);
+    case Q4_K: return launch_gemv_t<Q4_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
+    case Q5_K: return launch_gemv_t<Q5_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
+    case Q6_K: return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
+    case Q8_0: return launch_gemv_t<Q8_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
     default: return cudaErrorInvalidValue;
   }
 }

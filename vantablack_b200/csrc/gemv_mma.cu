@@ -116,7 +116,7 @@ struct MmaQ4K {
 template <int WARPS, int S, int CHB>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
-                    int ksplit) {
+                    int ksplit, int accumulate) {
   using C = MmaQ4K<CHB>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -261,14 +261,15 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
     if (kpart == 0) {
       float v = 0.f;
       for (int w = 0; w < min(ksplit, nch); ++w) v += red[(warp + w) * 32 + lane];
-      if (lane < nr) y[r0 + lane] = v;
+      if (lane < nr) y[r0 + lane] = accumulate ? y[r0 + lane] + v : v;
     }
     __syncthreads();
   }
 }
 
 template <int WARPS, int S, int CHB>
-static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl) {
+static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                                    int accumulate) {
   auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB>;
   const int smem = WARPS * S * MmaQ4K<CHB>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
@@ -306,11 +307,12 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, y, m, k, ksplit);
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, y, m, k, ksplit, accumulate);
 }
 
-cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl) {
-  return launch_q4k_mma_t<8, 2, 2>(w, x, y, m, k, st, pdl);
+cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                                int accumulate) {
+  return launch_q4k_mma_t<8, 2, 2>(w, x, y, m, k, st, pdl, accumulate);
 }
 
 }  // namespace vtb

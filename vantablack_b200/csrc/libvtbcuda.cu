@@ -5,3 +5,4 @@
 #include "gemv_mma.cu"
 #include "quant_aux.cu"
 #include "api.cu"
+#include "model.cu"

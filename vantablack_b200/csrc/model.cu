@@ -1,0 +1,781 @@
+// model.cu -- the Llama forward loop on the GPU: the CUDA counterpart of the
+// reference's CPU backend (src/runtime/backend_cpu.zig layerStep/finalStep)
+// and Metal segment (src/runtime/forward.zig:419-520), behind the vtable
+// seam of src/runtime/backend.zig:67-97.
+//
+// Device state per VtbCudaState:
+//   x[rows][dim]        residual stream (forward.zig State.x)
+//   xb[rows][dim]       normed activations
+//   qkv[rows][qd+2kvd]  fused Q|K|V projection output
+//   att[rows][qd]       attention output
+//   gu[rows][2*ffn]     fused gate|up output, h[rows][ffn] = swiglu
+//   logits[rows][vocab], argmax[rows]
+//   kv cache: K and V, f32, [seq][layer][max_seq][n_kv_heads*head_dim]
+//             (kv_cache.zig:20-73 layout, one slab per sequence)
+// Row r of a step is token `tok[r]` of sequence `seq[r]` at position
+// `pos[r]`: a decode step has one row per sequence, a prefill step has one
+// row per prompt token of one sequence (prefill.zig:111-232 semantics).
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "../../include/vtb_cuda.h"
+#include "common.cuh"
+
+namespace vtb {
+
+cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                        int accumulate);
+cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                                int accumulate);
+cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* out, int dim, int n_tok,
+                         cudaStream_t st);
+
+static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
+                            int accumulate) {
+  if (q == Q4_K) return launch_gemv_q4k_mma(w, x, y, m, k, st, true, accumulate);
+  return launch_gemv(q, w, x, y, m, k, st, true, accumulate);
+}
+
+// ---------------- kernels ----------------
+
+// rmsNorm (math.zig:11-32): out = (x * w) * (1 / sqrt(mean(x^2) + eps)), one
+// CTA per row.  With `res`, the row is first updated x += res (the residual
+// add of addInto, math.zig:178-187, fused; used after a tensor-parallel
+// all-reduce).
+__global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ res, const float* __restrict__ w,
+                               float* __restrict__ out, int n, float eps) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int r = blockIdx.x;
+  float* xr = x + (long long)r * n;
+  const float* rr = res ? res + (long long)r * n : nullptr;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = xr[i];
+    if (rr) {
+      v += rr[i];
+      xr[i] = v;
+    }
+    ss += v * v;
+  }
+  __shared__ float part[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) part[0] = v;
+  }
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(part[0] / (float)n + eps);
+  asm volatile("griddepcontrol.launch_dependents;");
+  float* o = out + (long long)r * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = (xr[i] * w[i]) * inv;
+}
+
+// rope (math.zig:88-104, interleaved pairs) on the row's Q and K heads, then
+// the KV-cache write of K and V at the row's position (forward.zig:268-269).
+struct RowInfo {
+  const int32_t* seq;
+  const int32_t* pos;
+};
+
+__global__ void rope_kv_kernel(float* __restrict__ qkv, float* __restrict__ kc, float* __restrict__ vc, RowInfo ri,
+                               int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd, float base) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int r = blockIdx.x;
+  const int qd = n_heads * hd, kvd = n_kv * hd, stride = qd + 2 * kvd;
+  float* q = qkv + (long long)r * stride;
+  float* k = q + qd;
+  const float* v = k + kvd;
+  const int pos = ri.pos[r], seq = ri.seq[r];
+  const float pos_f = (float)pos;
+  const long long slot = (((long long)seq * n_layers + layer) * max_seq + pos) * kvd;
+  const int half = hd / 2;
+  for (int p = threadIdx.x; p < (n_heads + n_kv) * half; p += blockDim.x) {
+    const int h = p / half, i = 2 * (p % half);
+    const float e = (float)i / (float)hd;
+    const float inv_freq = 1.0f / powf(base, e);
+    const float theta = pos_f * inv_freq;
+    const float c = cosf(theta), s = sinf(theta);
+    float* ptr = h < n_heads ? q + h * hd + i : k + (h - n_heads) * hd + i;
+    const float x0 = ptr[0], x1 = ptr[1];
+    const float a = x0 * c, b = x1 * s, pp = x0 * s, qq = x1 * c;
+    const float y0 = a - b, y1 = pp + qq;
+    if (h < n_heads) {
+      ptr[0] = y0;
+      ptr[1] = y1;
+    } else {
+      kc[slot + (h - n_heads) * hd + i] = y0;
+      kc[slot + (h - n_heads) * hd + i + 1] = y1;
+    }
+  }
+  for (int i = threadIdx.x; i < kvd; i += blockDim.x) vc[slot + i] = v[i];
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// Decode/causal attention (cpuAttention forward.zig:187-228, attentionCausal
+// prefill.zig:237-287): row r attends positions [0, pos[r]] of its sequence.
+// Split-K ("flash decode"): CTA (kv_head, row, split) handles positions
+// [split*CHUNK, ...) for the GQA group of q heads that share the kv head,
+// and writes a partial (max, sum, acc[hd]) per q head; attn_combine merges.
+constexpr int ATT_CHUNK = 256;
+constexpr int ATT_THREADS = 128;
+
+__global__ void __launch_bounds__(ATT_THREADS)
+attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
+                    RowInfo ri, int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd,
+                    float* __restrict__ part, int nsplit) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  extern __shared__ float sm[];
+  const int kvh = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
+  const int G = n_heads / n_kv;
+  const int qd = n_heads * hd, kvd = n_kv * hd;
+  const int pos = ri.pos[r], seq = ri.seq[r];
+  const int len = pos + 1, t0 = sp * ATT_CHUNK, t1 = min(len, t0 + ATT_CHUNK);
+  float* qs = sm;                  // [G][hd]
+  float* sc = sm + G * hd;         // [G][ATT_CHUNK]
+  float* pr = part + (((long long)r * n_heads + kvh * G) * nsplit + sp) * (hd + 2);  // head stride nsplit*(hd+2)
+  if (t0 >= t1) {
+    if (threadIdx.x < G) {
+      float* p = pr + (long long)threadIdx.x * nsplit * (hd + 2);
+      p[0] = -INFINITY;
+      p[1] = 0.f;
+    }
+    return;
+  }
+  const float inv_sqrt_hd = 1.0f / sqrtf((float)hd);
+  const float* q = qkv + (long long)r * (qd + 2 * kvd) + kvh * G * hd;
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[i];
+  __syncthreads();
+  const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
+  // scores: one thread per position, all G heads
+  for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
+    const float4* kt = reinterpret_cast<const float4*>(kc + (lbase + t) * kvd + kvh * hd);
+    for (int h = 0; h < G; ++h) {
+      const float4* qh = reinterpret_cast<const float4*>(qs + h * hd);
+      float s = 0.f;
+      for (int d = 0; d < hd / 4; ++d) {
+        const float4 a = kt[d], b = qh[d];
+        s += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+      }
+      sc[h * ATT_CHUNK + (t - t0)] = s * inv_sqrt_hd;
+    }
+  }
+  __syncthreads();
+  // per head: local max and exp-sum (warp h%4 handles head h)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n = t1 - t0;
+  __shared__ float hm[64], hl[64];
+  for (int h = warp; h < G; h += ATT_THREADS / 32) {
+    float m = -INFINITY;
+    for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h * ATT_CHUNK + i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int i = lane; i < n; i += 32) {
+      const float e = expf(sc[h * ATT_CHUNK + i] - m);
+      sc[h * ATT_CHUNK + i] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      hm[h] = m;
+      hl[h] = l;
+    }
+  }
+  __syncthreads();
+  // acc[h][d] = sum_t p[h][t] * v[t][d]
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+    const int h = i / hd, d = i % hd;
+    const float* vt = vc + (lbase + t0) * kvd + kvh * hd + d;
+    const float* ph = sc + h * ATT_CHUNK;
+    float a = 0.f;
+    for (int t = 0; t < n; ++t) a += ph[t] * vt[(long long)t * kvd];
+    float* p = pr + (long long)h * nsplit * (hd + 2);
+    p[2 + d] = a;
+    if (d == 0) {
+      p[0] = hm[h];
+      p[1] = hl[h];
+    }
+  }
+}
+
+// Merge the splits of each (row, q head): out = sum_s acc_s e^{m_s - M} / sum_s l_s e^{m_s - M}.
+__global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ att, int n_heads, int hd,
+                                    int nsplit) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int h = blockIdx.x, r = blockIdx.y;
+  const float* p = part + ((long long)r * n_heads + h) * nsplit * (hd + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, p[s * (hd + 2)]);
+  float L = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float m = p[s * (hd + 2)];
+    if (m != -INFINITY) L += p[s * (hd + 2) + 1] * expf(m - M);
+  }
+  const float invL = 1.0f / L;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float a = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float m = p[s * (hd + 2)];
+      if (m != -INFINITY) a += p[s * (hd + 2) + 2 + d] * expf(m - M);
+    }
+    att[((long long)r * n_heads + h) * hd + d] = a * invL;
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// swiglu (math.zig:154-161): h = (g / (1 + e^-g)) * u, gu = [gate | up] per row.
+__global__ void swiglu_kernel(const float* __restrict__ gu, float* __restrict__ h, int ffn, int rows) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const long long n = (long long)rows * ffn;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / ffn, j = i % ffn;
+    const float g = gu[r * 2 * ffn + j], u = gu[r * 2 * ffn + ffn + j];
+    const float den = 1.0f + expf(-g);
+    h[i] = (g / den) * u;
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// argmax (math.zig:190-201): first index of the maximum of each row.
+__global__ void argmax_kernel(const float* __restrict__ logits, int32_t* __restrict__ out, int n) {
+  const int r = blockIdx.x;
+  const float* l = logits + (long long)r * n;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = l[i];
+    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+    out[r] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+// Row-concatenate rows [r0, r1) of `n_parts` tensors (fuseRowConcat, model.zig:358-378).
+}  // namespace vtb
+
+using namespace vtb;
+
+// ---------------- runtime ----------------
+
+namespace {
+
+struct DevLayer {
+  const uint8_t* qkv;  // fused Q|K|V rows (all three share quant and k)
+  const uint8_t* q; const uint8_t* k; const uint8_t* v;  // unfused fallback
+  const uint8_t* o;
+  const uint8_t* gu;   // fused gate|up rows
+  const uint8_t* gate; const uint8_t* up;
+  const uint8_t* down;
+  const float* attn_norm;
+  const float* ffn_norm;
+  int q_q, q_k, q_v, q_o, q_gate, q_up, q_down;
+};
+
+}  // namespace
+
+struct VtbCudaModel {
+  VtbCudaCtx* ctx;
+  int device;
+  VtbCudaLlamaConfig c;
+  std::vector<DevLayer> layers;
+  const uint8_t* embd;
+  int q_embd;
+  const float* out_norm;
+  const uint8_t* out_w;
+  int q_out;
+  void* blob = nullptr;  // one allocation for every weight
+  size_t blob_bytes = 0;
+};
+
+struct VtbCudaState {
+  VtbCudaModel* m;
+  cudaStream_t st;
+  int n_seqs, max_rows;
+  float *x, *xb, *qkv, *att, *gu, *h, *logits, *part;
+  int32_t *tok, *seq, *pos, *amax;
+  float *kc, *vc;
+  int32_t* hbuf;            // pinned host staging: tok | seq | pos (3 * max_rows)
+  int32_t* hamax;           // pinned host argmax
+  std::vector<int64_t> seq_pos;  // host-authoritative positions (KvCache.pos, forward.zig:161,168)
+  int rows = 0;             // rows of the step in flight
+  int nsplit;
+  cudaGraphExec_t graph = nullptr;
+  int graph_rows = -1;
+};
+
+// Error text goes to the same thread-local buffer as the rest of the shim
+// (vtb_cuda_last_error); the library is one translation unit.
+static int merr(int st, const char* msg) { return set_err(st, "%s", msg); }
+static int mcuda(cudaError_t e) { return cuda_status(e); }
+
+static bool q_ok(int q) { return host_quant_ok(q); }
+
+extern "C" {
+
+VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* cfg, const VtbCudaLayerWeights* lw,
+                                    const void* token_embd, int32_t q_token_embd, const float* output_norm,
+                                    const void* output_w, int32_t q_output) {
+  if (!ctx || !cfg || !lw || !token_embd || !output_norm || !output_w) {
+    merr(VTB_CUDA_ERR_INVALID_ARG, "null argument");
+    return nullptr;
+  }
+  const VtbCudaLlamaConfig c = *cfg;
+  if (c.dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads ||
+      c.head_dim % 4 || c.n_heads * c.head_dim != c.dim || c.ffn_dim <= 0 || c.vocab_size <= 0 || c.max_seq <= 0 ||
+      c.n_heads / c.n_kv_heads > 64) {
+    merr(VTB_CUDA_ERR_INVALID_ARG, "inconsistent Llama config");
+    return nullptr;
+  }
+  // Every projection must have a GPU kernel; no CPU fallback
+  // (modelGpuEligible, forward.zig:372-396; BackendUnsupportedQuant, backend.zig:61).
+  for (int l = 0; l < c.n_layers; ++l) {
+    const int qs[7] = {lw[l].q_attn_q, lw[l].q_attn_k, lw[l].q_attn_v, lw[l].q_attn_o,
+                       lw[l].q_ffn_gate, lw[l].q_ffn_up, lw[l].q_ffn_down};
+    for (int q : qs)
+      if (!q_ok(q)) {
+        merr(VTB_CUDA_ERR_UNSUPPORTED, "projection quant type has no CUDA kernel");
+        return nullptr;
+      }
+  }
+  if (!q_ok(q_token_embd) || !q_ok(q_output)) {
+    merr(VTB_CUDA_ERR_UNSUPPORTED, "embedding/output quant type has no CUDA kernel");
+    return nullptr;
+  }
+  const int d = c.dim, kvd = c.n_kv_heads * c.head_dim, f = c.ffn_dim;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const int ks[7] = {d, d, d, d, d, d, f};
+    const int qs[7] = {lw[l].q_attn_q, lw[l].q_attn_k, lw[l].q_attn_v, lw[l].q_attn_o,
+                       lw[l].q_ffn_gate, lw[l].q_ffn_up, lw[l].q_ffn_down};
+    for (int i = 0; i < 7; ++i)
+      if (ks[i] % host_block_elems(qs[i])) {
+        merr(VTB_CUDA_ERR_INVALID_ARG, "matrix width is not a whole number of blocks");
+        return nullptr;
+      }
+  }
+  VtbCudaModel* m = new (std::nothrow) VtbCudaModel();
+  if (!m) return nullptr;
+  m->ctx = ctx;
+  m->c = c;
+  cudaGetDevice(&m->device);
+  // Layout pass: offsets of every tensor in one blob (256-byte aligned).
+  auto rbytes = [](int q, int k) { return (size_t)host_row_bytes(q, k); };
+  size_t off = 0;
+  auto take = [&](size_t n) { size_t o = off; off = (off + n + 255) & ~size_t(255); return o; };
+  struct Off { size_t qkv, q, k, v, o, gu, gate, up, down, an, fn; bool fq, fg; };
+  std::vector<Off> offs(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    Off& o = offs[l];
+    o.fq = lw[l].q_attn_q == lw[l].q_attn_k && lw[l].q_attn_q == lw[l].q_attn_v;
+    o.fg = lw[l].q_ffn_gate == lw[l].q_ffn_up;
+    if (o.fq) o.qkv = take(rbytes(lw[l].q_attn_q, d) * (d + 2 * kvd));
+    else { o.q = take(rbytes(lw[l].q_attn_q, d) * d); o.k = take(rbytes(lw[l].q_attn_k, d) * kvd); o.v = take(rbytes(lw[l].q_attn_v, d) * kvd); }
+    o.o = take(rbytes(lw[l].q_attn_o, d) * d);
+    if (o.fg) o.gu = take(rbytes(lw[l].q_ffn_gate, d) * 2 * f);
+    else { o.gate = take(rbytes(lw[l].q_ffn_gate, d) * f); o.up = take(rbytes(lw[l].q_ffn_up, d) * f); }
+    o.down = take(rbytes(lw[l].q_ffn_down, f) * d);
+    o.an = take(4 * (size_t)d);
+    o.fn = take(4 * (size_t)d);
+  }
+  const size_t o_embd = take(rbytes(q_token_embd, d) * c.vocab_size);
+  const size_t o_onorm = take(4 * (size_t)d);
+  const size_t o_out = take(rbytes(q_output, d) * c.vocab_size);
+  m->blob_bytes = off + 256;
+  if (cudaMalloc(&m->blob, m->blob_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    merr(VTB_CUDA_ERR_OOM, "weight upload: out of device memory");
+    delete m;
+    return nullptr;
+  }
+  uint8_t* B = static_cast<uint8_t*>(m->blob);
+  cudaStream_t st = (cudaStream_t)vtb_cuda_stream(ctx);
+  bool ok = true;
+  auto up = [&](size_t o, const void* src, size_t n) {
+    ok = ok && cudaMemcpyAsync(B + o, src, n, cudaMemcpyHostToDevice, st) == cudaSuccess;
+  };
+  m->layers.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    const Off& o = offs[l];
+    DevLayer& L = m->layers[l];
+    L.q_q = lw[l].q_attn_q; L.q_k = lw[l].q_attn_k; L.q_v = lw[l].q_attn_v; L.q_o = lw[l].q_attn_o;
+    L.q_gate = lw[l].q_ffn_gate; L.q_up = lw[l].q_ffn_up; L.q_down = lw[l].q_ffn_down;
+    const size_t rq = rbytes(L.q_q, d), rk = rbytes(L.q_k, d), rv = rbytes(L.q_v, d);
+    if (o.fq) {
+      L.qkv = B + o.qkv;
+      up(o.qkv, lw[l].attn_q, rq * d);
+      up(o.qkv + rq * d, lw[l].attn_k, rk * kvd);
+      up(o.qkv + rq * d + rk * kvd, lw[l].attn_v, rv * kvd);
+      L.q = L.k = L.v = nullptr;
+    } else {
+      L.qkv = nullptr;
+      L.q = B + o.q; L.k = B + o.k; L.v = B + o.v;
+      up(o.q, lw[l].attn_q, rq * d); up(o.k, lw[l].attn_k, rk * kvd); up(o.v, lw[l].attn_v, rv * kvd);
+    }
+    L.o = B + o.o;
+    up(o.o, lw[l].attn_o, rbytes(L.q_o, d) * d);
+    const size_t rg = rbytes(L.q_gate, d), ru = rbytes(L.q_up, d);
+    if (o.fg) {
+      L.gu = B + o.gu;
+      up(o.gu, lw[l].ffn_gate, rg * f);
+      up(o.gu + rg * f, lw[l].ffn_up, ru * f);
+      L.gate = L.up = nullptr;
+    } else {
+      L.gu = nullptr;
+      L.gate = B + o.gate; L.up = B + o.up;
+      up(o.gate, lw[l].ffn_gate, rg * f); up(o.up, lw[l].ffn_up, ru * f);
+    }
+    L.down = B + o.down;
+    up(o.down, lw[l].ffn_down, rbytes(L.q_down, f) * d);
+    L.attn_norm = reinterpret_cast<const float*>(B + o.an);
+    L.ffn_norm = reinterpret_cast<const float*>(B + o.fn);
+    up(o.an, lw[l].attn_norm, 4 * (size_t)d);
+    up(o.fn, lw[l].ffn_norm, 4 * (size_t)d);
+  }
+  m->embd = B + o_embd; m->q_embd = q_token_embd;
+  up(o_embd, token_embd, rbytes(q_token_embd, d) * c.vocab_size);
+  m->out_norm = reinterpret_cast<const float*>(B + o_onorm);
+  up(o_onorm, output_norm, 4 * (size_t)d);
+  m->out_w = B + o_out; m->q_out = q_output;
+  up(o_out, output_w, rbytes(q_output, d) * c.vocab_size);
+  ok = ok && cudaStreamSynchronize(st) == cudaSuccess;
+  if (!ok) {
+    mcuda(cudaGetLastError());
+    cudaFree(m->blob);
+    delete m;
+    return nullptr;
+  }
+  return m;
+}
+
+void vtb_cuda_model_destroy(VtbCudaModel* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  cudaFree(m->blob);
+  delete m;
+}
+
+size_t vtb_cuda_model_weight_bytes(VtbCudaModel* m) { return m ? m->blob_bytes : 0; }
+
+VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max_rows) {
+  if (!m || n_seqs <= 0 || max_rows < n_seqs || max_rows > 65535) {
+    merr(VTB_CUDA_ERR_INVALID_ARG, "bad state dimensions");
+    return nullptr;
+  }
+  cudaSetDevice(m->device);
+  const VtbCudaLlamaConfig& c = m->c;
+  VtbCudaState* s = new (std::nothrow) VtbCudaState();
+  if (!s) return nullptr;
+  s->m = m;
+  s->st = (cudaStream_t)vtb_cuda_stream(m->ctx);
+  s->n_seqs = n_seqs;
+  s->max_rows = max_rows;
+  s->nsplit = (c.max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
+  const size_t R = max_rows, d = c.dim, kvd = (size_t)c.n_kv_heads * c.head_dim, f = c.ffn_dim;
+  const size_t qkvw = d + 2 * kvd;
+  size_t fl = R * (d + d + qkvw + d + 2 * f + f + (size_t)c.vocab_size) +
+              R * c.n_heads * (size_t)s->nsplit * (c.head_dim + 2);
+  const size_t kvn = (size_t)n_seqs * c.n_layers * c.max_seq * kvd;
+  float* base = nullptr;
+  int32_t* ib = nullptr;
+  if (cudaMalloc(&base, (fl + 2 * kvn) * 4 + 64) != cudaSuccess || cudaMalloc(&ib, 4 * R * 4) != cudaSuccess ||
+      cudaMallocHost(&s->hbuf, 3 * R * 4) != cudaSuccess || cudaMallocHost(&s->hamax, R * 4) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(base);
+    cudaFree(ib);
+    merr(VTB_CUDA_ERR_OOM, "state: out of memory (KV cache)");
+    delete s;
+    return nullptr;
+  }
+  float* p = base;
+  auto carve = [&](size_t n) { float* r = p; p += (n + 3) & ~size_t(3); return r; };
+  s->x = carve(R * d); s->xb = carve(R * d); s->qkv = carve(R * qkvw); s->att = carve(R * d);
+  s->gu = carve(R * 2 * f); s->h = carve(R * f); s->logits = carve(R * c.vocab_size);
+  s->part = carve(R * c.n_heads * (size_t)s->nsplit * (c.head_dim + 2));
+  s->kc = carve(kvn); s->vc = carve(kvn);
+  s->tok = ib; s->seq = ib + R; s->pos = ib + 2 * R; s->amax = ib + 3 * R;
+  cudaMemsetAsync(s->kc, 0, 2 * kvn * 4, s->st);
+  s->seq_pos.assign(n_seqs, 0);
+  if (cudaStreamSynchronize(s->st) != cudaSuccess) {
+    mcuda(cudaGetLastError());
+    return nullptr;
+  }
+  return s;
+}
+
+void vtb_cuda_state_destroy(VtbCudaState* s) {
+  if (!s) return;
+  cudaSetDevice(s->m->device);
+  cudaStreamSynchronize(s->st);
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  cudaFree(s->x);
+  cudaFree(s->tok);
+  cudaFreeHost(s->hbuf);
+  cudaFreeHost(s->hamax);
+  delete s;
+}
+
+int vtb_cuda_state_reset(VtbCudaState* s) {
+  if (!s) return merr(VTB_CUDA_ERR_INVALID_ARG, "null state");
+  for (auto& p : s->seq_pos) p = 0;
+  return VTB_CUDA_OK;
+}
+
+int64_t vtb_cuda_state_pos(VtbCudaState* s, int32_t seq) {
+  if (!s || seq < 0 || seq >= s->n_seqs) return -1;
+  return s->seq_pos[seq];
+}
+
+}  // extern "C"
+
+// Stage the rows of a step (token, sequence, position) and embed them
+// (gatherEmbedding, forward.zig:163).  Checks mirror stepWithBackend's
+// (forward.zig:159-160) and prefillCpu's (prefill.zig:123-127).
+static int stage_rows(VtbCudaState* s, int rows, const int32_t* tok, const int32_t* seq, const int32_t* pos) {
+  const VtbCudaLlamaConfig& c = s->m->c;
+  if (rows <= 0 || rows > s->max_rows) return merr(VTB_CUDA_ERR_INVALID_ARG, "too many rows for this state");
+  for (int r = 0; r < rows; ++r) {
+    if (tok[r] < 0 || tok[r] >= c.vocab_size) return merr(VTB_CUDA_ERR_INVALID_ARG, "token id out of range");
+    if (pos[r] >= c.max_seq) return merr(VTB_CUDA_ERR_STREAM_ABORTED, "KV cache full");
+    s->hbuf[r] = tok[r];
+    s->hbuf[s->max_rows + r] = seq[r];
+    s->hbuf[2 * s->max_rows + r] = pos[r];
+  }
+  s->rows = rows;
+  return VTB_CUDA_OK;
+}
+
+static cudaError_t enqueue_embed(VtbCudaState* s) {
+  const int R = s->max_rows;
+  cudaError_t e = cudaMemcpyAsync(s->tok, s->hbuf, 3 * R * 4, cudaMemcpyHostToDevice, s->st);
+  if (e != cudaSuccess) return e;
+  return launch_embed(s->m->q_embd, s->m->embd, s->tok, s->x, s->m->c.dim, s->rows, s->st);
+}
+
+template <typename K, typename... A>
+static cudaError_t pdl_launch(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// One transformer block for the staged rows (cpuLayerStep, forward.zig:230-288).
+static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
+  VtbCudaModel* m = s->m;
+  const VtbCudaLlamaConfig& c = m->c;
+  const DevLayer& L = m->layers[l];
+  const int R = s->rows, d = c.dim, kvd = c.n_kv_heads * c.head_dim, f = c.ffn_dim, qkvw = d + 2 * kvd;
+  const int hd = c.head_dim, G = c.n_heads / c.n_kv_heads;
+  cudaStream_t st = s->st;
+  cudaError_t e;
+  RowInfo ri{s->seq, s->pos};
+  if ((e = pdl_launch(rmsnorm_kernel, dim3(R), dim3(256), 0, st, s->x, (const float*)nullptr, L.attn_norm, s->xb, d,
+                      c.rms_eps)))
+    return e;
+  for (int r = 0; r < R; ++r) {
+    const float* xr = s->xb + (size_t)r * d;
+    float* o = s->qkv + (size_t)r * qkvw;
+    if (L.qkv) {
+      if ((e = gemv_any(L.q_q, L.qkv, xr, o, qkvw, d, st, 0))) return e;
+    } else {
+      if ((e = gemv_any(L.q_q, L.q, xr, o, d, d, st, 0))) return e;
+      if ((e = gemv_any(L.q_k, L.k, xr, o + d, kvd, d, st, 0))) return e;
+      if ((e = gemv_any(L.q_v, L.v, xr, o + d + kvd, kvd, d, st, 0))) return e;
+    }
+  }
+  if ((e = pdl_launch(rope_kv_kernel, dim3(R), dim3(256), 0, st, s->qkv, s->kc, s->vc, ri, l, c.n_layers, c.max_seq,
+                      c.n_heads, c.n_kv_heads, hd, c.rope_base)))
+    return e;
+  const size_t asmem = (size_t)G * (hd + ATT_CHUNK) * 4;
+  if ((e = pdl_launch(attn_partial_kernel, dim3(c.n_kv_heads, R, s->nsplit), dim3(ATT_THREADS), asmem, st,
+                      (const float*)s->qkv, (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq,
+                      c.n_heads, c.n_kv_heads, hd, s->part, s->nsplit)))
+    return e;
+  if ((e = pdl_launch(attn_combine_kernel, dim3(c.n_heads, R), dim3(128), 0, st, (const float*)s->part, s->att,
+                      c.n_heads, hd, s->nsplit)))
+    return e;
+  for (int r = 0; r < R; ++r)  // x += W_o . att  (addInto fused as accumulate)
+    if ((e = gemv_any(L.q_o, L.o, s->att + (size_t)r * d, s->x + (size_t)r * d, d, d, st, 1))) return e;
+  if ((e = pdl_launch(rmsnorm_kernel, dim3(R), dim3(256), 0, st, s->x, (const float*)nullptr, L.ffn_norm, s->xb, d,
+                      c.rms_eps)))
+    return e;
+  for (int r = 0; r < R; ++r) {
+    const float* xr = s->xb + (size_t)r * d;
+    float* o = s->gu + (size_t)r * 2 * f;
+    if (L.gu) {
+      if ((e = gemv_any(L.q_gate, L.gu, xr, o, 2 * f, d, st, 0))) return e;
+    } else {
+      if ((e = gemv_any(L.q_gate, L.gate, xr, o, f, d, st, 0))) return e;
+      if ((e = gemv_any(L.q_up, L.up, xr, o + f, f, d, st, 0))) return e;
+    }
+  }
+  if ((e = pdl_launch(swiglu_kernel, dim3(min(1184, (R * f + 255) / 256)), dim3(256), 0, st, (const float*)s->gu, s->h,
+                      f, R)))
+    return e;
+  for (int r = 0; r < R; ++r)
+    if ((e = gemv_any(L.q_down, L.down, s->h + (size_t)r * f, s->x + (size_t)r * d, d, f, st, 1))) return e;
+  return cudaSuccess;
+}
+
+// Final RMSNorm + LM head (backend_cpu.zig finalStep :88-106) and argmax.
+// `last_only`: prefill computes logits for its last row only (prefill.zig:141-146).
+static cudaError_t enqueue_final(VtbCudaState* s, bool last_only) {
+  VtbCudaModel* m = s->m;
+  const VtbCudaLlamaConfig& c = m->c;
+  cudaStream_t st = s->st;
+  cudaError_t e;
+  const int r0 = last_only ? s->rows - 1 : 0, n = last_only ? 1 : s->rows;
+  if ((e = pdl_launch(rmsnorm_kernel, dim3(n), dim3(256), 0, st, s->x + (size_t)r0 * c.dim, (const float*)nullptr,
+                      m->out_norm, s->xb, c.dim, c.rms_eps)))
+    return e;
+  for (int r = 0; r < n; ++r)
+    if ((e = gemv_any(m->q_out, m->out_w, s->xb + (size_t)r * c.dim, s->logits + (size_t)r * c.vocab_size,
+                      c.vocab_size, c.dim, st, 0)))
+      return e;
+  argmax_kernel<<<n, 1024, 0, st>>>(s->logits, s->amax, c.vocab_size);
+  return cudaGetLastError();
+}
+
+static int finalize(VtbCudaState* s, int n, float* logits, int32_t* argmax) {
+  const VtbCudaLlamaConfig& c = s->m->c;
+  cudaError_t e = cudaSuccess;
+  if (argmax) e = cudaMemcpyAsync(s->hamax, s->amax, n * 4, cudaMemcpyDeviceToHost, s->st);
+  if (e == cudaSuccess && logits)
+    e = cudaMemcpyAsync(logits, s->logits, (size_t)n * c.vocab_size * 4, cudaMemcpyDeviceToHost, s->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
+  if (e != cudaSuccess) return mcuda(e);
+  if (argmax) memcpy(argmax, s->hamax, n * 4);
+  return VTB_CUDA_OK;
+}
+
+extern "C" {
+
+// ---- the backend vtable, one call per slot (backend.zig:67-97) ----
+
+int vtb_cuda_begin_token(VtbCudaState* s, const int32_t* tokens) {
+  if (!s || !tokens) return merr(VTB_CUDA_ERR_INVALID_ARG, "null argument");
+  cudaSetDevice(s->m->device);
+  std::vector<int32_t> seq(s->n_seqs), pos(s->n_seqs);
+  for (int i = 0; i < s->n_seqs; ++i) { seq[i] = i; pos[i] = (int32_t)s->seq_pos[i]; }
+  int rc = stage_rows(s, s->n_seqs, tokens, seq.data(), pos.data());
+  if (rc) return rc;
+  return mcuda(enqueue_embed(s));
+}
+
+int vtb_cuda_layer_step(VtbCudaState* s, int32_t layer) {
+  if (!s || layer < 0 || layer >= s->m->c.n_layers || s->rows <= 0)
+    return merr(VTB_CUDA_ERR_INVALID_ARG, "bad layer step");
+  return mcuda(enqueue_layer(s, layer));
+}
+
+int vtb_cuda_final_step(VtbCudaState* s) {
+  if (!s || s->rows <= 0) return merr(VTB_CUDA_ERR_INVALID_ARG, "no token staged");
+  return mcuda(enqueue_final(s, false));
+}
+
+int vtb_cuda_finalize_token(VtbCudaState* s, float* logits, int32_t* argmax) {
+  if (!s || s->rows <= 0) return merr(VTB_CUDA_ERR_INVALID_ARG, "no token staged");
+  const int n = s->rows;
+  int rc = finalize(s, n, logits, argmax);
+  if (rc == VTB_CUDA_OK)  // cache.advance (forward.zig:168)
+    for (int i = 0; i < s->n_seqs; ++i) s->seq_pos[i] += 1;
+  s->rows = 0;
+  return rc;
+}
+
+// Whole decode step (stepWithBackend, forward.zig:152-172) as one CUDA graph
+// per state: the graph reads tokens and positions from pinned host staging,
+// so it is captured once and replayed every token.
+int vtb_cuda_step(VtbCudaState* s, const int32_t* tokens, float* logits, int32_t* argmax) {
+  if (!s || !tokens) return merr(VTB_CUDA_ERR_INVALID_ARG, "null argument");
+  cudaSetDevice(s->m->device);
+  std::vector<int32_t> seq(s->n_seqs), pos(s->n_seqs);
+  for (int i = 0; i < s->n_seqs; ++i) { seq[i] = i; pos[i] = (int32_t)s->seq_pos[i]; }
+  int rc = stage_rows(s, s->n_seqs, tokens, seq.data(), pos.data());
+  if (rc) return rc;
+  if (!s->graph || s->graph_rows != s->rows) {
+    if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+    // Warm the kernels' one-time attribute setup outside of capture.
+    cudaError_t e = enqueue_embed(s);
+    for (int l = 0; l < s->m->c.n_layers && e == cudaSuccess; ++l) e = enqueue_layer(s, l);
+    if (e == cudaSuccess) e = enqueue_final(s, false);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
+    // The warm-up wrote this token's K/V; the replay below rewrites the same slots.
+    cudaGraph_t g;
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      cudaError_t ee = enqueue_embed(s);
+      for (int l = 0; l < s->m->c.n_layers && ee == cudaSuccess; ++l) ee = enqueue_layer(s, l);
+      if (ee == cudaSuccess) ee = enqueue_final(s, false);
+      e = cudaStreamEndCapture(s->st, &g);
+      if (ee != cudaSuccess) e = ee;
+    }
+    if (e == cudaSuccess) {
+      e = cudaGraphInstantiate(&s->graph, g, 0);
+      cudaGraphDestroy(g);
+    }
+    if (e != cudaSuccess) return mcuda(e);
+    s->graph_rows = s->rows;
+  }
+  cudaError_t e = cudaGraphLaunch(s->graph, s->st);
+  if (e != cudaSuccess) return mcuda(e);
+  return vtb_cuda_finalize_token(s, logits, argmax);
+}
+
+// Batched prompt prefill of sequence `seq` (prefillCpu, prefill.zig:111-147):
+// all n tokens go through each layer together; logits of the last token.
+int vtb_cuda_prefill(VtbCudaState* s, int32_t seq, const int32_t* tokens, int32_t n, float* logits, int32_t* argmax) {
+  if (!s || !tokens || seq < 0 || seq >= s->n_seqs) return merr(VTB_CUDA_ERR_INVALID_ARG, "bad prefill arguments");
+  if (n == 0) return VTB_CUDA_OK;
+  const VtbCudaLlamaConfig& c = s->m->c;
+  if (s->seq_pos[seq] + n > c.max_seq) return merr(VTB_CUDA_ERR_STREAM_ABORTED, "KV cache full");
+  cudaSetDevice(s->m->device);
+  int done = 0;
+  while (done < n) {  // chunks of max_rows tokens
+    const int rows = min(n - done, s->max_rows);
+    std::vector<int32_t> sq(rows, seq), pos(rows);
+    for (int r = 0; r < rows; ++r) pos[r] = (int32_t)(s->seq_pos[seq] + r);
+    int rc = stage_rows(s, rows, tokens + done, sq.data(), pos.data());
+    if (rc) return rc;
+    cudaError_t e = enqueue_embed(s);
+    for (int l = 0; l < c.n_layers && e == cudaSuccess; ++l) e = enqueue_layer(s, l);
+    const bool last = done + rows == n;
+    if (e == cudaSuccess && last) e = enqueue_final(s, true);
+    if (e != cudaSuccess) return mcuda(e);
+    s->seq_pos[seq] += rows;
+    done += rows;
+    if (last) {
+      s->rows = 1;
+      rc = finalize(s, 1, logits, argmax);
+      s->rows = 0;
+      return rc;
+    }
+  }
+  return VTB_CUDA_OK;
+}
+
+}  // extern "C"

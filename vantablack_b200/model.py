@@ -1,0 +1,227 @@
+"""Host side of the Llama forward loop: configs, seeded random-init GGUF-style
+weights, and the CUDA model/state handles behind the C ABI.
+
+Names follow the reference: ``LlamaConfig`` (src/runtime/model.zig:40-149),
+``LayerWeights`` (:172-189), ``step`` (forward.zig:119-172), ``prefill``
+(prefill.zig:111-147).  Weights live on the host as numpy arrays standing in
+for the GGUF mmap and are uploaded once by ``vtb_cuda_model_create``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, replace
+
+import numpy as np
+
+from . import _lib
+from .synth import Q4_K, Q6_K, activations, norm_weight, quant_tensor  # noqa: F401
+
+MATS = ("attn_q", "attn_k", "attn_v", "attn_o", "ffn_gate", "ffn_up", "ffn_down")
+
+
+@dataclass(frozen=True)
+class LlamaConfig:
+    dim: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn_dim: int
+    vocab_size: int
+    max_seq: int
+    rope_base: float = 10000.0
+    rms_eps: float = 1e-5
+
+    def with_(self, **kw) -> "LlamaConfig":
+        return replace(self, **kw)
+
+
+# TinyLlama-1.1B architecture.
+TINYLLAMA = LlamaConfig(dim=2048, n_layers=22, n_heads=32, n_kv_heads=4, head_dim=64, ffn_dim=5632,
+                        vocab_size=32000, max_seq=2048, rope_base=10000.0)
+# Llama-3-8B architecture (context 2048 prefill + 512 decode).
+LLAMA3_8B = LlamaConfig(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336,
+                        vocab_size=128256, max_seq=2560, rope_base=500000.0)
+
+# Q4_K_M-style layout of both configs: ffn_down and output Q6_K, the rest Q4_K.
+DEFAULT_QUANTS = {"attn_q": Q4_K, "attn_k": Q4_K, "attn_v": Q4_K, "attn_o": Q4_K, "ffn_gate": Q4_K,
+                  "ffn_up": Q4_K, "ffn_down": Q6_K, "token_embd": Q4_K, "output": Q6_K}
+
+
+class HostWeights:
+    """Seeded random-init weights of a Llama config (numpy, host memory)."""
+
+    def __init__(self, cfg: LlamaConfig, seed: int = 0, quants: dict | None = None):
+        q = dict(DEFAULT_QUANTS, **(quants or {}))
+        rng = np.random.default_rng(seed)
+        d, kvd, f = cfg.dim, cfg.n_kv_heads * cfg.head_dim, cfg.ffn_dim
+        shapes = {"attn_q": (d, d), "attn_k": (kvd, d), "attn_v": (kvd, d), "attn_o": (d, d),
+                  "ffn_gate": (f, d), "ffn_up": (f, d), "ffn_down": (d, f)}
+        self.cfg = cfg
+        self.layers = []
+        for _ in range(cfg.n_layers):
+            lw = {n: (q[n], quant_tensor(rng, q[n], *shapes[n])) for n in MATS}
+            lw["attn_norm"] = norm_weight(rng, d)
+            lw["ffn_norm"] = norm_weight(rng, d)
+            self.layers.append(lw)
+        self.token_embd = (q["token_embd"], quant_tensor(rng, q["token_embd"], cfg.vocab_size, d))
+        self.output_norm = norm_weight(rng, d)
+        self.output = (q["output"], quant_tensor(rng, q["output"], cfg.vocab_size, d))
+
+    def nbytes(self) -> int:
+        n = sum(a.nbytes for lw in self.layers for k, v in lw.items() for a in ([v[1]] if k in MATS else [v]))
+        return n + self.token_embd[1].nbytes + self.output[1].nbytes + self.output_norm.nbytes
+
+
+class _CConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in
+                ("dim", "n_layers", "n_heads", "n_kv_heads", "head_dim", "ffn_dim", "vocab_size", "max_seq")] + \
+               [("rope_base", C.c_float), ("rms_eps", C.c_float)]
+
+
+class _CLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in MATS] + [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p)] + \
+               [("q_" + n, C.c_int32) for n in MATS]
+
+
+_vp = C.c_void_p
+
+
+def _lib_loaded():
+    return _lib.load()
+
+
+def _ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+class Context:
+    """A device context (vtb_cuda_init): one stream on one GPU."""
+
+    def __init__(self, device: int = 0):
+        self.lib = _lib_loaded()
+        self.h = self.lib.vtb_cuda_init(device)
+        if not self.h:
+            raise _lib.VtbError(-5, "vtb_cuda_init")
+        self.device = device
+
+    def close(self):
+        if self.h:
+            self.lib.vtb_cuda_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CudaModel:
+    """Weights resident in HBM (vtb_cuda_model_create)."""
+
+    def __init__(self, ctx: Context, w: HostWeights):
+        self.ctx, self.cfg, self.lib = ctx, w.cfg, ctx.lib
+        c = w.cfg
+        cc = _CConfig(c.dim, c.n_layers, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn_dim, c.vocab_size, c.max_seq,
+                      c.rope_base, c.rms_eps)
+        layers = (_CLayer * c.n_layers)()
+        for i, lw in enumerate(w.layers):
+            L = layers[i]
+            for n in MATS:
+                q, arr = lw[n]
+                setattr(L, n, _ptr(arr))
+                setattr(L, "q_" + n, q)
+            L.attn_norm = _ptr(lw["attn_norm"])
+            L.ffn_norm = _ptr(lw["ffn_norm"])
+        qe, emb = w.token_embd
+        qo, out = w.output
+        self.h = self.lib.vtb_cuda_model_create(ctx.h, C.byref(cc), C.cast(layers, _vp), _ptr(emb), qe,
+                                                _ptr(w.output_norm), _ptr(out), qo)
+        if not self.h:
+            raise _lib.VtbError(-1, "vtb_cuda_model_create")
+
+    @property
+    def weight_bytes(self) -> int:
+        return self.lib.vtb_cuda_model_weight_bytes(self.h)
+
+    def close(self):
+        if self.h:
+            self.lib.vtb_cuda_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CudaState:
+    """KV cache + scratch for n_seqs sequences (vtb_cuda_state_create)."""
+
+    def __init__(self, model: CudaModel, n_seqs: int = 1, max_rows: int = 256):
+        self.model, self.lib, self.cfg = model, model.lib, model.cfg
+        self.n_seqs = n_seqs
+        self.h = self.lib.vtb_cuda_state_create(model.h, n_seqs, max(max_rows, n_seqs))
+        if not self.h:
+            raise _lib.VtbError(-4, "vtb_cuda_state_create")
+
+    def close(self):
+        if self.h:
+            self.lib.vtb_cuda_state_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        _lib.check(self.lib.vtb_cuda_state_reset(self.h), "reset")
+
+    def pos(self, seq: int = 0) -> int:
+        return self.lib.vtb_cuda_state_pos(self.h, seq)
+
+    def step(self, tokens, want_logits: bool = True, graph: bool = True):
+        """One token per sequence; returns (logits [n_seqs, vocab] or None, argmax [n_seqs])."""
+        t = np.ascontiguousarray(np.atleast_1d(tokens), np.int32)
+        assert t.size == self.n_seqs
+        am = np.empty(self.n_seqs, np.int32)
+        lg = np.empty((self.n_seqs, self.cfg.vocab_size), np.float32) if want_logits else None
+        lp = _ptr(lg) if want_logits else None
+        if graph:
+            _lib.check(self.lib.vtb_cuda_step(self.h, _ptr(t), lp, _ptr(am)), "vtb_cuda_step")
+        else:  # the vtable slot by slot
+            _lib.check(self.lib.vtb_cuda_begin_token(self.h, _ptr(t)), "begin_token")
+            for layer in range(self.cfg.n_layers):
+                _lib.check(self.lib.vtb_cuda_layer_step(self.h, layer), "layer_step")
+            _lib.check(self.lib.vtb_cuda_final_step(self.h), "final_step")
+            _lib.check(self.lib.vtb_cuda_finalize_token(self.h, lp, _ptr(am)), "finalize_token")
+        return lg, am
+
+    def prefill(self, tokens, seq: int = 0, want_logits: bool = True):
+        t = np.ascontiguousarray(tokens, np.int32)
+        am = np.empty(1, np.int32)
+        lg = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
+        _lib.check(self.lib.vtb_cuda_prefill(self.h, seq, _ptr(t), t.size, _ptr(lg) if want_logits else None,
+                                             _ptr(am)), "vtb_cuda_prefill")
+        return lg, int(am[0])
+
+    def generate_greedy(self, prompt, n_gen: int, use_prefill: bool = True):
+        """Prompt then greedy decode of one sequence (n_seqs == 1)."""
+        assert self.n_seqs == 1
+        if use_prefill:
+            logits, nxt = self.prefill(prompt)
+        else:
+            for tok in prompt:
+                lg, am = self.step([int(tok)])
+            logits, nxt = lg[0], int(am[0])
+        out = []
+        for _ in range(n_gen):
+            out.append(nxt)
+            lg, am = self.step([nxt])
+            logits, nxt = lg[0], int(am[0])
+        return out, logits
