@@ -105,6 +105,21 @@ int vtb_cuda_q8_0_block_dots(const void *w, const int8_t *xq, int32_t *dots, int
 int vtb_cuda_gemv_q8_0_q8_0(const void *w, const float *x, float *y, int64_t m, int64_t k,
                             int8_t *xq_scratch, float *dx_scratch, void *stream, int pdl);
 
+/* Allocation-free Q8_0 x Q8_0 GEMV.  No counterpart in the reference: it is
+ * for hosts that cannot call cudaMalloc on their decode path (a fixed device
+ * memory budget reserved up front, or a warm serving loop that forbids
+ * allocation).  Same result as vtb_cuda_gemv_q8_0_q8_0, but the activation
+ * scratch lives in a fixed array inside the library (72 KiB per GPU that
+ * loads it, held until exit), so k must be <= VTB_CUDA_NOALLOC_MAX_K; larger
+ * k is rejected with VTB_CUDA_ERR_INVALID_ARG.  The first call on a device
+ * resolves the array's address on the current device; make that first call
+ * before any stream capture.  All calls share the one array: calls that can
+ * overlap on the GPU (other streams, other host threads) race and must be
+ * serialized by the caller.  Allocates nothing. */
+#define VTB_CUDA_NOALLOC_MAX_K 65536
+int vtb_cuda_gemv_q8_0_q8_0_noalloc(const void *w, const float *x, float *y, int64_t m, int64_t k,
+                                    void *stream, int pdl);
+
 /* ------------------------------------------------------------------ */
 /* Context / buffers (mirrors the Metal bridge, bridge.h:25-46)         */
 /* ------------------------------------------------------------------ */

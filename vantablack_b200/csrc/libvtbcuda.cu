@@ -6,3 +6,4 @@
 #include "quant_aux.cu"
 #include "api.cu"
 #include "model.cu"
+#include "noalloc.cu"
