@@ -105,6 +105,18 @@ int vtb_cuda_q8_0_block_dots(const void *w, const int8_t *xq, int32_t *dots, int
 int vtb_cuda_gemv_q8_0_q8_0(const void *w, const float *x, float *y, int64_t m, int64_t k,
                             int8_t *xq_scratch, float *dx_scratch, void *stream, int pdl);
 
+/* Prefill GEMM: out[b, i] = sum_j W[i, j] * acts[b, j] for n_tokens rows of
+ * f32 activations (acts [n_tokens][k], out [n_tokens][m]) -- matmulBatched
+ * (src/runtime/prefill.zig:325-378).  Runs on the tcgen05 tensor cores with
+ * W dequantized (bit-exactly) to bf16 tiles in shared memory.  precise = 0:
+ * bf16 operands (tolerance 2e-2); precise = 1: hi/lo-split operands, three
+ * MMAs per tile (~16-bit products, fp32-class results).  k % 64 == 0.
+ * `workspace` (device, 16-byte aligned) holds the converted activations:
+ * vtb_cuda_gemm_workspace_bytes(k, n_tokens, precise) bytes. */
+size_t vtb_cuda_gemm_workspace_bytes(int64_t k, int64_t n_tokens, int precise);
+int vtb_cuda_gemm(int quant, const void *w, const float *acts, float *out, int64_t m, int64_t k,
+                  int64_t n_tokens, int precise, void *workspace, size_t workspace_bytes, void *stream);
+
 /* Allocation-free Q8_0 x Q8_0 GEMV.  No counterpart in the reference: it is
  * for hosts that cannot call cudaMalloc on their decode path (a fixed device
  * memory budget reserved up front, or a warm serving loop that forbids

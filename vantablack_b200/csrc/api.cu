@@ -21,6 +21,8 @@ cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* ou
                          cudaStream_t st);
 cudaError_t launch_quantize_q8_0(const float* x, int8_t* qs, float* d, int nblocks, cudaStream_t st);
 cudaError_t launch_q8_0_block_dots(const void* w, const int8_t* xq, int32_t* dots, int m, int nb, cudaStream_t st);
+cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
+                           void* ws, cudaStream_t st);
 }  // namespace vtb
 
 using namespace vtb;
@@ -101,6 +103,7 @@ int vtb_cuda_check_device_error(void) {
 }
 
 int vtb_cuda_gemv(int quant, const void* w, const float* x, float* y, int64_t m, int64_t k, void* stream, int pdl) {
+  cudaGetLastError();  // drop a stale error left by an unrelated earlier call
   int rc = check_mat(quant, w, m, k);
   if (rc) return rc;
   if (!x || !y) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null x or y");
@@ -111,6 +114,7 @@ int vtb_cuda_gemv(int quant, const void* w, const float* x, float* y, int64_t m,
 }
 
 int vtb_cuda_dequant(int quant, const void* w, float* out, int64_t n, void* stream) {
+  cudaGetLastError();
   if (!host_quant_ok(quant)) return set_err(VTB_CUDA_ERR_UNSUPPORTED, "unsupported quant type");
   if (!w || !out || n < 0 || n % host_block_elems(quant))
     return set_err(VTB_CUDA_ERR_INVALID_ARG, "bad dequant arguments");
@@ -120,6 +124,7 @@ int vtb_cuda_dequant(int quant, const void* w, float* out, int64_t n, void* stre
 
 int vtb_cuda_embed(int quant, const void* table, const int32_t* ids, float* out, int64_t dim, int64_t n_tokens,
                    void* stream) {
+  cudaGetLastError();
   if (!host_quant_ok(quant)) return set_err(VTB_CUDA_ERR_UNSUPPORTED, "unsupported quant type");
   if (!table || !ids || !out || dim <= 0 || dim % host_block_elems(quant) || n_tokens < 0 || n_tokens > 65535)
     return set_err(VTB_CUDA_ERR_INVALID_ARG, "bad embed arguments");
@@ -128,12 +133,14 @@ int vtb_cuda_embed(int quant, const void* table, const int32_t* ids, float* out,
 }
 
 int vtb_cuda_quantize_q8_0(const float* x, int64_t k, int8_t* qs, float* d, void* stream) {
+  cudaGetLastError();
   if (!x || !qs || !d || k <= 0 || k % 32 || k > INT_MAX)
     return set_err(VTB_CUDA_ERR_INVALID_ARG, "bad quantize arguments");
   return cuda_status(launch_quantize_q8_0(x, qs, d, (int)(k / 32), (cudaStream_t)stream));
 }
 
 int vtb_cuda_q8_0_block_dots(const void* w, const int8_t* xq, int32_t* dots, int64_t m, int64_t k, void* stream) {
+  cudaGetLastError();
   int rc = check_mat(Q8_0, w, m, k);
   if (rc) return rc;
   if (!xq || !dots || (reinterpret_cast<uintptr_t>(xq) & 3u))
@@ -143,6 +150,7 @@ int vtb_cuda_q8_0_block_dots(const void* w, const int8_t* xq, int32_t* dots, int
 
 int vtb_cuda_gemv_q8_0_q8_0(const void* w, const float* x, float* y, int64_t m, int64_t k, int8_t* xq_scratch,
                             float* dx_scratch, void* stream, int pdl) {
+  cudaGetLastError();
   int rc = check_mat(Q8_0, w, m, k);
   if (rc) return rc;
   if (!x || !y || !xq_scratch || !dx_scratch) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null pointer");
@@ -151,6 +159,26 @@ int vtb_cuda_gemv_q8_0_q8_0(const void* w, const float* x, float* y, int64_t m, 
   cudaError_t e = launch_quantize_q8_0(x, xq_scratch, dx_scratch, (int)(k / 32), st);
   if (e != cudaSuccess) return cuda_status(e);
   return cuda_status(launch_gemv_q8_0_q8_0(w, xq_scratch, dx_scratch, y, (int)m, (int)k, st, pdl != 0));
+}
+
+size_t vtb_cuda_gemm_workspace_bytes(int64_t k, int64_t n_tokens, int precise) {
+  if (k <= 0 || n_tokens <= 0) return 0;
+  return (size_t)(k * n_tokens * 2 * (precise ? 2 : 1));
+}
+
+int vtb_cuda_gemm(int quant, const void* w, const float* acts, float* out, int64_t m, int64_t k, int64_t n_tokens,
+                  int precise, void* workspace, size_t workspace_bytes, void* stream) {
+  cudaGetLastError();
+  int rc = check_mat(quant, w, m, k);
+  if (rc) return rc;
+  if (k % 64) return set_err(VTB_CUDA_ERR_INVALID_ARG, "gemm needs k to be a multiple of 64");
+  if (!acts || !out || !workspace || n_tokens <= 0 || n_tokens > 65535 * 64)
+    return set_err(VTB_CUDA_ERR_INVALID_ARG, "bad gemm arguments");
+  if (workspace_bytes < vtb_cuda_gemm_workspace_bytes(k, n_tokens, precise))
+    return set_err(VTB_CUDA_ERR_INVALID_ARG, "gemm workspace too small");
+  if (!aligned16(acts) || !aligned16(workspace)) return set_err(VTB_CUDA_ERR_INVALID_ARG, "acts/workspace not 16-byte aligned");
+  return cuda_status(launch_gemm_tc(quant, w, acts, out, (int)m, (int)k, (int)n_tokens, precise != 0, workspace,
+                                    (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -7,6 +7,7 @@
 //   Q6_K 210 B / 256        : u8 ql[128] | u8 qh[64] | i8 sc[16] | f16 d
 #pragma once
 #include <cstdint>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -29,6 +30,10 @@ inline int64_t host_row_bytes(int q, int64_t k) {
     case Q6_K: return (k / 256) * 210;
     default: return -1;
   }
+}
+template <int Q>
+__host__ __device__ __forceinline__ long long host_row_bytes_dev(long long k) {
+  return (k / Fmt<Q>::elems) * Fmt<Q>::bytes;
 }
 inline int host_block_elems(int q) { return q == Q8_0 ? 32 : (q == F32 ? 1 : 256); }
 inline bool host_quant_ok(int q) { return q == Q8_0 || q == Q4_K || q == Q5_K || q == Q6_K; }

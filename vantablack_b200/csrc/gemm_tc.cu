@@ -1,0 +1,392 @@
+// gemm_tc.cu -- prefill GEMM on the 5th-generation tensor cores:
+// out[b, m] = sum_k W[m, k] * acts[b, k] for GGUF-quantized W (Q4_K, Q5_K,
+// Q6_K, Q8_0) and f32 activations -- the reference's matmulBatched
+// (src/runtime/prefill.zig:325-378: dequantize a row once, then B dot_f32).
+//
+// Per CTA: a 128-row weight tile x BN-token tile, the full K range.
+//  * Warps 0-3 (producers): thread t dequantizes row t of the tile, 64 weights
+//    per k-block, with the reference's exact f32 formula (bit-identical to
+//    dequantToF32), converts to bf16 and stores into a 128-byte-swizzled
+//    K-major shared tile (the UMMA SWIZZLE_128B canonical layout: 8-row atoms
+//    of 1024 B, 16-byte chunk c of row r at chunk c ^ (r % 8)).  The same
+//    threads copy the bf16 activation tile with cp.async into the same layout.
+//  * Warp 4, one elected thread: tcgen05.mma.cta_group::1.kind::f16 (bf16 x
+//    bf16 -> f32), D in TMEM (BN columns), 4 MMAs of K=16 per k-block;
+//    tcgen05.commit releases each stage back to the producers.
+//  * Epilogue (warps 0-3): tcgen05.ld 32x32b, coalesced stores of out.
+// Precision modes:
+//  * PASSES = 1: bf16 operands (the north star's 2e-2 bf16 tolerance).
+//  * PASSES = 3: both operands split into bf16 hi + lo parts and
+//    hi*hi + hi*lo + lo*hi accumulated (~16-bit products): used by the model
+//    prefill so its KV cache and logits stay within fp32-class tolerance of
+//    the reference (greedy token identity).
+// Every wait is bounded; a timeout sets the device error word, and all warps
+// still reach the TMEM dealloc.
+#include "common.cuh"
+
+namespace vtb {
+
+constexpr int TC_BM = 128, TC_BK = 64, TC_PROD = 128;
+
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                     // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;           // stride byte offset: 8-row atom pitch
+  d |= (uint64_t)1 << 46;                     // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                     // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, unsigned src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t sw128_off(int r, int chunk) {  // byte offset of 16-B chunk `chunk` of row r
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4));
+}
+
+// ---- bit-exact dequantization of 64 consecutive weights [k0, k0+64) of one row ----
+__device__ __forceinline__ uint32_t ldg_u32(const uint8_t* p) { return __ldg(reinterpret_cast<const uint32_t*>(p)); }
+// 4-byte words from a 2-byte-aligned global address
+template <int NW>
+__device__ __forceinline__ void ldg_words_a2(const uint8_t* p, uint32_t* out) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint8_t* b = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
+  const unsigned sh = (unsigned)(a & 3) * 8u;
+  uint32_t w[NW + 1];
+#pragma unroll
+  for (int i = 0; i <= NW; ++i) w[i] = ldg_u32(b + 4 * i);
+#pragma unroll
+  for (int i = 0; i < NW; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
+}
+__device__ __forceinline__ unsigned byte_of(const uint32_t* w, int i) { return (w[i >> 2] >> (8 * (i & 3))) & 0xffu; }
+
+template <int Q>
+__device__ __forceinline__ void dequant64(const uint8_t* row, int k0, float* v) {
+  if constexpr (Q == Q4_K || Q == Q5_K) {
+    constexpr int BB = Q == Q4_K ? 144 : 176;
+    const uint8_t* blk = row + (k0 >> 8) * BB;
+    const int j = (k0 & 255) >> 6;  // sub-block pair: sub-blocks 2j, 2j+1
+    const uint4 h = __ldg(reinterpret_cast<const uint4*>(blk));
+    const float d = h2f((uint16_t)(h.x & 0xffffu)), dmin = h2f((uint16_t)(h.x >> 16));
+    const uint32_t sw[3] = {h.y, h.z, h.w};
+    unsigned sc[2], mn[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {  // q4kScaleMin (simd.zig:211-219)
+      const int s = 2 * j + u;
+      if (s < 4) {
+        sc[u] = byte_of(sw, s) & 63u; mn[u] = byte_of(sw, s + 4) & 63u;
+      } else {
+        sc[u] = (byte_of(sw, s + 4) & 15u) | ((byte_of(sw, s - 4) >> 6) << 4);
+        mn[u] = (byte_of(sw, s + 4) >> 4) | ((byte_of(sw, s) >> 6) << 4);
+      }
+    }
+    const float d1 = __fmul_rn(d, (float)sc[0]), m1 = __fmul_rn(dmin, (float)mn[0]);
+    const float d2 = __fmul_rn(d, (float)sc[1]), m2 = __fmul_rn(dmin, (float)mn[1]);
+    const uint8_t* qs = blk + (Q == Q4_K ? 16 : 48) + 32 * j;
+    uint32_t q[8];
+    const uint4 qa = __ldg(reinterpret_cast<const uint4*>(qs)), qb = __ldg(reinterpret_cast<const uint4*>(qs + 16));
+    q[0] = qa.x; q[1] = qa.y; q[2] = qa.z; q[3] = qa.w; q[4] = qb.x; q[5] = qb.y; q[6] = qb.z; q[7] = qb.w;
+    uint32_t qh[8];
+    if constexpr (Q == Q5_K) {
+      const uint4 ha = __ldg(reinterpret_cast<const uint4*>(blk + 16)), hb = __ldg(reinterpret_cast<const uint4*>(blk + 32));
+      qh[0] = ha.x; qh[1] = ha.y; qh[2] = ha.z; qh[3] = ha.w; qh[4] = hb.x; qh[5] = hb.y; qh[6] = hb.z; qh[7] = hb.w;
+    }
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      unsigned lo = byte_of(q, l) & 15u, hi = byte_of(q, l) >> 4;
+      if constexpr (Q == Q5_K) {
+        lo += (byte_of(qh, l) >> (2 * j)) & 1u ? 16u : 0u;
+        hi += (byte_of(qh, l) >> (2 * j + 1)) & 1u ? 16u : 0u;
+      }
+      v[l] = __fsub_rn(__fmul_rn(d1, (float)lo), m1);
+      v[32 + l] = __fsub_rn(__fmul_rn(d2, (float)hi), m2);
+    }
+  } else if constexpr (Q == Q6_K) {
+    const uint8_t* blk = row + (k0 >> 8) * 210;
+    const int half = (k0 & 255) >> 7, nb = ((k0 & 127) >> 6) * 2;  // n in {nb, nb+1}
+    uint32_t ql[16], qh[8], sc[2];
+    ldg_words_a2<16>(blk + half * 64, ql);
+    ldg_words_a2<8>(blk + 128 + half * 32, qh);
+    ldg_words_a2<2>(blk + 192 + half * 8, sc);
+    const float d = h2f((uint16_t)(ldg_u32(reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(blk + 208) & ~uintptr_t(3))) >>
+                                   ((reinterpret_cast<uintptr_t>(blk + 208) & 3) * 8)));
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int n = nb + u;
+#pragma unroll
+      for (int l = 0; l < 32; ++l) {
+        unsigned b = byte_of(ql, (n & 1) ? l + 32 : l);
+        b = (n & 2) ? (b >> 4) : (b & 15u);
+        const int qv = (int)(b | (((byte_of(qh, l) >> (2 * n)) & 3u) << 4)) - 32;
+        const float s = (float)(int8_t)byte_of(sc, (l >> 4) + 2 * n);
+        v[32 * u + l] = __fmul_rn(__fmul_rn(d, s), (float)qv);
+      }
+    }
+  } else {  // Q8_0: two 34-byte blocks
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint8_t* blk = row + ((k0 >> 5) + u) * 34;
+      uint32_t w[9];
+      ldg_words_a2<9>(blk, w);
+      const float d = h2f((uint16_t)(w[0] & 0xffffu));
+#pragma unroll
+      for (int l = 0; l < 32; ++l) v[32 * u + l] = __fmul_rn(d, (float)(int8_t)byte_of(w, l + 2));
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Activations f32 [B][K] -> bf16 hi [B][K] (and lo = bf16(x - hi)).
+__global__ void acts_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
+                                    __nv_bfloat16* __restrict__ lo, long long n) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+template <int Q, int BN, int PASSES, int S>
+struct TcCfg {
+  static constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KiB
+  static constexpr int B_BYTES = BN * TC_BK * 2;
+  static constexpr int NOPS = PASSES == 1 ? 1 : 2;    // hi only, or hi + lo
+  static constexpr int STAGE = NOPS * (A_BYTES + B_BYTES);
+  static constexpr int SMEM = S * STAGE + 1024 /*align*/ + 256 /*barriers + tmem slot*/;
+};
+
+template <int Q, int BN, int PASSES, int S>
+__global__ void __launch_bounds__(160, 1)
+gemm_tc_kernel(const uint8_t* __restrict__ W, const __nv_bfloat16* __restrict__ xh, const __nv_bfloat16* __restrict__ xl,
+               float* __restrict__ out, int M, int K, int NB) {
+  using C = TcCfg<Q, BN, PASSES, S>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE);
+  uint64_t* empty = full + S;
+  uint64_t* done = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int m0 = blockIdx.x * TC_BM, n0 = blockIdx.y * BN;
+  const int nk = K / TC_BK;
+  const long long rb = host_row_bytes_dev<Q>(K);
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], TC_PROD);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 4) {  // TMEM: BN fp32 columns x 128 lanes
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(smem_u32(tmem_slot)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
+
+  if (warp < 4) {
+    // ---------------- producers ----------------
+    const int r = tid;  // tile row
+    const bool row_ok = m0 + r < M;
+    const uint8_t* wrow = W + (long long)(row_ok ? m0 + r : 0) * rb;
+    for (int kb = 0; kb < nk && ok; ++kb) {
+      const int s = kb % S;
+      if (kb >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((kb / S) - 1) & 1))) { ok = false; break; }
+      uint8_t* st = smem + s * C::STAGE;
+      const uint32_t a_hi = smem_u32(st), b_hi = a_hi + C::A_BYTES;
+      const uint32_t a_lo = b_hi + C::B_BYTES, b_lo = a_lo + C::A_BYTES;
+      // B tile (activations): BN rows x 8 chunks of 16 B, zero-filled past NB
+      for (int i = tid; i < BN * 8; i += TC_PROD) {
+        const int n = i >> 3, c = i & 7;
+        const bool in = n0 + n < NB;
+        const long long off = (long long)(in ? n0 + n : 0) * K + kb * TC_BK + c * 8;
+        cp_async16(b_hi + sw128_off(n, c), xh + off, in ? 16u : 0u);
+        if constexpr (PASSES == 3) cp_async16(b_lo + sw128_off(n, c), xl + off, in ? 16u : 0u);
+      }
+      // A tile: this thread's row, 64 weights
+      float v[64];
+      if (row_ok) dequant64<Q>(wrow, kb * TC_BK, v);
+      else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = 0.f;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 hv, lv;
+        float h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = __bfloat162float(__float2bfloat16_rn(v[8 * c + e]));
+        hv.x = pack_bf16(h[0], h[1]); hv.y = pack_bf16(h[2], h[3]); hv.z = pack_bf16(h[4], h[5]); hv.w = pack_bf16(h[6], h[7]);
+        *reinterpret_cast<uint4*>(st + sw128_off(r, c)) = hv;
+        if constexpr (PASSES == 3) {
+          lv.x = pack_bf16(v[8 * c + 0] - h[0], v[8 * c + 1] - h[1]);
+          lv.y = pack_bf16(v[8 * c + 2] - h[2], v[8 * c + 3] - h[3]);
+          lv.z = pack_bf16(v[8 * c + 4] - h[4], v[8 * c + 5] - h[5]);
+          lv.w = pack_bf16(v[8 * c + 6] - h[6], v[8 * c + 7] - h[7]);
+          *reinterpret_cast<uint4*>(st + C::A_BYTES + C::B_BYTES + sw128_off(r, c)) = lv;
+        }
+      }
+      cp_async_wait_all();
+      fence_async_smem();  // generic-proxy smem writes -> visible to the tensor core
+      mbar_arrive(&full[s]);
+    }
+  } else if (lane == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+    for (int kb = 0; kb < nk && ok; ++kb) {
+      const int s = kb % S;
+      if (!mbar_wait_bounded(&full[s], (unsigned)((kb / S) & 1))) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t a_hi = smem_u32(smem + s * C::STAGE), b_hi = a_hi + C::A_BYTES;
+      const uint32_t a_lo = b_hi + C::B_BYTES, b_lo = a_lo + C::A_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < TC_BK / 16; ++kk) {  // K = 16 per MMA: +32 B within the swizzled row
+        const int acc = (kb | kk) != 0;
+        mma_bf16(tmem, sw128_desc(a_hi + 32 * kk), sw128_desc(b_hi + 32 * kk), idesc, acc);
+        if constexpr (PASSES == 3) {
+          mma_bf16(tmem, sw128_desc(a_hi + 32 * kk), sw128_desc(b_lo + 32 * kk), idesc, 1);
+          mma_bf16(tmem, sw128_desc(a_lo + 32 * kk), sw128_desc(b_hi + 32 * kk), idesc, 1);
+        }
+      }
+      mma_commit(&empty[s]);
+    }
+    mma_commit(done);
+  }
+  __syncwarp();
+
+  // ---------------- epilogue (warps 0-3: TMEM lanes 32w..32w+31 = tile rows) ----------------
+  if (warp < 4) {
+    if (ok && mbar_wait_bounded(done, 0u)) {
+      tc_fence_after();
+      const int row = m0 + 32 * warp + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+              "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < M) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + c0 + j < NB) out[(long long)(n0 + c0 + j) * M + row] = __uint_as_float(v[j]);
+        }
+      }
+    }
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(BN));
+  }
+}
+
+template <int Q, int BN, int PASSES, int S>
+static cudaError_t launch_gemm_tc_t(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
+                                    int k, int nb, cudaStream_t st) {
+  using C = TcCfg<Q, BN, PASSES, S>;
+  auto kern = gemm_tc_kernel<Q, BN, PASSES, S>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((m + TC_BM - 1) / TC_BM, (nb + BN - 1) / BN);
+  cfg.blockDim = dim3(160);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute a[1];
+  a[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = a;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, xh, xl, out, m, k, nb);
+}
+
+template <int Q>
+static cudaError_t launch_gemm_tc_q(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
+                                    int k, int nb, bool precise, cudaStream_t st) {
+  if (precise) {
+    if (nb <= 64) return launch_gemm_tc_t<Q, 64, 3, 4>(w, xh, xl, out, m, k, nb, st);
+    if (nb <= 128) return launch_gemm_tc_t<Q, 128, 3, 3>(w, xh, xl, out, m, k, nb, st);
+    return launch_gemm_tc_t<Q, 256, 3, 2>(w, xh, xl, out, m, k, nb, st);
+  }
+  if (nb <= 64) return launch_gemm_tc_t<Q, 64, 1, 6>(w, xh, xl, out, m, k, nb, st);
+  if (nb <= 128) return launch_gemm_tc_t<Q, 128, 1, 4>(w, xh, xl, out, m, k, nb, st);
+  return launch_gemm_tc_t<Q, 256, 1, 4>(w, xh, xl, out, m, k, nb, st);
+}
+
+// out[nb][m] = acts[nb][k] . W^T.  `ws` is bf16 scratch of nb*k*(precise ? 2 : 1) elements.
+cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
+                           void* ws, cudaStream_t st) {
+  __nv_bfloat16* xh = static_cast<__nv_bfloat16*>(ws);
+  __nv_bfloat16* xl = precise ? xh + (size_t)nb * k : nullptr;
+  const long long n = (long long)nb * k;
+  cudaLaunchConfig_t cfg = {};
+  const long long blocks = (n + 255) / 256;
+  cfg.gridDim = dim3((unsigned)(blocks < 148LL * 16 ? blocks : 148LL * 16));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute a[1];
+  a[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = a;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, acts_to_bf16_kernel, acts, xh, xl, n);
+  if (e != cudaSuccess) return e;
+  switch (q) {
+    case Q4_K: return launch_gemm_tc_q<Q4_K>(w, xh, xl, out, m, k, nb, precise, st);
+    case Q5_K: return launch_gemm_tc_q<Q5_K>(w, xh, xl, out, m, k, nb, precise, st);
+    case Q6_K: return launch_gemm_tc_q<Q6_K>(w, xh, xl, out, m, k, nb, precise, st);
+    case Q8_0: return launch_gemm_tc_q<Q8_0>(w, xh, xl, out, m, k, nb, precise, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace vtb

@@ -4,6 +4,7 @@
 #include "gemv.cu"
 #include "gemv_mma.cu"
 #include "quant_aux.cu"
+#include "gemm_tc.cu"
 #include "api.cu"
 #include "model.cu"
 #include "noalloc.cu"

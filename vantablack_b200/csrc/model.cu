@@ -32,6 +32,20 @@ cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, 
                                 int accumulate);
 cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* out, int dim, int n_tok,
                          cudaStream_t st);
+cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
+                           void* ws, cudaStream_t st);
+
+// Prefill steps with at least this many rows run their projections as one
+// tensor-core GEMM (precise mode) instead of one GEMV per row.
+constexpr int GEMM_MIN_ROWS = 8;
+
+// x += t (addInto, math.zig:178-187) for the GEMM path's residual adds.
+__global__ void add_kernel(float* __restrict__ x, const float* __restrict__ t, long long n) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    x[i] += t[i];
+  asm volatile("griddepcontrol.launch_dependents;");
+}
 
 static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
                             int accumulate) {
@@ -307,9 +321,11 @@ struct VtbCudaModel {
 
 struct VtbCudaState {
   VtbCudaModel* m;
+  int device;  // kept here so destroy never touches the model
   cudaStream_t st;
   int n_seqs, max_rows;
-  float *x, *xb, *qkv, *att, *gu, *h, *logits, *part;
+  float *x, *xb, *qkv, *att, *gu, *h, *logits, *part, *tmp;
+  void* ws;  // GEMM activation workspace (bf16 hi + lo)
   int32_t *tok, *seq, *pos, *amax;
   float *kc, *vc;
   int32_t* hbuf;            // pinned host staging: tok | seq | pos (3 * max_rows)
@@ -483,14 +499,21 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   VtbCudaState* s = new (std::nothrow) VtbCudaState();
   if (!s) return nullptr;
   s->m = m;
-  s->st = (cudaStream_t)vtb_cuda_stream(m->ctx);
+  s->device = m->device;
+  // The state owns its stream, so it never depends on the context outliving it.
+  if (cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
+    mcuda(cudaGetLastError());
+    delete s;
+    return nullptr;
+  }
   s->n_seqs = n_seqs;
   s->max_rows = max_rows;
   s->nsplit = (c.max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
   const size_t R = max_rows, d = c.dim, kvd = (size_t)c.n_kv_heads * c.head_dim, f = c.ffn_dim;
   const size_t qkvw = d + 2 * kvd;
-  size_t fl = R * (d + d + qkvw + d + 2 * f + f + (size_t)c.vocab_size) +
-              R * c.n_heads * (size_t)s->nsplit * (c.head_dim + 2);
+  const size_t kmax = d > f ? d : f;
+  size_t fl = R * (d + d + qkvw + d + 2 * f + f + (size_t)c.vocab_size + d + kmax) +
+              R * c.n_heads * (size_t)s->nsplit * (c.head_dim + 2) + 64;
   const size_t kvn = (size_t)n_seqs * c.n_layers * c.max_seq * kvd;
   float* base = nullptr;
   int32_t* ib = nullptr;
@@ -508,6 +531,8 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   s->x = carve(R * d); s->xb = carve(R * d); s->qkv = carve(R * qkvw); s->att = carve(R * d);
   s->gu = carve(R * 2 * f); s->h = carve(R * f); s->logits = carve(R * c.vocab_size);
   s->part = carve(R * c.n_heads * (size_t)s->nsplit * (c.head_dim + 2));
+  s->tmp = carve(R * d);
+  s->ws = carve(R * kmax);  // bf16 hi + lo = 4 bytes per activation
   s->kc = carve(kvn); s->vc = carve(kvn);
   s->tok = ib; s->seq = ib + R; s->pos = ib + 2 * R; s->amax = ib + 3 * R;
   cudaMemsetAsync(s->kc, 0, 2 * kvn * 4, s->st);
@@ -521,9 +546,10 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
 
 void vtb_cuda_state_destroy(VtbCudaState* s) {
   if (!s) return;
-  cudaSetDevice(s->m->device);
+  cudaSetDevice(s->device);
   cudaStreamSynchronize(s->st);
   if (s->graph) cudaGraphExecDestroy(s->graph);
+  cudaStreamDestroy(s->st);
   cudaFree(s->x);
   cudaFree(s->tok);
   cudaFreeHost(s->hbuf);
@@ -596,16 +622,30 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   if ((e = pdl_launch(rmsnorm_kernel, dim3(R), dim3(256), 0, st, s->x, (const float*)nullptr, L.attn_norm, s->xb, d,
                       c.rms_eps)))
     return e;
-  for (int r = 0; r < R; ++r) {
-    const float* xr = s->xb + (size_t)r * d;
-    float* o = s->qkv + (size_t)r * qkvw;
-    if (L.qkv) {
-      if ((e = gemv_any(L.q_q, L.qkv, xr, o, qkvw, d, st, 0))) return e;
-    } else {
-      if ((e = gemv_any(L.q_q, L.q, xr, o, d, d, st, 0))) return e;
-      if ((e = gemv_any(L.q_k, L.k, xr, o + d, kvd, d, st, 0))) return e;
-      if ((e = gemv_any(L.q_v, L.v, xr, o + d + kvd, kvd, d, st, 0))) return e;
+  const bool gemm = R >= GEMM_MIN_ROWS;
+  auto proj = [&](int q, const uint8_t* w, const float* in, float* out, int m, int k, int ld_out, int acc) -> cudaError_t {
+    // out[r*ld_out + i] (+)= W . in[r]; GEMM rows need a dense out, so `acc` goes through tmp
+    if (gemm && k % 64 == 0 && (acc || ld_out == m)) {
+      if (acc) {
+        cudaError_t e2 = launch_gemm_tc(q, w, in, s->tmp, m, k, R, true, s->ws, st);
+        if (e2) return e2;
+        return pdl_launch(add_kernel, dim3(min(1184, (R * m + 255) / 256)), dim3(256), 0, st, out, (const float*)s->tmp,
+                          (long long)R * m);
+      }
+      return launch_gemm_tc(q, w, in, out, m, k, R, true, s->ws, st);
     }
+    for (int r = 0; r < R; ++r) {
+      cudaError_t e2 = gemv_any(q, w, in + (size_t)r * k, out + (size_t)r * ld_out, m, k, st, acc);
+      if (e2) return e2;
+    }
+    return cudaSuccess;
+  };
+  if (L.qkv) {
+    if ((e = proj(L.q_q, L.qkv, s->xb, s->qkv, qkvw, d, qkvw, 0))) return e;
+  } else {
+    if ((e = proj(L.q_q, L.q, s->xb, s->qkv, d, d, qkvw, 0))) return e;
+    if ((e = proj(L.q_k, L.k, s->xb, s->qkv + d, kvd, d, qkvw, 0))) return e;
+    if ((e = proj(L.q_v, L.v, s->xb, s->qkv + d + kvd, kvd, d, qkvw, 0))) return e;
   }
   if ((e = pdl_launch(rope_kv_kernel, dim3(R), dim3(256), 0, st, s->qkv, s->kc, s->vc, ri, l, c.n_layers, c.max_seq,
                       c.n_heads, c.n_kv_heads, hd, c.rope_base)))
@@ -618,26 +658,20 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   if ((e = pdl_launch(attn_combine_kernel, dim3(c.n_heads, R), dim3(128), 0, st, (const float*)s->part, s->att,
                       c.n_heads, hd, s->nsplit)))
     return e;
-  for (int r = 0; r < R; ++r)  // x += W_o . att  (addInto fused as accumulate)
-    if ((e = gemv_any(L.q_o, L.o, s->att + (size_t)r * d, s->x + (size_t)r * d, d, d, st, 1))) return e;
+  if ((e = proj(L.q_o, L.o, s->att, s->x, d, d, d, 1))) return e;  // x += W_o . att (addInto fused)
   if ((e = pdl_launch(rmsnorm_kernel, dim3(R), dim3(256), 0, st, s->x, (const float*)nullptr, L.ffn_norm, s->xb, d,
                       c.rms_eps)))
     return e;
-  for (int r = 0; r < R; ++r) {
-    const float* xr = s->xb + (size_t)r * d;
-    float* o = s->gu + (size_t)r * 2 * f;
-    if (L.gu) {
-      if ((e = gemv_any(L.q_gate, L.gu, xr, o, 2 * f, d, st, 0))) return e;
-    } else {
-      if ((e = gemv_any(L.q_gate, L.gate, xr, o, f, d, st, 0))) return e;
-      if ((e = gemv_any(L.q_up, L.up, xr, o + f, f, d, st, 0))) return e;
-    }
+  if (L.gu) {
+    if ((e = proj(L.q_gate, L.gu, s->xb, s->gu, 2 * f, d, 2 * f, 0))) return e;
+  } else {
+    if ((e = proj(L.q_gate, L.gate, s->xb, s->gu, f, d, 2 * f, 0))) return e;
+    if ((e = proj(L.q_up, L.up, s->xb, s->gu + f, f, d, 2 * f, 0))) return e;
   }
   if ((e = pdl_launch(swiglu_kernel, dim3(min(1184, (R * f + 255) / 256)), dim3(256), 0, st, (const float*)s->gu, s->h,
                       f, R)))
     return e;
-  for (int r = 0; r < R; ++r)
-    if ((e = gemv_any(L.q_down, L.down, s->h + (size_t)r * f, s->x + (size_t)r * d, d, f, st, 1))) return e;
+  if ((e = proj(L.q_down, L.down, s->h, s->x, d, f, d, 1))) return e;
   return cudaSuccess;
 }
 
@@ -677,6 +711,7 @@ extern "C" {
 // ---- the backend vtable, one call per slot (backend.zig:67-97) ----
 
 int vtb_cuda_begin_token(VtbCudaState* s, const int32_t* tokens) {
+  cudaGetLastError();  // drop a stale error left by an unrelated earlier call
   if (!s || !tokens) return merr(VTB_CUDA_ERR_INVALID_ARG, "null argument");
   cudaSetDevice(s->m->device);
   std::vector<int32_t> seq(s->n_seqs), pos(s->n_seqs);
@@ -687,17 +722,20 @@ int vtb_cuda_begin_token(VtbCudaState* s, const int32_t* tokens) {
 }
 
 int vtb_cuda_layer_step(VtbCudaState* s, int32_t layer) {
+  cudaGetLastError();  // drop a stale error left by an unrelated earlier call
   if (!s || layer < 0 || layer >= s->m->c.n_layers || s->rows <= 0)
     return merr(VTB_CUDA_ERR_INVALID_ARG, "bad layer step");
   return mcuda(enqueue_layer(s, layer));
 }
 
 int vtb_cuda_final_step(VtbCudaState* s) {
+  cudaGetLastError();  // drop a stale error left by an unrelated earlier call
   if (!s || s->rows <= 0) return merr(VTB_CUDA_ERR_INVALID_ARG, "no token staged");
   return mcuda(enqueue_final(s, false));
 }
 
 int vtb_cuda_finalize_token(VtbCudaState* s, float* logits, int32_t* argmax) {
+  cudaGetLastError();  // drop a stale error left by an unrelated earlier call
   if (!s || s->rows <= 0) return merr(VTB_CUDA_ERR_INVALID_ARG, "no token staged");
   const int n = s->rows;
   int rc = finalize(s, n, logits, argmax);
@@ -711,6 +749,7 @@ int vtb_cuda_finalize_token(VtbCudaState* s, float* logits, int32_t* argmax) {
 // per state: the graph reads tokens and positions from pinned host staging,
 // so it is captured once and replayed every token.
 int vtb_cuda_step(VtbCudaState* s, const int32_t* tokens, float* logits, int32_t* argmax) {
+  cudaGetLastError();  // drop a stale error left by an unrelated earlier call
   if (!s || !tokens) return merr(VTB_CUDA_ERR_INVALID_ARG, "null argument");
   cudaSetDevice(s->m->device);
   std::vector<int32_t> seq(s->n_seqs), pos(s->n_seqs);
@@ -749,6 +788,7 @@ int vtb_cuda_step(VtbCudaState* s, const int32_t* tokens, float* logits, int32_t
 // Batched prompt prefill of sequence `seq` (prefillCpu, prefill.zig:111-147):
 // all n tokens go through each layer together; logits of the last token.
 int vtb_cuda_prefill(VtbCudaState* s, int32_t seq, const int32_t* tokens, int32_t n, float* logits, int32_t* argmax) {
+  cudaGetLastError();  // drop a stale error left by an unrelated earlier call
   if (!s || !tokens || seq < 0 || seq >= s->n_seqs) return merr(VTB_CUDA_ERR_INVALID_ARG, "bad prefill arguments");
   if (n == 0) return VTB_CUDA_OK;
   const VtbCudaLlamaConfig& c = s->m->c;

@@ -31,6 +31,7 @@ static unsigned char* g_noalloc_dev_ptr[64];  // per device ordinal, filled on f
 extern "C" int vtb_cuda_gemv_q8_0_q8_0_noalloc(const void* w, const float* x, float* y, int64_t m, int64_t k,
                                                void* stream, int pdl) {
   using namespace vtb;
+  cudaGetLastError();
   int rc = check_mat(Q8_0, w, m, k);
   if (rc) return rc;
   if (!x || !y) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null x or y");

@@ -86,5 +86,20 @@ def gemv_q8_0_q8_0(w: torch.Tensor, x: torch.Tensor, m: int, k: int, out=None, s
     return y
 
 
+def gemm(quant: int, w: torch.Tensor, acts: torch.Tensor, m: int, k: int, precise: bool = False,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[B, m] = acts[B, k] . W^T on the tcgen05 tensor cores (prefill)."""
+    _dev(w, "w"); _dev(acts, "acts")
+    nb = acts.shape[0]
+    if acts.dtype != torch.float32 or acts.numel() != nb * k:
+        raise ValueError("acts must be f32[B, k]")
+    o = torch.empty(nb, m, dtype=torch.float32, device=acts.device) if out is None else out
+    wsb = lib.vtb_cuda_gemm_workspace_bytes(k, nb, int(precise))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=acts.device)
+    _lib.check(lib.vtb_cuda_gemm(quant, w.data_ptr(), acts.data_ptr(), o.data_ptr(), m, k, nb, int(precise),
+                                 ws.data_ptr(), wsb, _stream()), "vtb_cuda_gemm")
+    return o
+
+
 def check_device_error() -> None:
     _lib.check(lib.vtb_cuda_check_device_error(), "device error word")
