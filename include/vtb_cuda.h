@@ -234,6 +234,45 @@ int vtb_cuda_step(VtbCudaState *s, const int32_t *tokens, float *logits, int32_t
 int vtb_cuda_prefill(VtbCudaState *s, int32_t seq, const int32_t *tokens, int32_t n, float *logits,
                      int32_t *argmax);
 
+/* ------------------------------------------------------------------ */
+/* Tensor parallelism (NCCL over NVLink/NVSwitch; no counterpart in the   */
+/* reference, which is single-device)                                   */
+/* ------------------------------------------------------------------ */
+
+#define VTB_CUDA_TP_ID_BYTES 128
+typedef struct VtbCudaTp VtbCudaTp;
+
+/* Rows and columns one rank owns: Q/K/V and gate/up by output rows, O and
+ * down along K (head / ffn columns, whole quantization blocks), LM head by
+ * vocabulary rows. */
+typedef struct {
+  int32_t heads, kv_heads;
+  int32_t q_row0, q_rows, kv_row0, kv_rows, ffn_row0, ffn_rows;
+  int32_t o_col0, o_cols, down_col0, down_cols, vocab_row0, vocab_rows;
+} VtbCudaTpShard;
+
+/* Rank 0 creates the communicator id and shares it with the other ranks
+ * (any host channel); every rank then calls vtb_cuda_tp_init. */
+int vtb_cuda_tp_unique_id(uint8_t *id_out /* VTB_CUDA_TP_ID_BYTES */);
+VtbCudaTp *vtb_cuda_tp_init(int device, int rank, int world, const uint8_t *id);
+void vtb_cuda_tp_destroy(VtbCudaTp *tp);
+int vtb_cuda_tp_rank(const VtbCudaTp *tp);
+int vtb_cuda_tp_world(const VtbCudaTp *tp);
+/* Host-only helpers (no GPU needed): the shard plan, and a copy of a row x
+ * column block of a quantized tensor (columns on block boundaries). */
+int vtb_cuda_tp_shard_plan(const VtbCudaLlamaConfig *cfg, int rank, int world, int32_t k_block,
+                           VtbCudaTpShard *out);
+int vtb_cuda_tp_slice(int quant, const void *src, int64_t rows, int64_t k, int64_t row0, int64_t nrows,
+                      int64_t col0, int64_t ncols, void *dst);
+/* vtb_cuda_model_create for one rank of a tensor-parallel group: takes the
+ * full host tensors and uploads this rank's shard; layer steps then
+ * all-reduce after O and down and all-gather the logits.  tp = NULL is the
+ * single-GPU model. */
+VtbCudaModel *vtb_cuda_model_create_tp(VtbCudaCtx *ctx, VtbCudaTp *tp, const VtbCudaLlamaConfig *cfg,
+                                       const VtbCudaLayerWeights *layers, const void *token_embd,
+                                       int32_t q_token_embd, const float *output_norm, const void *output_w,
+                                       int32_t q_output);
+
 #ifdef __cplusplus
 }
 #endif

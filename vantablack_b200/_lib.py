@@ -65,6 +65,14 @@ SIGNATURES = {
     "vtb_cuda_finalize_token": (_int, [_vp, _vp, _vp]),
     "vtb_cuda_step": (_int, [_vp, _vp, _vp, _vp]),
     "vtb_cuda_prefill": (_int, [_vp, _i32, _vp, _i32, _vp, _vp]),
+    "vtb_cuda_tp_unique_id": (_int, [_vp]),
+    "vtb_cuda_tp_init": (_vp, [_int, _int, _int, _vp]),
+    "vtb_cuda_tp_destroy": (None, [_vp]),
+    "vtb_cuda_tp_rank": (_int, [_vp]),
+    "vtb_cuda_tp_world": (_int, [_vp]),
+    "vtb_cuda_tp_shard_plan": (_int, [_vp, _int, _int, _i32, _vp]),
+    "vtb_cuda_tp_slice": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "vtb_cuda_model_create_tp": (_vp, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _i32]),
 }
 
 

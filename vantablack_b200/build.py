@@ -20,6 +20,19 @@ ROOT = os.path.dirname(HERE)
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
+def nccl_dirs():
+    """NCCL headers and library: the copy PyTorch ships (same library torch
+    loads in-process), else the system one."""
+    try:
+        import nvidia.nccl as n
+        base = list(n.__path__)[0]
+        if os.path.exists(os.path.join(base, "include", "nccl.h")):
+            return os.path.join(base, "include"), os.path.join(base, "lib")
+    except Exception:
+        pass
+    return "/usr/include", "/usr/lib/x86_64-linux-gnu"
+
+
 def nvcc() -> str:
     cand = [os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"]
     for c in cand:
@@ -46,6 +59,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
            "-Xcompiler", "-fPIC", "-shared", "-o", LIB + ".tmp",
            os.path.join(CSRC, "libvtbcuda.cu"), "-lcudart"]
+    inc, libdir = nccl_dirs()
+    cmd += ["-I" + inc, "-L" + libdir, "-l:libnccl.so.2", "-Xlinker", "-rpath," + libdir]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)

@@ -6,5 +6,6 @@
 #include "quant_aux.cu"
 #include "gemm_tc.cu"
 #include "api.cu"
+#include "tp.cu"
 #include "model.cu"
 #include "noalloc.cu"

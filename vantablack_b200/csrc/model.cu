@@ -15,6 +15,7 @@
 // Row r of a step is token `tok[r]` of sequence `seq[r]` at position
 // `pos[r]`: a decode step has one row per sequence, a prefill step has one
 // row per prompt token of one sequence (prefill.zig:111-232 semantics).
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -317,6 +318,10 @@ struct VtbCudaModel {
   int q_out;
   void* blob = nullptr;  // one allocation for every weight
   size_t blob_bytes = 0;
+  // Tensor parallelism (tp.cu): this rank's shard; world 1 = the whole model.
+  VtbCudaTp* tp = nullptr;
+  VtbCudaTpShard sh;
+  int H, KV, F, V;  // local q heads, kv heads, ffn rows, vocab rows
 };
 
 struct VtbCudaState {
@@ -333,6 +338,8 @@ struct VtbCudaState {
   std::vector<int64_t> seq_pos;  // host-authoritative positions (KvCache.pos, forward.zig:161,168)
   int rows = 0;             // rows of the step in flight
   int nsplit;
+  float* logits_local;      // [rows][V] LM-head slice under tensor parallelism
+  bool pending = false;     // tmp holds an all-reduced partial still to be added to x
   cudaGraphExec_t graph = nullptr;
   int graph_rows = -1;
 };
@@ -340,15 +347,19 @@ struct VtbCudaState {
 // Error text goes to the same thread-local buffer as the rest of the shim
 // (vtb_cuda_last_error); the library is one translation unit.
 static int merr(int st, const char* msg) { return set_err(st, "%s", msg); }
-static int mcuda(cudaError_t e) { return cuda_status(e); }
+static int mcuda(cudaError_t e) {
+  if (e == cudaErrorUnknown && strncmp(g_last_err, "NCCL", 4) == 0) return VTB_CUDA_ERR_COMM;
+  return cuda_status(e);
+}
 
 static bool q_ok(int q) { return host_quant_ok(q); }
 
 extern "C" {
 
-VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* cfg, const VtbCudaLayerWeights* lw,
-                                    const void* token_embd, int32_t q_token_embd, const float* output_norm,
-                                    const void* output_w, int32_t q_output) {
+VtbCudaModel* vtb_cuda_model_create_tp(VtbCudaCtx* ctx, VtbCudaTp* tp, const VtbCudaLlamaConfig* cfg,
+                                       const VtbCudaLayerWeights* lw, const void* token_embd, int32_t q_token_embd,
+                                       const float* output_norm, const void* output_w, int32_t q_output) {
+  cudaGetLastError();
   if (!ctx || !cfg || !lw || !token_embd || !output_norm || !output_w) {
     merr(VTB_CUDA_ERR_INVALID_ARG, "null argument");
     return nullptr;
@@ -375,7 +386,7 @@ VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* c
     merr(VTB_CUDA_ERR_UNSUPPORTED, "embedding/output quant type has no CUDA kernel");
     return nullptr;
   }
-  const int d = c.dim, kvd = c.n_kv_heads * c.head_dim, f = c.ffn_dim;
+  const int d = c.dim, f = c.ffn_dim, hd = c.head_dim;
   for (int l = 0; l < c.n_layers; ++l) {
     const int ks[7] = {d, d, d, d, d, d, f};
     const int qs[7] = {lw[l].q_attn_q, lw[l].q_attn_k, lw[l].q_attn_v, lw[l].q_attn_o,
@@ -386,12 +397,22 @@ VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* c
         return nullptr;
       }
   }
+  const int rank = tp ? tp->rank : 0, world = tp ? tp->world : 1;
+  VtbCudaTpShard sh;
+  int kblock = 32;
+  for (int l = 0; l < c.n_layers; ++l)
+    kblock = std::max(kblock, std::max(host_block_elems(lw[l].q_attn_o), host_block_elems(lw[l].q_ffn_down)));
+  if (vtb_cuda_tp_shard_plan(&c, rank, world, kblock, &sh) != VTB_CUDA_OK) return nullptr;
   VtbCudaModel* m = new (std::nothrow) VtbCudaModel();
   if (!m) return nullptr;
   m->ctx = ctx;
   m->c = c;
+  m->tp = tp;
+  m->sh = sh;
+  m->H = sh.heads; m->KV = sh.kv_heads; m->F = sh.ffn_rows; m->V = sh.vocab_rows;
   cudaGetDevice(&m->device);
-  // Layout pass: offsets of every tensor in one blob (256-byte aligned).
+  const int qd = m->H * hd, kvd = m->KV * hd, F = m->F, V = m->V;
+  // Layout pass: offsets of every (sharded) tensor in one blob, 256-byte aligned.
   auto rbytes = [](int q, int k) { return (size_t)host_row_bytes(q, k); };
   size_t off = 0;
   auto take = [&](size_t n) { size_t o = off; off = (off + n + 255) & ~size_t(255); return o; };
@@ -401,18 +422,18 @@ VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* c
     Off& o = offs[l];
     o.fq = lw[l].q_attn_q == lw[l].q_attn_k && lw[l].q_attn_q == lw[l].q_attn_v;
     o.fg = lw[l].q_ffn_gate == lw[l].q_ffn_up;
-    if (o.fq) o.qkv = take(rbytes(lw[l].q_attn_q, d) * (d + 2 * kvd));
-    else { o.q = take(rbytes(lw[l].q_attn_q, d) * d); o.k = take(rbytes(lw[l].q_attn_k, d) * kvd); o.v = take(rbytes(lw[l].q_attn_v, d) * kvd); }
-    o.o = take(rbytes(lw[l].q_attn_o, d) * d);
-    if (o.fg) o.gu = take(rbytes(lw[l].q_ffn_gate, d) * 2 * f);
-    else { o.gate = take(rbytes(lw[l].q_ffn_gate, d) * f); o.up = take(rbytes(lw[l].q_ffn_up, d) * f); }
-    o.down = take(rbytes(lw[l].q_ffn_down, f) * d);
+    if (o.fq) o.qkv = take(rbytes(lw[l].q_attn_q, d) * (qd + 2 * kvd));
+    else { o.q = take(rbytes(lw[l].q_attn_q, d) * qd); o.k = take(rbytes(lw[l].q_attn_k, d) * kvd); o.v = take(rbytes(lw[l].q_attn_v, d) * kvd); }
+    o.o = take(rbytes(lw[l].q_attn_o, qd) * d);
+    if (o.fg) o.gu = take(rbytes(lw[l].q_ffn_gate, d) * 2 * F);
+    else { o.gate = take(rbytes(lw[l].q_ffn_gate, d) * F); o.up = take(rbytes(lw[l].q_ffn_up, d) * F); }
+    o.down = take(rbytes(lw[l].q_ffn_down, F) * d);
     o.an = take(4 * (size_t)d);
     o.fn = take(4 * (size_t)d);
   }
   const size_t o_embd = take(rbytes(q_token_embd, d) * c.vocab_size);
   const size_t o_onorm = take(4 * (size_t)d);
-  const size_t o_out = take(rbytes(q_output, d) * c.vocab_size);
+  const size_t o_out = take(rbytes(q_output, d) * V);
   m->blob_bytes = off + 256;
   if (cudaMalloc(&m->blob, m->blob_bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -426,39 +447,49 @@ VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* c
   auto up = [&](size_t o, const void* src, size_t n) {
     ok = ok && cudaMemcpyAsync(B + o, src, n, cudaMemcpyHostToDevice, st) == cudaSuccess;
   };
+  // rows [row0, row0+nrows) x columns [col0, col0+ncols) of a [*, k] tensor -> dense at blob offset o
+  auto up_shard = [&](size_t o, int q, const void* src, int k, int row0, int nrows, int col0, int ncols) {
+    const size_t rb = rbytes(q, k), w = rbytes(q, ncols), c0 = rbytes(q, col0);
+    const uint8_t* sp = static_cast<const uint8_t*>(src) + (size_t)row0 * rb + c0;
+    if (w == rb) up(o, sp, rb * nrows);
+    else ok = ok && cudaMemcpy2DAsync(B + o, w, sp, rb, w, nrows, cudaMemcpyHostToDevice, st) == cudaSuccess;
+  };
   m->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
     const Off& o = offs[l];
     DevLayer& L = m->layers[l];
     L.q_q = lw[l].q_attn_q; L.q_k = lw[l].q_attn_k; L.q_v = lw[l].q_attn_v; L.q_o = lw[l].q_attn_o;
     L.q_gate = lw[l].q_ffn_gate; L.q_up = lw[l].q_ffn_up; L.q_down = lw[l].q_ffn_down;
-    const size_t rq = rbytes(L.q_q, d), rk = rbytes(L.q_k, d), rv = rbytes(L.q_v, d);
+    const size_t rq = rbytes(L.q_q, d), rk = rbytes(L.q_k, d);
     if (o.fq) {
       L.qkv = B + o.qkv;
-      up(o.qkv, lw[l].attn_q, rq * d);
-      up(o.qkv + rq * d, lw[l].attn_k, rk * kvd);
-      up(o.qkv + rq * d + rk * kvd, lw[l].attn_v, rv * kvd);
+      up_shard(o.qkv, L.q_q, lw[l].attn_q, d, sh.q_row0, qd, 0, d);
+      up_shard(o.qkv + rq * qd, L.q_k, lw[l].attn_k, d, sh.kv_row0, kvd, 0, d);
+      up_shard(o.qkv + rq * qd + rk * kvd, L.q_v, lw[l].attn_v, d, sh.kv_row0, kvd, 0, d);
       L.q = L.k = L.v = nullptr;
     } else {
       L.qkv = nullptr;
       L.q = B + o.q; L.k = B + o.k; L.v = B + o.v;
-      up(o.q, lw[l].attn_q, rq * d); up(o.k, lw[l].attn_k, rk * kvd); up(o.v, lw[l].attn_v, rv * kvd);
+      up_shard(o.q, L.q_q, lw[l].attn_q, d, sh.q_row0, qd, 0, d);
+      up_shard(o.k, L.q_k, lw[l].attn_k, d, sh.kv_row0, kvd, 0, d);
+      up_shard(o.v, L.q_v, lw[l].attn_v, d, sh.kv_row0, kvd, 0, d);
     }
     L.o = B + o.o;
-    up(o.o, lw[l].attn_o, rbytes(L.q_o, d) * d);
-    const size_t rg = rbytes(L.q_gate, d), ru = rbytes(L.q_up, d);
+    up_shard(o.o, L.q_o, lw[l].attn_o, d, 0, d, sh.o_col0, sh.o_cols);
+    const size_t rg = rbytes(L.q_gate, d);
     if (o.fg) {
       L.gu = B + o.gu;
-      up(o.gu, lw[l].ffn_gate, rg * f);
-      up(o.gu + rg * f, lw[l].ffn_up, ru * f);
+      up_shard(o.gu, L.q_gate, lw[l].ffn_gate, d, sh.ffn_row0, F, 0, d);
+      up_shard(o.gu + rg * F, L.q_up, lw[l].ffn_up, d, sh.ffn_row0, F, 0, d);
       L.gate = L.up = nullptr;
     } else {
       L.gu = nullptr;
       L.gate = B + o.gate; L.up = B + o.up;
-      up(o.gate, lw[l].ffn_gate, rg * f); up(o.up, lw[l].ffn_up, ru * f);
+      up_shard(o.gate, L.q_gate, lw[l].ffn_gate, d, sh.ffn_row0, F, 0, d);
+      up_shard(o.up, L.q_up, lw[l].ffn_up, d, sh.ffn_row0, F, 0, d);
     }
     L.down = B + o.down;
-    up(o.down, lw[l].ffn_down, rbytes(L.q_down, f) * d);
+    up_shard(o.down, L.q_down, lw[l].ffn_down, f, 0, d, sh.down_col0, sh.down_cols);
     L.attn_norm = reinterpret_cast<const float*>(B + o.an);
     L.ffn_norm = reinterpret_cast<const float*>(B + o.fn);
     up(o.an, lw[l].attn_norm, 4 * (size_t)d);
@@ -469,7 +500,7 @@ VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* c
   m->out_norm = reinterpret_cast<const float*>(B + o_onorm);
   up(o_onorm, output_norm, 4 * (size_t)d);
   m->out_w = B + o_out; m->q_out = q_output;
-  up(o_out, output_w, rbytes(q_output, d) * c.vocab_size);
+  up_shard(o_out, q_output, output_w, d, sh.vocab_row0, V, 0, d);
   ok = ok && cudaStreamSynchronize(st) == cudaSuccess;
   if (!ok) {
     mcuda(cudaGetLastError());
@@ -478,6 +509,12 @@ VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* c
     return nullptr;
   }
   return m;
+}
+
+VtbCudaModel* vtb_cuda_model_create(VtbCudaCtx* ctx, const VtbCudaLlamaConfig* cfg, const VtbCudaLayerWeights* lw,
+                                    const void* token_embd, int32_t q_token_embd, const float* output_norm,
+                                    const void* output_w, int32_t q_output) {
+  return vtb_cuda_model_create_tp(ctx, nullptr, cfg, lw, token_embd, q_token_embd, output_norm, output_w, q_output);
 }
 
 void vtb_cuda_model_destroy(VtbCudaModel* m) {
@@ -509,11 +546,11 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   s->n_seqs = n_seqs;
   s->max_rows = max_rows;
   s->nsplit = (c.max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
-  const size_t R = max_rows, d = c.dim, kvd = (size_t)c.n_kv_heads * c.head_dim, f = c.ffn_dim;
-  const size_t qkvw = d + 2 * kvd;
+  const size_t R = max_rows, d = c.dim, hd = c.head_dim, qd = (size_t)m->H * hd, kvd = (size_t)m->KV * hd, f = m->F;
+  const size_t qkvw = qd + 2 * kvd;
   const size_t kmax = d > f ? d : f;
-  size_t fl = R * (d + d + qkvw + d + 2 * f + f + (size_t)c.vocab_size + d + kmax) +
-              R * c.n_heads * (size_t)s->nsplit * (c.head_dim + 2) + 64;
+  size_t fl = R * (d + d + qkvw + qd + 2 * f + f + (size_t)c.vocab_size + m->V + d + kmax) +
+              R * m->H * (size_t)s->nsplit * (hd + 2) + 64;
   const size_t kvn = (size_t)n_seqs * c.n_layers * c.max_seq * kvd;
   float* base = nullptr;
   int32_t* ib = nullptr;
@@ -528,9 +565,10 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   }
   float* p = base;
   auto carve = [&](size_t n) { float* r = p; p += (n + 3) & ~size_t(3); return r; };
-  s->x = carve(R * d); s->xb = carve(R * d); s->qkv = carve(R * qkvw); s->att = carve(R * d);
+  s->x = carve(R * d); s->xb = carve(R * d); s->qkv = carve(R * qkvw); s->att = carve(R * qd);
   s->gu = carve(R * 2 * f); s->h = carve(R * f); s->logits = carve(R * c.vocab_size);
-  s->part = carve(R * c.n_heads * (size_t)s->nsplit * (c.head_dim + 2));
+  s->logits_local = carve(R * m->V);
+  s->part = carve(R * m->H * (size_t)s->nsplit * (hd + 2));
   s->tmp = carve(R * d);
   s->ws = carve(R * kmax);  // bf16 hi + lo = 4 bytes per activation
   s->kc = carve(kvn); s->vc = carve(kvn);
@@ -584,6 +622,7 @@ static int stage_rows(VtbCudaState* s, int rows, const int32_t* tok, const int32
     s->hbuf[2 * s->max_rows + r] = pos[r];
   }
   s->rows = rows;
+  s->pending = false;
   return VTB_CUDA_OK;
 }
 
@@ -609,59 +648,84 @@ static cudaError_t pdl_launch(K kern, dim3 grid, dim3 block, size_t smem, cudaSt
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// RMSNorm of the staged rows; under tensor parallelism the all-reduced partial
+// waiting in tmp is added to x first (addInto fused into the norm).
+static cudaError_t enqueue_norm(VtbCudaState* s, const float* w, int r0, int n) {
+  const VtbCudaLlamaConfig& c = s->m->c;
+  const float* res = s->pending ? s->tmp + (size_t)r0 * c.dim : nullptr;
+  s->pending = false;
+  return pdl_launch(rmsnorm_kernel, dim3(n), dim3(256), 0, s->st, s->x + (size_t)r0 * c.dim, res, w, s->xb, c.dim,
+                    c.rms_eps);
+}
+
+static cudaError_t allreduce_tmp(VtbCudaState* s, size_t n) {
+  const ncclResult_t r = ncclAllReduce(s->tmp, s->tmp, n, ncclFloat32, ncclSum, s->m->tp->comm, s->st);
+  if (r != ncclSuccess) {
+    nccl_status(r);
+    return cudaErrorUnknown;
+  }
+  s->pending = true;
+  return cudaSuccess;
+}
+
 // One transformer block for the staged rows (cpuLayerStep, forward.zig:230-288).
 static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   VtbCudaModel* m = s->m;
   const VtbCudaLlamaConfig& c = m->c;
   const DevLayer& L = m->layers[l];
-  const int R = s->rows, d = c.dim, kvd = c.n_kv_heads * c.head_dim, f = c.ffn_dim, qkvw = d + 2 * kvd;
-  const int hd = c.head_dim, G = c.n_heads / c.n_kv_heads;
+  const int hd = c.head_dim, H = m->H, KV = m->KV, G = H / KV;
+  const int R = s->rows, d = c.dim, qd = H * hd, kvd = KV * hd, f = m->F, qkvw = qd + 2 * kvd;
+  const bool tp = m->tp && m->tp->world > 1;
   cudaStream_t st = s->st;
   cudaError_t e;
   RowInfo ri{s->seq, s->pos};
-  if ((e = pdl_launch(rmsnorm_kernel, dim3(R), dim3(256), 0, st, s->x, (const float*)nullptr, L.attn_norm, s->xb, d,
-                      c.rms_eps)))
-    return e;
+  if ((e = enqueue_norm(s, L.attn_norm, 0, R))) return e;
   const bool gemm = R >= GEMM_MIN_ROWS;
-  auto proj = [&](int q, const uint8_t* w, const float* in, float* out, int m, int k, int ld_out, int acc) -> cudaError_t {
+  auto proj = [&](int q, const uint8_t* w, const float* in, float* out, int mm, int k, int ld_out, int acc) -> cudaError_t {
     // out[r*ld_out + i] (+)= W . in[r]; GEMM rows need a dense out, so `acc` goes through tmp
-    if (gemm && k % 64 == 0 && (acc || ld_out == m)) {
+    if (gemm && k % 64 == 0 && (acc || ld_out == mm)) {
       if (acc) {
-        cudaError_t e2 = launch_gemm_tc(q, w, in, s->tmp, m, k, R, true, s->ws, st);
+        cudaError_t e2 = launch_gemm_tc(q, w, in, s->tmp, mm, k, R, true, s->ws, st);
         if (e2) return e2;
-        return pdl_launch(add_kernel, dim3(min(1184, (R * m + 255) / 256)), dim3(256), 0, st, out, (const float*)s->tmp,
-                          (long long)R * m);
+        return pdl_launch(add_kernel, dim3(min(1184, (R * mm + 255) / 256)), dim3(256), 0, st, out,
+                          (const float*)s->tmp, (long long)R * mm);
       }
-      return launch_gemm_tc(q, w, in, out, m, k, R, true, s->ws, st);
+      return launch_gemm_tc(q, w, in, out, mm, k, R, true, s->ws, st);
     }
     for (int r = 0; r < R; ++r) {
-      cudaError_t e2 = gemv_any(q, w, in + (size_t)r * k, out + (size_t)r * ld_out, m, k, st, acc);
+      cudaError_t e2 = gemv_any(q, w, in + (size_t)r * k, out + (size_t)r * ld_out, mm, k, st, acc);
       if (e2) return e2;
     }
     return cudaSuccess;
   };
+  // x += W . in for the row-parallel projections (O, down): single GPU adds
+  // straight into x; tensor parallel writes the partial to tmp and all-reduces.
+  auto residual = [&](int q, const uint8_t* w, const float* in, int k) -> cudaError_t {
+    if (!tp) return proj(q, w, in, s->x, d, k, d, 1);
+    cudaError_t e2 = proj(q, w, in, s->tmp, d, k, d, 0);
+    if (e2) return e2;
+    return allreduce_tmp(s, (size_t)R * d);
+  };
   if (L.qkv) {
     if ((e = proj(L.q_q, L.qkv, s->xb, s->qkv, qkvw, d, qkvw, 0))) return e;
   } else {
-    if ((e = proj(L.q_q, L.q, s->xb, s->qkv, d, d, qkvw, 0))) return e;
-    if ((e = proj(L.q_k, L.k, s->xb, s->qkv + d, kvd, d, qkvw, 0))) return e;
-    if ((e = proj(L.q_v, L.v, s->xb, s->qkv + d + kvd, kvd, d, qkvw, 0))) return e;
+    if ((e = proj(L.q_q, L.q, s->xb, s->qkv, qd, d, qkvw, 0))) return e;
+    if ((e = proj(L.q_k, L.k, s->xb, s->qkv + qd, kvd, d, qkvw, 0))) return e;
+    if ((e = proj(L.q_v, L.v, s->xb, s->qkv + qd + kvd, kvd, d, qkvw, 0))) return e;
   }
   if ((e = pdl_launch(rope_kv_kernel, dim3(R), dim3(256), 0, st, s->qkv, s->kc, s->vc, ri, l, c.n_layers, c.max_seq,
-                      c.n_heads, c.n_kv_heads, hd, c.rope_base)))
+                      H, KV, hd, c.rope_base)))
     return e;
   const size_t asmem = (size_t)G * (hd + ATT_CHUNK) * 4;
-  if ((e = pdl_launch(attn_partial_kernel, dim3(c.n_kv_heads, R, s->nsplit), dim3(ATT_THREADS), asmem, st,
+  if ((e = pdl_launch(attn_partial_kernel, dim3(KV, R, s->nsplit), dim3(ATT_THREADS), asmem, st,
                       (const float*)s->qkv, (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq,
-                      c.n_heads, c.n_kv_heads, hd, s->part, s->nsplit)))
+                      H, KV, hd, s->part, s->nsplit)))
     return e;
-  if ((e = pdl_launch(attn_combine_kernel, dim3(c.n_heads, R), dim3(128), 0, st, (const float*)s->part, s->att,
-                      c.n_heads, hd, s->nsplit)))
+  if ((e = pdl_launch(attn_combine_kernel, dim3(H, R), dim3(128), 0, st, (const float*)s->part, s->att, H, hd,
+                      s->nsplit)))
     return e;
-  if ((e = proj(L.q_o, L.o, s->att, s->x, d, d, d, 1))) return e;  // x += W_o . att (addInto fused)
-  if ((e = pdl_launch(rmsnorm_kernel, dim3(R), dim3(256), 0, st, s->x, (const float*)nullptr, L.ffn_norm, s->xb, d,
-                      c.rms_eps)))
-    return e;
+  if ((e = residual(L.q_o, L.o, s->att, qd))) return e;  // x += W_o . att (addInto fused)
+  if ((e = enqueue_norm(s, L.ffn_norm, 0, R))) return e;
   if (L.gu) {
     if ((e = proj(L.q_gate, L.gu, s->xb, s->gu, 2 * f, d, 2 * f, 0))) return e;
   } else {
@@ -671,8 +735,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   if ((e = pdl_launch(swiglu_kernel, dim3(min(1184, (R * f + 255) / 256)), dim3(256), 0, st, (const float*)s->gu, s->h,
                       f, R)))
     return e;
-  if ((e = proj(L.q_down, L.down, s->h, s->x, d, f, d, 1))) return e;
-  return cudaSuccess;
+  return residual(L.q_down, L.down, s->h, f);
 }
 
 // Final RMSNorm + LM head (backend_cpu.zig finalStep :88-106) and argmax.
@@ -682,14 +745,24 @@ static cudaError_t enqueue_final(VtbCudaState* s, bool last_only) {
   const VtbCudaLlamaConfig& c = m->c;
   cudaStream_t st = s->st;
   cudaError_t e;
+  const bool tp = m->tp && m->tp->world > 1;
   const int r0 = last_only ? s->rows - 1 : 0, n = last_only ? 1 : s->rows;
-  if ((e = pdl_launch(rmsnorm_kernel, dim3(n), dim3(256), 0, st, s->x + (size_t)r0 * c.dim, (const float*)nullptr,
-                      m->out_norm, s->xb, c.dim, c.rms_eps)))
-    return e;
+  if ((e = enqueue_norm(s, m->out_norm, r0, n))) return e;
+  float* lg = tp ? s->logits_local : s->logits;
   for (int r = 0; r < n; ++r)
-    if ((e = gemv_any(m->q_out, m->out_w, s->xb + (size_t)r * c.dim, s->logits + (size_t)r * c.vocab_size,
-                      c.vocab_size, c.dim, st, 0)))
+    if ((e = gemv_any(m->q_out, m->out_w, s->xb + (size_t)r * c.dim, lg + (size_t)r * m->V, m->V, c.dim, st, 0)))
       return e;
+  if (tp) {  // all-gather the vocabulary slices, one row at a time (rank slices are contiguous vocab ranges)
+    ncclResult_t rr = ncclGroupStart();
+    for (int r = 0; r < n && rr == ncclSuccess; ++r)
+      rr = ncclAllGather(s->logits_local + (size_t)r * m->V, s->logits + (size_t)r * c.vocab_size, m->V, ncclFloat32,
+                         m->tp->comm, st);
+    if (rr == ncclSuccess) rr = ncclGroupEnd();
+    if (rr != ncclSuccess) {
+      nccl_status(rr);
+      return cudaErrorUnknown;
+    }
+  }
   argmax_kernel<<<n, 1024, 0, st>>>(s->logits, s->amax, c.vocab_size);
   return cudaGetLastError();
 }

@@ -118,11 +118,66 @@ class Context:
             pass
 
 
-class CudaModel:
-    """Weights resident in HBM (vtb_cuda_model_create)."""
+class TensorParallel:
+    """One rank of a tensor-parallel group (NCCL communicator, vtb_cuda_tp_init).
 
-    def __init__(self, ctx: Context, w: HostWeights):
-        self.ctx, self.cfg, self.lib = ctx, w.cfg, ctx.lib
+    ``exchange(id_bytes) -> id_bytes`` shares rank 0's communicator id with the
+    other ranks (e.g. a torch.distributed broadcast over gloo)."""
+
+    def __init__(self, device: int, rank: int, world: int, exchange):
+        self.lib = _lib_loaded()
+        self.rank, self.world = rank, world
+        buf = (C.c_uint8 * 128)()
+        if rank == 0:
+            _lib.check(self.lib.vtb_cuda_tp_unique_id(buf), "vtb_cuda_tp_unique_id")
+        raw = exchange(bytes(buf))
+        buf = (C.c_uint8 * 128).from_buffer_copy(raw)
+        self.h = self.lib.vtb_cuda_tp_init(device, rank, world, buf)
+        if not self.h:
+            raise _lib.VtbError(-10, "vtb_cuda_tp_init")
+
+    def close(self):
+        if self.h:
+            self.lib.vtb_cuda_tp_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class TpShard(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("heads", "kv_heads", "q_row0", "q_rows", "kv_row0", "kv_rows", "ffn_row0",
+                                         "ffn_rows", "o_col0", "o_cols", "down_col0", "down_cols", "vocab_row0",
+                                         "vocab_rows")]
+
+
+def shard_plan(cfg: LlamaConfig, rank: int, world: int, k_block: int = 256) -> TpShard:
+    """vtb_cuda_tp_shard_plan (host-only)."""
+    lib = _lib_loaded()
+    cc = _CConfig(cfg.dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab_size,
+                  cfg.max_seq, cfg.rope_base, cfg.rms_eps)
+    out = TpShard()
+    _lib.check(lib.vtb_cuda_tp_shard_plan(C.byref(cc), rank, world, k_block, C.byref(out)), "tp_shard_plan")
+    return out
+
+
+def tp_slice(quant: int, t: np.ndarray, rows: int, k: int, row0: int, nrows: int, col0: int, ncols: int):
+    """vtb_cuda_tp_slice (host-only): a row x column block of a quantized tensor."""
+    from .synth import row_bytes
+    lib = _lib_loaded()
+    out = np.empty(nrows * row_bytes(quant, ncols), np.uint8)
+    _lib.check(lib.vtb_cuda_tp_slice(quant, _ptr(t), rows, k, row0, nrows, col0, ncols, _ptr(out)), "tp_slice")
+    return out
+
+
+class CudaModel:
+    """Weights resident in HBM (vtb_cuda_model_create / _tp)."""
+
+    def __init__(self, ctx: Context, w: HostWeights, tp: "TensorParallel | None" = None):
+        self.ctx, self.cfg, self.lib, self.tp = ctx, w.cfg, ctx.lib, tp
         c = w.cfg
         cc = _CConfig(c.dim, c.n_layers, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn_dim, c.vocab_size, c.max_seq,
                       c.rope_base, c.rms_eps)
@@ -137,8 +192,8 @@ class CudaModel:
             L.ffn_norm = _ptr(lw["ffn_norm"])
         qe, emb = w.token_embd
         qo, out = w.output
-        self.h = self.lib.vtb_cuda_model_create(ctx.h, C.byref(cc), C.cast(layers, _vp), _ptr(emb), qe,
-                                                _ptr(w.output_norm), _ptr(out), qo)
+        self.h = self.lib.vtb_cuda_model_create_tp(ctx.h, tp.h if tp else None, C.byref(cc), C.cast(layers, _vp),
+                                                   _ptr(emb), qe, _ptr(w.output_norm), _ptr(out), qo)
         if not self.h:
             raise _lib.VtbError(-1, "vtb_cuda_model_create")
 
