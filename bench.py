@@ -253,6 +253,8 @@ def run_ours(args):
         lib.vtb_cuda_release(b)
     lib.vtb_cuda_destroy(ctx)
 
+    model = model_metrics(rank, world, local, dist, args) if args.model_steps > 0 else None
+
     if rank == 0:
         hbm, peak_kind = peaks()
         launches = args.steps * N_COPIES
@@ -274,6 +276,8 @@ def run_ours(args):
             "clocks": clk.summary(),
             "max_rel_err_vs_oracle": err,
         }
+        if model:
+            line["config"]["model_8b"] = model
         if cpu_v is not None:
             line["cpu_baseline"] = {"value": cpu_v, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
                                     "sample": f"{cpu_n} GEMVs of 5632x2048 Q4_K over {args.cpu_budget:.0f} s, "
@@ -287,6 +291,76 @@ def run_ours(args):
 ALG_BYTES_TRAFFIC = None
 
 
+def model_metrics(rank: int, world: int, local: int, dist, args) -> dict:
+    """BASELINE config 5 (Llama-3-8B architecture, random init, Q4_K_M-style):
+    decode tok/s at batch 1 and 32 and prefill tok/s of a 2048-token prompt,
+    tensor parallel over all ranks (NCCL).  Wall-clocked per call (each call
+    ends with its logits/argmax on the host), max over ranks."""
+    import torch
+    from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState, HostWeights, TensorParallel
+
+    def exchange(b: bytes) -> bytes:
+        if world == 1:
+            return b
+        obj = [b]
+        dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def tmax(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    cfg = LLAMA3_8B
+    w = HostWeights(cfg, seed=8)
+    ctx = Context(local)
+    tp = TensorParallel(local, rank, world, exchange) if world > 1 else None
+    m = CudaModel(ctx, w, tp)
+    del w
+    res = {"model": "llama3_8b_random_init_q4_k_m", "tp": world}
+    rng = np.random.default_rng(1)
+    # prefill: 2048-token prompt
+    st = CudaState(m, 1, max_rows=2048)
+    prompt = rng.integers(3, cfg.vocab_size, 2048)
+    st.prefill(prompt[:64]); st.reset()  # warm-up
+    barrier(); t0 = time.perf_counter()
+    st.prefill(prompt)
+    res["prefill_2048_tok_s"] = 2048 / tmax(time.perf_counter() - t0)
+    # decode, batch 1, continuing after the prompt
+    nxt = 5
+    for _ in range(3):
+        _, am = st.step([nxt], want_logits=False); nxt = int(am[0])
+    n = args.model_steps
+    barrier(); t0 = time.perf_counter()
+    for _ in range(n):
+        _, am = st.step([nxt], want_logits=False); nxt = int(am[0])
+    res["decode_b1_tok_s"] = n / tmax(time.perf_counter() - t0)
+    res["decode_b1_ctx"] = int(st.pos())
+    st.close()
+    # decode, batch 32 (32 independent sequences, one token each per step)
+    st = CudaState(m, 32, max_rows=32)
+    toks = rng.integers(3, cfg.vocab_size, 32)
+    for _ in range(3):
+        _, toks = st.step(toks, want_logits=False)
+    nb = max(2, n // 4)
+    barrier(); t0 = time.perf_counter()
+    for _ in range(nb):
+        _, toks = st.step(toks, want_logits=False)
+    res["decode_b32_tok_s"] = 32 * nb / tmax(time.perf_counter() - t0)
+    st.close()
+    m.close()
+    if tp:
+        tp.close()
+    ctx.close()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -294,6 +368,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--model-steps", type=int, default=32, help="decode steps of the 8B model metrics (0 = skip)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
