@@ -361,6 +361,37 @@ def model_metrics(rank: int, world: int, local: int, dist, args) -> dict:
     return res
 
 
+def run_profile_case(case: str) -> None:
+    """Small, self-terminating workloads for ncu captures (one GPU)."""
+    import torch
+    from vantablack_b200 import ops, synth as S
+    rng = np.random.default_rng(0)
+    if case == "gemv":  # one config-1 launch, then one 311 MB streaming launch
+        for m in (M, M * 48):
+            w = torch.from_numpy(S.quant_tensor(rng, Q4_K, m, K)).cuda()
+            x = torch.from_numpy(S.activations(rng, K)).cuda()
+            ops.gemv(Q4_K, w, x, m, K)
+            torch.cuda.synchronize()
+    elif case == "gemm":  # config 3: Q4_K 14336 x 4096, B = 2048, bf16 mode, two launches
+        m, k, b = 14336, 4096, 2048
+        w = torch.from_numpy(S.quant_tensor(rng, Q4_K, m, k)).cuda()
+        acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
+        for _ in range(2):
+            ops.gemm(Q4_K, w, acts, m, k, precise=False)
+    elif case == "decode":  # TinyLlama architecture: 128-token prefill + 5 decode steps
+        from vantablack_b200.model import TINYLLAMA, Context, CudaModel, CudaState, HostWeights
+        ctx = Context(0)
+        st = CudaState(CudaModel(ctx, HostWeights(TINYLLAMA, seed=1)), 1, max_rows=128)
+        st.prefill(np.arange(3, 131))
+        for i in range(5):
+            st.step([5 + i], want_logits=False)
+    else:
+        raise SystemExit(f"unknown profile case {case}")
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    print("ok", case)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -369,7 +400,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--model-steps", type=int, default=32, help="decode steps of the 8B model metrics (0 = skip)")
+    ap.add_argument("--profile", choices=["gemv", "gemm", "decode"], help="run a small case for ncu and exit")
     args = ap.parse_args()
+    if args.profile:
+        run_profile_case(args.profile)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
