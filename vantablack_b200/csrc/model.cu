@@ -137,9 +137,11 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, float* __restrict__ kc, 
 // Split-K ("flash decode"): CTA (kv_head, row, split) handles positions
 // [split*CHUNK, ...) for the GQA group of q heads that share the kv head,
 // and writes a partial (max, sum, acc[hd]) per q head; attn_combine merges.
-constexpr int ATT_CHUNK = 256;
+constexpr int ATT_CHUNK = 128;
 constexpr int ATT_THREADS = 128;
+constexpr int ATT_GMAX = 8;  // GQA group sizes up to 8 keep their accumulators in registers
 
+template <int GT>  // GT: compile-time group size, or 0 for the generic path
 __global__ void __launch_bounds__(ATT_THREADS)
 attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
                     RowInfo ri, int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd,
@@ -147,7 +149,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ float sm[];
   const int kvh = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
-  const int G = n_heads / n_kv;
+  const int G = GT ? GT : n_heads / n_kv;
   const int qd = n_heads * hd, kvd = n_kv * hd;
   const int pos = ri.pos[r], seq = ri.seq[r];
   const int len = pos + 1, t0 = sp * ATT_CHUNK, t1 = min(len, t0 + ATT_CHUNK);
@@ -167,22 +169,45 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[i];
   __syncthreads();
   const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
-  // scores: one thread per position, all G heads
-  for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
-    const float4* kt = reinterpret_cast<const float4*>(kc + (lbase + t) * kvd + kvh * hd);
-    for (int h = 0; h < G; ++h) {
-      const float4* qh = reinterpret_cast<const float4*>(qs + h * hd);
-      float s = 0.f;
-      for (int d = 0; d < hd / 4; ++d) {
-        const float4 a = kt[d], b = qh[d];
-        s += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+  const int n = t1 - t0;
+  // scores: one thread per position; the K row is read once, all G heads accumulate together
+  for (int tt = threadIdx.x; tt < n; tt += blockDim.x) {
+    const float4* kt = reinterpret_cast<const float4*>(kc + (lbase + t0 + tt) * kvd + kvh * hd);
+    if constexpr (GT > 0) {
+      float acc[GT];
+#pragma unroll
+      for (int h = 0; h < GT; ++h) acc[h] = 0.f;
+      for (int d4 = 0; d4 < hd / 4; d4 += 4) {
+        float4 k4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) k4[u] = kt[d4 + u];
+#pragma unroll
+        for (int h = 0; h < GT; ++h) {
+          const float4* qh = reinterpret_cast<const float4*>(qs + h * hd) + d4;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 b = qh[u];
+            acc[h] += k4[u].x * b.x + k4[u].y * b.y + k4[u].z * b.z + k4[u].w * b.w;
+          }
+        }
       }
-      sc[h * ATT_CHUNK + (t - t0)] = s * inv_sqrt_hd;
+#pragma unroll
+      for (int h = 0; h < GT; ++h) sc[h * ATT_CHUNK + tt] = acc[h] * inv_sqrt_hd;
+    } else {
+      for (int h = 0; h < G; ++h) {
+        const float4* qh = reinterpret_cast<const float4*>(qs + h * hd);
+        float s = 0.f;
+        for (int d = 0; d < hd / 4; ++d) {
+          const float4 a = kt[d], b = qh[d];
+          s += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+        }
+        sc[h * ATT_CHUNK + tt] = s * inv_sqrt_hd;
+      }
     }
   }
   __syncthreads();
-  // per head: local max and exp-sum (warp h%4 handles head h)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n = t1 - t0;
+  // per head: local max and exp-sum
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float hm[64], hl[64];
   for (int h = warp; h < G; h += ATT_THREADS / 32) {
     float m = -INFINITY;
@@ -202,18 +227,52 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     }
   }
   __syncthreads();
-  // acc[h][d] = sum_t p[h][t] * v[t][d]
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-    const int h = i / hd, d = i % hd;
-    const float* vt = vc + (lbase + t0) * kvd + kvh * hd + d;
-    const float* ph = sc + h * ATT_CHUNK;
-    float a = 0.f;
-    for (int t = 0; t < n; ++t) a += ph[t] * vt[(long long)t * kvd];
-    float* p = pr + (long long)h * nsplit * (hd + 2);
-    p[2 + d] = a;
-    if (d == 0) {
-      p[0] = hm[h];
-      p[1] = hl[h];
+  // acc[h][d] = sum_t p[h][t] v[t][d]: thread (slice, d) reads v[t][d] once for every head of the group;
+  // `slices` threads share a dimension and split the positions, then add through shared memory.
+  const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
+  const int dd = threadIdx.x % hd, sl = threadIdx.x / hd;
+  if constexpr (GT > 0) {
+    float acc[GT];
+#pragma unroll
+    for (int h = 0; h < GT; ++h) acc[h] = 0.f;
+    if (sl < slices && dd < hd) {
+      const float* vt = vc + (lbase + t0) * kvd + kvh * hd + dd;
+      for (int t = sl; t < n; t += slices) {
+        const float v = vt[(long long)t * kvd];
+#pragma unroll
+        for (int h = 0; h < GT; ++h) acc[h] += sc[h * ATT_CHUNK + t] * v;
+      }
+    }
+    __syncthreads();
+    float* red = sc;  // reuse the score buffer: [slices][GT][hd]
+    if (sl < slices && dd < hd)
+#pragma unroll
+      for (int h = 0; h < GT; ++h) red[(sl * GT + h) * hd + dd] = acc[h];
+    __syncthreads();
+    for (int i = threadIdx.x; i < GT * hd; i += blockDim.x) {
+      const int h = i / hd, d = i % hd;
+      float a = 0.f;
+      for (int z = 0; z < slices; ++z) a += red[(z * GT + h) * hd + d];
+      float* p = pr + (long long)h * nsplit * (hd + 2);
+      p[2 + d] = a;
+      if (d == 0) {
+        p[0] = hm[h];
+        p[1] = hl[h];
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+      const int h = i / hd, d = i % hd;
+      const float* vt = vc + (lbase + t0) * kvd + kvh * hd + d;
+      const float* ph = sc + h * ATT_CHUNK;
+      float a = 0.f;
+      for (int t = 0; t < n; ++t) a += ph[t] * vt[(long long)t * kvd];
+      float* p = pr + (long long)h * nsplit * (hd + 2);
+      p[2 + d] = a;
+      if (d == 0) {
+        p[0] = hm[h];
+        p[1] = hl[h];
+      }
     }
   }
 }
@@ -716,11 +775,25 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   if ((e = pdl_launch(rope_kv_kernel, dim3(R), dim3(256), 0, st, s->qkv, s->kc, s->vc, ri, l, c.n_layers, c.max_seq,
                       H, KV, hd, c.rope_base)))
     return e;
-  const size_t asmem = (size_t)G * (hd + ATT_CHUNK) * 4;
-  if ((e = pdl_launch(attn_partial_kernel, dim3(KV, R, s->nsplit), dim3(ATT_THREADS), asmem, st,
-                      (const float*)s->qkv, (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq,
-                      H, KV, hd, s->part, s->nsplit)))
-    return e;
+  // shared: q [G][hd] + scores [G][CHUNK]; the PV reduction reuses the score area ([slices][G][hd])
+  const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
+  const size_t asmem = (size_t)(G * hd + std::max(G * ATT_CHUNK, slices * G * hd)) * 4;
+  const dim3 agrid(KV, R, s->nsplit);
+  switch (hd <= ATT_THREADS && hd % 16 == 0 ? G : 0) {  // register path needs hd <= 128, hd % 16 == 0
+#define VTB_ATT(g)                                                                                               \
+  case g:                                                                                                      \
+    e = pdl_launch(attn_partial_kernel<g>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,             \
+                   (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,     \
+                   s->nsplit);                                                                                 \
+    break;
+    VTB_ATT(1) VTB_ATT(2) VTB_ATT(4) VTB_ATT(8)
+#undef VTB_ATT
+    default:
+      e = pdl_launch(attn_partial_kernel<0>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,
+                     (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,
+                     s->nsplit);
+  }
+  if (e) return e;
   if ((e = pdl_launch(attn_combine_kernel, dim3(H, R), dim3(128), 0, st, (const float*)s->part, s->att, H, hd,
                       s->nsplit)))
     return e;
