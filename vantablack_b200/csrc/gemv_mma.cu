@@ -54,8 +54,11 @@ struct XShared {
 
 // Each warp converts 4 sub-blocks per float4 load (8 lanes per sub-block) and
 // keeps up to 8 loads in flight, so the prologue costs about one L2 round trip.
+// With `nw` (an RMSNorm weight), x is replaced by (x * nw) * inv where
+// inv = 1 / sqrt(mean(x^2) + eps): the layer's rmsNorm (math.zig:11-32)
+// fused into the GEMV that consumes it.  `inv` is computed by the caller.
 __device__ __forceinline__ void build_x_shared(const float* __restrict__ x, int K, XShared xsh, int warp, int lane,
-                                               int nwarps) {
+                                               int nwarps, const float* __restrict__ nw, float inv) {
   const int n4 = K / 128;  // groups of 4 sub-blocks
   const int sub = lane >> 3, part = lane & 7;
   for (int base = warp; base < n4; base += nwarps * 8) {
@@ -63,7 +66,13 @@ __device__ __forceinline__ void build_x_shared(const float* __restrict__ x, int 
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int gi = base + u * nwarps;
-      if (gi < n4) v[u] = __ldg(reinterpret_cast<const float4*>(x + gi * 128) + lane);
+      if (gi < n4) {
+        v[u] = __ldg(reinterpret_cast<const float4*>(x + gi * 128) + lane);
+        if (nw) {
+          const float4 wv = __ldg(reinterpret_cast<const float4*>(nw + gi * 128) + lane);
+          v[u] = make_float4((v[u].x * wv.x) * inv, (v[u].y * wv.y) * inv, (v[u].z * wv.z) * inv, (v[u].w * wv.w) * inv);
+        }
+      }
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -116,7 +125,7 @@ struct MmaQ4K {
 template <int WARPS, int S, int CHB>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
-                    int ksplit, int accumulate) {
+                    int ksplit, int accumulate, const float* __restrict__ norm_w, float eps) {
   using C = MmaQ4K<CHB>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -165,7 +174,22 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
   for (int tt = 0; tt < min(S, ntiles); ++tt) issue(tt);
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  build_x_shared(x, K, xsh, warp, lane, WARPS);
+  float inv = 1.f;
+  if (norm_w) {  // sum of squares of the whole row (every CTA; x is L2-resident)
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < K / 4; i += WARPS * 32) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(x) + i);
+      ss += (a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < WARPS; ++w) t += red[w];
+    inv = 1.0f / sqrtf(t / (float)K + eps);
+    __syncthreads();
+  }
+  build_x_shared(x, K, xsh, warp, lane, WARPS, norm_w, inv);
   __syncthreads();
   asm volatile("griddepcontrol.launch_dependents;");
 
@@ -269,7 +293,7 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
 
 template <int WARPS, int S, int CHB>
 static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                    int accumulate) {
+                                    int accumulate, const float* norm_w, float eps) {
   auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB>;
   const int smem = WARPS * S * MmaQ4K<CHB>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
@@ -307,12 +331,12 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, y, m, k, ksplit, accumulate);
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, y, m, k, ksplit, accumulate, norm_w, eps);
 }
 
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                int accumulate) {
-  return launch_q4k_mma_t<8, 2, 2>(w, x, y, m, k, st, pdl, accumulate);
+                                int accumulate, const float* norm_w = nullptr, float eps = 0.f) {
+  return launch_q4k_mma_t<8, 2, 2>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
 }
 
 }  // namespace vtb

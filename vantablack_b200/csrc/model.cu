@@ -30,7 +30,7 @@ namespace vtb {
 cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                         int accumulate);
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                int accumulate);
+                                int accumulate, const float* norm_w, float eps);
 cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* out, int dim, int n_tok,
                          cudaStream_t st);
 cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
@@ -50,7 +50,7 @@ __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ t, l
 
 static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
                             int accumulate) {
-  if (q == Q4_K) return launch_gemv_q4k_mma(w, x, y, m, k, st, true, accumulate);
+  if (q == Q4_K) return launch_gemv_q4k_mma(w, x, y, m, k, st, true, accumulate, nullptr, 0.f);
   return launch_gemv(q, w, x, y, m, k, st, true, accumulate);
 }
 
@@ -738,8 +738,14 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   cudaStream_t st = s->st;
   cudaError_t e;
   RowInfo ri{s->seq, s->pos};
-  if ((e = enqueue_norm(s, L.attn_norm, 0, R))) return e;
   const bool gemm = R >= GEMM_MIN_ROWS;
+  // RMSNorm fused into a Q4_K GEMV's activation prologue when nothing is pending in tmp.
+  auto fused_norm_gemv = [&](const float* nw, int q, const uint8_t* w, float* out, int mm) -> bool {
+    if (gemm || s->pending || q != Q4_K || !w) return false;
+    for (int r = 0; r < R && e == cudaSuccess; ++r)
+      e = launch_gemv_q4k_mma(w, s->x + (size_t)r * d, out + (size_t)r * mm, mm, d, st, true, 0, nw, c.rms_eps);
+    return true;
+  };
   auto proj = [&](int q, const uint8_t* w, const float* in, float* out, int mm, int k, int ld_out, int acc) -> cudaError_t {
     // out[r*ld_out + i] (+)= W . in[r]; GEMM rows need a dense out, so `acc` goes through tmp
     if (gemm && k % 64 == 0 && (acc || ld_out == mm)) {
@@ -765,7 +771,12 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
     if (e2) return e2;
     return allreduce_tmp(s, (size_t)R * d);
   };
-  if (L.qkv) {
+  e = cudaSuccess;
+  if (fused_norm_gemv(L.attn_norm, L.q_q, L.qkv, s->qkv, qkvw)) {
+    if (e) return e;
+  } else if ((e = enqueue_norm(s, L.attn_norm, 0, R))) {
+    return e;
+  } else if (L.qkv) {
     if ((e = proj(L.q_q, L.qkv, s->xb, s->qkv, qkvw, d, qkvw, 0))) return e;
   } else {
     if ((e = proj(L.q_q, L.q, s->xb, s->qkv, qd, d, qkvw, 0))) return e;
@@ -798,8 +809,11 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
                       s->nsplit)))
     return e;
   if ((e = residual(L.q_o, L.o, s->att, qd))) return e;  // x += W_o . att (addInto fused)
-  if ((e = enqueue_norm(s, L.ffn_norm, 0, R))) return e;
-  if (L.gu) {
+  if (fused_norm_gemv(L.ffn_norm, L.q_gate, L.gu, s->gu, 2 * f)) {
+    if (e) return e;
+  } else if ((e = enqueue_norm(s, L.ffn_norm, 0, R))) {
+    return e;
+  } else if (L.gu) {
     if ((e = proj(L.q_gate, L.gu, s->xb, s->gu, 2 * f, d, 2 * f, 0))) return e;
   } else {
     if ((e = proj(L.q_gate, L.gate, s->xb, s->gu, f, d, 2 * f, 0))) return e;
