@@ -145,7 +145,11 @@ template <int GT>  // GT: compile-time group size, or 0 for the generic path
 __global__ void __launch_bounds__(ATT_THREADS)
 attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
                     RowInfo ri, int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd,
-                    float* __restrict__ part, int nsplit) {
+                    float* __restrict__ part, int nsplit, float* __restrict__ kcw, float* __restrict__ vcw,
+                    float rope_base) {
+  // kcw / vcw non-null: decode step with RoPE + KV write fused in (rope_kv_kernel's
+  // work): q is rotated in shared memory, and the split that holds the row's
+  // position rotates its K, writes K and V to the cache, then reads them back.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ float sm[];
   const int kvh = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
@@ -169,6 +173,38 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[i];
   __syncthreads();
   const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
+  if (kcw) {
+    const float pos_f = (float)pos;
+    const int half = hd / 2;
+    for (int p = threadIdx.x; p < G * half; p += blockDim.x) {  // rope (math.zig:88-104) on q in smem
+      const int h = p / half, i = 2 * (p % half);
+      const float inv_freq = 1.0f / powf(rope_base, (float)i / (float)hd);
+      const float theta = pos_f * inv_freq;
+      const float c = cosf(theta), sn = sinf(theta);
+      float* ptr = qs + h * hd + i;
+      const float x0 = ptr[0], x1 = ptr[1];
+      const float a = x0 * c, b = x1 * sn, pp = x0 * sn, qq = x1 * c;
+      ptr[0] = a - b;
+      ptr[1] = pp + qq;
+    }
+    if (sp == pos / ATT_CHUNK) {  // this split owns position `pos`: write its K (rotated) and V
+      const float* kr = qkv + (long long)r * (qd + 2 * kvd) + qd + kvh * hd;
+      const float* vr = kr + kvd;
+      const long long slot = (lbase + pos) * kvd + kvh * hd;
+      for (int p = threadIdx.x; p < half; p += blockDim.x) {
+        const int i = 2 * p;
+        const float inv_freq = 1.0f / powf(rope_base, (float)i / (float)hd);
+        const float theta = pos_f * inv_freq;
+        const float c = cosf(theta), sn = sinf(theta);
+        const float x0 = kr[i], x1 = kr[i + 1];
+        const float a = x0 * c, b = x1 * sn, pp = x0 * sn, qq = x1 * c;
+        kcw[slot + i] = a - b;
+        kcw[slot + i + 1] = pp + qq;
+      }
+      for (int i = threadIdx.x; i < hd; i += blockDim.x) vcw[slot + i] = vr[i];
+    }
+    __syncthreads();  // block-wide: the cache writes above are visible to this CTA's reads below
+  }
   const int n = t1 - t0;
   // scores: one thread per position; the K row is read once, all G heads accumulate together
   for (int tt = threadIdx.x; tt < n; tt += blockDim.x) {
@@ -399,6 +435,7 @@ struct VtbCudaState {
   int nsplit;
   float* logits_local;      // [rows][V] LM-head slice under tensor parallelism
   bool pending = false;     // tmp holds an all-reduced partial still to be added to x
+  bool decode_rows = false; // staged rows are distinct sequences (decode), not one prompt (prefill)
   cudaGraphExec_t graph = nullptr;
   int graph_rows = -1;
 };
@@ -682,6 +719,10 @@ static int stage_rows(VtbCudaState* s, int rows, const int32_t* tok, const int32
   }
   s->rows = rows;
   s->pending = false;
+  s->decode_rows = true;
+  for (int r = 1; r < rows && s->decode_rows; ++r)
+    for (int q = 0; q < r; ++q)
+      if (seq[q] == seq[r]) { s->decode_rows = false; break; }
   return VTB_CUDA_OK;
 }
 
@@ -783,9 +824,15 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
     if ((e = proj(L.q_k, L.k, s->xb, s->qkv + qd, kvd, d, qkvw, 0))) return e;
     if ((e = proj(L.q_v, L.v, s->xb, s->qkv + qd + kvd, kvd, d, qkvw, 0))) return e;
   }
-  if ((e = pdl_launch(rope_kv_kernel, dim3(R), dim3(256), 0, st, s->qkv, s->kc, s->vc, ri, l, c.n_layers, c.max_seq,
-                      H, KV, hd, c.rope_base)))
+  // Decode rows are distinct sequences: each row's new K/V is read only by its
+  // own attention, so RoPE + the cache write fold into the attention kernel.
+  // Prefill rows of one sequence read each other's K/V: separate kernel first.
+  const bool fuse_rope = s->decode_rows;
+  if (!fuse_rope && (e = pdl_launch(rope_kv_kernel, dim3(R), dim3(256), 0, st, s->qkv, s->kc, s->vc, ri, l, c.n_layers,
+                                    c.max_seq, H, KV, hd, c.rope_base)))
     return e;
+  float* kcw = fuse_rope ? s->kc : nullptr;
+  float* vcw = fuse_rope ? s->vc : nullptr;
   // shared: q [G][hd] + scores [G][CHUNK]; the PV reduction reuses the score area ([slices][G][hd])
   const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
   const size_t asmem = (size_t)(G * hd + std::max(G * ATT_CHUNK, slices * G * hd)) * 4;
@@ -795,14 +842,14 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   case g:                                                                                                      \
     e = pdl_launch(attn_partial_kernel<g>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,             \
                    (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,     \
-                   s->nsplit);                                                                                 \
+                   s->nsplit, kcw, vcw, c.rope_base);                                                          \
     break;
     VTB_ATT(1) VTB_ATT(2) VTB_ATT(4) VTB_ATT(8)
 #undef VTB_ATT
     default:
       e = pdl_launch(attn_partial_kernel<0>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,
                      (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,
-                     s->nsplit);
+                     s->nsplit, kcw, vcw, c.rope_base);
   }
   if (e) return e;
   if ((e = pdl_launch(attn_combine_kernel, dim3(H, R), dim3(128), 0, st, (const float*)s->part, s->att, H, hd,
