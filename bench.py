@@ -378,10 +378,11 @@ def run_profile_case(case: str) -> None:
         acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
         for _ in range(2):
             ops.gemm(Q4_K, w, acts, m, k, precise=False)
-    elif case == "decode":  # TinyLlama architecture: 128-token prefill + 5 decode steps
-        from vantablack_b200.model import TINYLLAMA, Context, CudaModel, CudaState, HostWeights
+    elif case in ("decode", "decode8b"):  # 128-token prefill + 5 decode steps (TinyLlama / Llama-3-8B)
+        from vantablack_b200.model import LLAMA3_8B, TINYLLAMA, Context, CudaModel, CudaState, HostWeights
         ctx = Context(0)
-        st = CudaState(CudaModel(ctx, HostWeights(TINYLLAMA, seed=1)), 1, max_rows=128)
+        cfg = TINYLLAMA if case == "decode" else LLAMA3_8B
+        st = CudaState(CudaModel(ctx, HostWeights(cfg, seed=1)), 1, max_rows=128)
         st.prefill(np.arange(3, 131))
         for i in range(5):
             st.step([5 + i], want_logits=False)
@@ -400,7 +401,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--model-steps", type=int, default=32, help="decode steps of the 8B model metrics (0 = skip)")
-    ap.add_argument("--profile", choices=["gemv", "gemm", "decode"], help="run a small case for ncu and exit")
+    ap.add_argument("--profile", choices=["gemv", "gemm", "decode", "decode8b"], help="run a small case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)

@@ -137,7 +137,7 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, float* __restrict__ kc, 
 // Split-K ("flash decode"): CTA (kv_head, row, split) handles positions
 // [split*CHUNK, ...) for the GQA group of q heads that share the kv head,
 // and writes a partial (max, sum, acc[hd]) per q head; attn_combine merges.
-constexpr int ATT_CHUNK = 128;
+constexpr int ATT_CHUNK = 64;
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_GMAX = 8;  // GQA group sizes up to 8 keep their accumulators in registers
 
@@ -213,6 +213,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
       float acc[GT];
 #pragma unroll
       for (int h = 0; h < GT; ++h) acc[h] = 0.f;
+#pragma unroll 2
       for (int d4 = 0; d4 < hd / 4; d4 += 4) {
         float4 k4[4];
 #pragma unroll
@@ -273,7 +274,17 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     for (int h = 0; h < GT; ++h) acc[h] = 0.f;
     if (sl < slices && dd < hd) {
       const float* vt = vc + (lbase + t0) * kvd + kvh * hd + dd;
-      for (int t = sl; t < n; t += slices) {
+      int t = sl;
+      for (; t + 3 * slices < n; t += 4 * slices) {  // four independent loads in flight
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = vt[(long long)(t + u * slices) * kvd];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int h = 0; h < GT; ++h) acc[h] += sc[h * ATT_CHUNK + t + u * slices] * v[u];
+      }
+      for (; t < n; t += slices) {
         const float v = vt[(long long)t * kvd];
 #pragma unroll
         for (int h = 0; h < GT; ++h) acc[h] += sc[h * ATT_CHUNK + t] * v;
