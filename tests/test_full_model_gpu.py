@@ -22,3 +22,45 @@ def test_tinyllama_prompt128_decode256_greedy_identical():
     first_diff = next((i for i, (a, b) in enumerate(zip(ids, ids_ref)) if a != b), None)
     assert first_diff is None, f"first differing decode step: {first_diff}"
     assert float(np.abs(lg - lg_ref).max() / np.abs(lg_ref).max()) <= 1e-3
+
+
+def test_llama3_8b_greedy_identical():
+    """BASELINE config 5 architecture (Llama-3-8B, Q4_K_M-style, random init)
+    on one GPU.  Default: 256-token prefill + 32 greedy steps; with
+    VTB_FULL_8B=1 the configured 2048-token prefill + 512 steps (slow on the
+    CPU oracle)."""
+    import os
+    from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState
+    full = os.environ.get("VTB_FULL_8B") == "1"
+    n_prompt, n_gen = (2048, 512) if full else (256, 32)
+    O.set_threads(os.cpu_count() or 16)
+    w = HostWeights(LLAMA3_8B, seed=5)
+    prompt = np.random.default_rng(55).integers(3, LLAMA3_8B.vocab_size, n_prompt)
+    ctx = Context(0)
+    st = CudaState(CudaModel(ctx, w), 1, max_rows=n_prompt)
+    ids, lg = st.generate_greedy(prompt, n_gen, use_prefill=True)
+    ids_ref, lg_ref = O.Model(w).generate_greedy(prompt, n_gen, use_prefill=True)
+    first_diff = next((i for i, (a, b) in enumerate(zip(ids, ids_ref)) if a != b), None)
+    assert first_diff is None, f"first differing decode step: {first_diff}"
+    assert float(np.abs(lg - lg_ref).max() / np.abs(lg_ref).max()) <= 1e-3
+
+
+def test_llama3_8b_batch32_subset():
+    """Batch-32 decode of the 8B architecture: all 32 sequences for the first
+    steps, two of them checked against independent oracle runs."""
+    import os
+    from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState
+    O.set_threads(os.cpu_count() or 16)
+    w = HostWeights(LLAMA3_8B, seed=6)
+    rng = np.random.default_rng(66)
+    toks = rng.integers(3, LLAMA3_8B.vocab_size, 32)
+    st = CudaState(CudaModel(Context(0), w), 32, max_rows=32)
+    refs = {0: O.Model(w), 17: O.Model(w)}
+    ref_tok = {s: int(toks[s]) for s in refs}
+    for step in range(6):
+        _, am = st.step(toks, want_logits=False)
+        for s, ref in refs.items():
+            nxt = O.argmax(ref.step(ref_tok[s]))
+            assert int(am[s]) == nxt, f"sequence {s} step {step}"
+            ref_tok[s] = nxt
+        toks = am

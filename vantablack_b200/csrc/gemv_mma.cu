@@ -255,8 +255,10 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int mt = i >> 1, e = (i & 1) * 2;
-            const float lo = (float)E[mt][e] * (1.0f / 254.0f) + (float)E[mt][e + 1] * (1.0f / 64516.0f);
-            const float sq = ((float)D[mt][e] + ((float)D[mt][e + 1] + lo) * (1.0f / 254.0f)) * fx;  // sum_k q_k x_k
+            // limbs combined exactly in int32 (|D0*254 + D1| < 2^27), then converted once
+            const float hi = (float)(D[mt][e] * 254 + D[mt][e + 1]);
+            const float lo = (float)(E[mt][e] * 254 + E[mt][e + 1]);
+            const float sq = (hi + lo * (1.0f / 64516.0f)) * (fx * (1.0f / 254.0f));  // sum_k q_k x_k
             const uint4 hh = hd[i];
             const unsigned yb = (hh.y >> (8 * t)) & 0xffu, zb = (hh.z >> (8 * t)) & 0xffu;
             unsigned sc, mn;
