@@ -22,6 +22,11 @@
 //    the reference (greedy token identity).
 // Every wait is bounded; a timeout sets the device error word, and all warps
 // still reach the TMEM dealloc.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
 #include "common.cuh"
 
 namespace vtb {
@@ -67,26 +72,34 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int chunk) {  // byte offse
 // ---- bit-exact dequantization of 64 consecutive weights [k0, k0+64) of one row ----
 __device__ __forceinline__ uint32_t ldg_u32(const uint8_t* p) { return __ldg(reinterpret_cast<const uint32_t*>(p)); }
 // 4-byte words from a 2-byte-aligned global address
-template <int NW>
+template <int NW, bool SMEM = false>
 __device__ __forceinline__ void ldg_words_a2(const uint8_t* p, uint32_t* out) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(p);
   const uint8_t* b = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
   const unsigned sh = (unsigned)(a & 3) * 8u;
   uint32_t w[NW + 1];
 #pragma unroll
-  for (int i = 0; i <= NW; ++i) w[i] = ldg_u32(b + 4 * i);
+  for (int i = 0; i <= NW; ++i) w[i] = SMEM ? *reinterpret_cast<const uint32_t*>(b + 4 * i) : ldg_u32(b + 4 * i);
 #pragma unroll
   for (int i = 0; i < NW; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }
 __device__ __forceinline__ unsigned byte_of(const uint32_t* w, int i) { return (w[i >> 2] >> (8 * (i & 3))) & 0xffu; }
 
-template <int Q>
+// SMEM: `blk` points into shared memory (TMA-staged super-block), read with
+// generic loads; otherwise it is global memory, read through the read-only path.
+template <bool SMEM>
+__device__ __forceinline__ uint4 ld16(const uint8_t* p) {
+  if constexpr (SMEM) return *reinterpret_cast<const uint4*>(p);
+  else return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+template <int Q, bool SMEM = false>
 __device__ __forceinline__ void dequant64(const uint8_t* row, int k0, float* v) {
   if constexpr (Q == Q4_K || Q == Q5_K) {
     constexpr int BB = Q == Q4_K ? 144 : 176;
-    const uint8_t* blk = row + (k0 >> 8) * BB;
+    const uint8_t* blk = SMEM ? row : row + (k0 >> 8) * BB;  // SMEM: `row` is the staged super-block itself
     const int j = (k0 & 255) >> 6;  // sub-block pair: sub-blocks 2j, 2j+1
-    const uint4 h = __ldg(reinterpret_cast<const uint4*>(blk));
+    const uint4 h = ld16<SMEM>(blk);
     const float d = h2f((uint16_t)(h.x & 0xffffu)), dmin = h2f((uint16_t)(h.x >> 16));
     const uint32_t sw[3] = {h.y, h.z, h.w};
     unsigned sc[2], mn[2];
@@ -104,11 +117,11 @@ __device__ __forceinline__ void dequant64(const uint8_t* row, int k0, float* v) 
     const float d2 = __fmul_rn(d, (float)sc[1]), m2 = __fmul_rn(dmin, (float)mn[1]);
     const uint8_t* qs = blk + (Q == Q4_K ? 16 : 48) + 32 * j;
     uint32_t q[8];
-    const uint4 qa = __ldg(reinterpret_cast<const uint4*>(qs)), qb = __ldg(reinterpret_cast<const uint4*>(qs + 16));
+    const uint4 qa = ld16<SMEM>(qs), qb = ld16<SMEM>(qs + 16);
     q[0] = qa.x; q[1] = qa.y; q[2] = qa.z; q[3] = qa.w; q[4] = qb.x; q[5] = qb.y; q[6] = qb.z; q[7] = qb.w;
     uint32_t qh[8];
     if constexpr (Q == Q5_K) {
-      const uint4 ha = __ldg(reinterpret_cast<const uint4*>(blk + 16)), hb = __ldg(reinterpret_cast<const uint4*>(blk + 32));
+      const uint4 ha = ld16<SMEM>(blk + 16), hb = ld16<SMEM>(blk + 32);
       qh[0] = ha.x; qh[1] = ha.y; qh[2] = ha.z; qh[3] = ha.w; qh[4] = hb.x; qh[5] = hb.y; qh[6] = hb.z; qh[7] = hb.w;
     }
 #pragma unroll
@@ -122,14 +135,15 @@ __device__ __forceinline__ void dequant64(const uint8_t* row, int k0, float* v) 
       v[32 + l] = __fsub_rn(__fmul_rn(d2, (float)hi), m2);
     }
   } else if constexpr (Q == Q6_K) {
-    const uint8_t* blk = row + (k0 >> 8) * 210;
+    const uint8_t* blk = SMEM ? row : row + (k0 >> 8) * 210;
     const int half = (k0 & 255) >> 7, nb = ((k0 & 127) >> 6) * 2;  // n in {nb, nb+1}
     uint32_t ql[16], qh[8], sc[2];
-    ldg_words_a2<16>(blk + half * 64, ql);
-    ldg_words_a2<8>(blk + 128 + half * 32, qh);
-    ldg_words_a2<2>(blk + 192 + half * 8, sc);
-    const float d = h2f((uint16_t)(ldg_u32(reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(blk + 208) & ~uintptr_t(3))) >>
-                                   ((reinterpret_cast<uintptr_t>(blk + 208) & 3) * 8)));
+    ldg_words_a2<16, SMEM>(blk + half * 64, ql);
+    ldg_words_a2<8, SMEM>(blk + 128 + half * 32, qh);
+    ldg_words_a2<2, SMEM>(blk + 192 + half * 8, sc);
+    uint32_t dw[1];
+    ldg_words_a2<1, SMEM>(blk + 208, dw);
+    const float d = h2f((uint16_t)(dw[0] & 0xffffu));
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int n = nb + u;
@@ -173,36 +187,91 @@ __global__ void acts_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* 
   asm volatile("griddepcontrol.launch_dependents;");
 }
 
-template <int Q, int BN, int PASSES, int S>
+// ---------------- tensor maps (TMA descriptors) ----------------
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D map of a [rows][inner] array (inner contiguous, row pitch in bytes).
+static bool make_tmap(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+                      uint64_t pitch, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+  auto fn = tmap_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {pitch};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// TMA_A: raw weight super-blocks arrive by 2-D TMA (Q4_K / Q5_K: 16-byte
+// multiples); otherwise producers read them from global memory directly.
+// Q6_K super-blocks (210 B) start on 2-byte boundaries: the box covers 240 B
+// from the 16-byte boundary at or below the super-block (TMA's x alignment rule).
+template <int Q>
+struct TmaA {
+  static constexpr int BOX = Q == Q6_K ? 240 : Fmt<Q>::bytes;  // one super-block of one row (+ lead)
+  __host__ __device__ static constexpr int x0(int j) { return Q == Q6_K ? (j * 210) & ~15 : j * Fmt<Q>::bytes; }
+};
+
+template <int Q, int BN, int PASSES, int S, bool TA>
 struct TcCfg {
   static constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KiB
   static constexpr int B_BYTES = BN * TC_BK * 2;
   static constexpr int NOPS = PASSES == 1 ? 1 : 2;    // hi only, or hi + lo
   static constexpr int STAGE = NOPS * (A_BYTES + B_BYTES);
-  static constexpr int SMEM = S * STAGE + 1024 /*align*/ + 256 /*barriers + tmem slot*/;
+  static constexpr int SR = 3;                          // raw weight super-block stages
+  static constexpr int RAW = TA ? TC_BM * TmaA<Q>::BOX : 0;
+  static constexpr int SMEM = S * STAGE + SR * RAW + 1024 /*align*/ + 512 /*barriers + tmem slot*/;
 };
 
-template <int Q, int BN, int PASSES, int S>
-__global__ void __launch_bounds__(160, 1)
-gemm_tc_kernel(const uint8_t* __restrict__ W, const __nv_bfloat16* __restrict__ xh, const __nv_bfloat16* __restrict__ xl,
-               float* __restrict__ out, int M, int K, int NB) {
-  using C = TcCfg<Q, BN, PASSES, S>;
+// Warps 0-3 dequantize (thread = tile row), warp 4 lane 0 issues MMAs,
+// warp 5 lane 0 issues the TMA loads.
+template <int Q, int BN, int PASSES, int S, bool TA>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapBh,
+               const __grid_constant__ CUtensorMap mapBl, const uint8_t* __restrict__ W, float* __restrict__ out,
+               int M, int K, int NB) {
+  using C = TcCfg<Q, BN, PASSES, S, TA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE);
+  uint8_t* raw = smem + S * C::STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(raw + C::SR * C::RAW);
   uint64_t* empty = full + S;
-  uint64_t* done = empty + S;
+  uint64_t* rfull = empty + S;
+  uint64_t* rempty = rfull + C::SR;
+  uint64_t* done = rempty + C::SR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int m0 = blockIdx.x * TC_BM, n0 = blockIdx.y * BN;
-  const int nk = K / TC_BK;
+  const int nk = K / TC_BK, nsb = K / 256;
   const long long rb = host_row_bytes_dev<Q>(K);
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], TC_PROD);
+      mbar_init(&full[s], TC_PROD + 1);  // every dequant thread + the TMA thread (B bytes)
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < C::SR; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], TC_PROD);
     }
     mbar_init(done, 1);
     fence_mbar_init();
@@ -218,31 +287,50 @@ gemm_tc_kernel(const uint8_t* __restrict__ W, const __nv_bfloat16* __restrict__ 
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
-
-  if (warp < 4) {
-    // ---------------- producers ----------------
-    const int r = tid;  // tile row
+  if (warp == 5) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      constexpr unsigned BBYTES = (unsigned)C::B_BYTES * (PASSES == 3 ? 2u : 1u);
+      int jr = 0;  // next raw weight super-block
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        if constexpr (TA) {  // weights run up to SR - 1 super-blocks ahead (independent of the activations)
+          while (jr < nsb && jr <= kb / 4 + C::SR - 1 && ok) {
+            const int rs = jr % C::SR;
+            if (jr >= C::SR && !mbar_wait_bounded(&rempty[rs], (unsigned)(((jr / C::SR) - 1) & 1))) { ok = false; break; }
+            mbar_expect_tx(&rfull[rs], (unsigned)C::RAW);
+            tma_load_2d(raw + rs * C::RAW, &mapA, TmaA<Q>::x0(jr), m0, &rfull[rs]);
+            ++jr;
+          }
+        }
+        if (kb == 0) asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
+        const int s = kb % S;
+        if (kb >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((kb / S) - 1) & 1))) { ok = false; break; }
+        uint8_t* st = smem + s * C::STAGE;
+        mbar_expect_tx(&full[s], BBYTES);
+        tma_load_2d(st + C::A_BYTES, &mapBh, kb * TC_BK, n0, &full[s]);
+        if constexpr (PASSES == 3) tma_load_2d(st + 2 * C::A_BYTES + C::B_BYTES, &mapBl, kb * TC_BK, n0, &full[s]);
+      }
+    }
+  } else if (warp < 4) {
+    // ---------------- dequantizers (thread = tile row) ----------------
+    const int r = tid;
     const bool row_ok = m0 + r < M;
     const uint8_t* wrow = W + (long long)(row_ok ? m0 + r : 0) * rb;
     for (int kb = 0; kb < nk && ok; ++kb) {
-      const int s = kb % S;
+      const int s = kb % S, j = kb >> 2;
+      if constexpr (TA) {
+        if ((kb & 3) == 0 && !mbar_wait_bounded(&rfull[j % C::SR], (unsigned)((j / C::SR) & 1))) { ok = false; break; }
+      }
       if (kb >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((kb / S) - 1) & 1))) { ok = false; break; }
       uint8_t* st = smem + s * C::STAGE;
-      const uint32_t a_hi = smem_u32(st), b_hi = a_hi + C::A_BYTES;
-      const uint32_t a_lo = b_hi + C::B_BYTES, b_lo = a_lo + C::A_BYTES;
-      // B tile (activations): BN rows x 8 chunks of 16 B, zero-filled past NB
-      for (int i = tid; i < BN * 8; i += TC_PROD) {
-        const int n = i >> 3, c = i & 7;
-        const bool in = n0 + n < NB;
-        const long long off = (long long)(in ? n0 + n : 0) * K + kb * TC_BK + c * 8;
-        cp_async16(b_hi + sw128_off(n, c), xh + off, in ? 16u : 0u);
-        if constexpr (PASSES == 3) cp_async16(b_lo + sw128_off(n, c), xl + off, in ? 16u : 0u);
-      }
-      // A tile: this thread's row, 64 weights
       float v[64];
-      if (row_ok) dequant64<Q>(wrow, kb * TC_BK, v);
-      else {
+      if constexpr (TA) {  // this row's super-block sits at raw[j % SR] + r * BOX (out-of-range rows read as zeros)
+        dequant64<Q, true>(raw + (j % C::SR) * C::RAW + r * TmaA<Q>::BOX + (j * Fmt<Q>::bytes - TmaA<Q>::x0(j)),
+                           kb * TC_BK, v);
+        if ((kb & 3) == 3 || kb == nk - 1) mbar_arrive(&rempty[j % C::SR]);
+      } else if (row_ok) {
+        dequant64<Q>(wrow, kb * TC_BK, v);
+      } else {
 #pragma unroll
         for (int i = 0; i < 64; ++i) v[i] = 0.f;
       }
@@ -262,12 +350,11 @@ gemm_tc_kernel(const uint8_t* __restrict__ W, const __nv_bfloat16* __restrict__ 
           *reinterpret_cast<uint4*>(st + C::A_BYTES + C::B_BYTES + sw128_off(r, c)) = lv;
         }
       }
-      cp_async_wait_all();
       fence_async_smem();  // generic-proxy smem writes -> visible to the tensor core
       mbar_arrive(&full[s]);
     }
   } else if (lane == 0) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer (warp 4) ----------------
     const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
     for (int kb = 0; kb < nk && ok; ++kb) {
       const int s = kb % S;
@@ -310,8 +397,8 @@ gemm_tc_kernel(const uint8_t* __restrict__ W, const __nv_bfloat16* __restrict__ 
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         if (row < M) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + c0 + j < NB) out[(long long)(n0 + c0 + j) * M + row] = __uint_as_float(v[j]);
+          for (int jj = 0; jj < 32; ++jj)
+            if (n0 + c0 + jj < NB) out[(long long)(n0 + c0 + jj) * M + row] = __uint_as_float(v[jj]);
         }
       }
     }
@@ -325,20 +412,37 @@ gemm_tc_kernel(const uint8_t* __restrict__ W, const __nv_bfloat16* __restrict__ 
   }
 }
 
-template <int Q, int BN, int PASSES, int S>
+template <int Q, int BN, int PASSES, int S, bool TA>
 static cudaError_t launch_gemm_tc_t(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
                                     int k, int nb, cudaStream_t st) {
-  using C = TcCfg<Q, BN, PASSES, S>;
-  auto kern = gemm_tc_kernel<Q, BN, PASSES, S>;
+  using C = TcCfg<Q, BN, PASSES, S, TA>;
+  auto kern = gemm_tc_kernel<Q, BN, PASSES, S, TA>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr = true;
   }
+  CUtensorMap mA, mBh, mBl;
+  memset(&mA, 0, sizeof mA);
+  const uint64_t rbytes = (uint64_t)host_row_bytes_dev<Q>(k);
+  if (TA &&
+      !make_tmap(&mA, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, rbytes, (uint64_t)m, rbytes, TmaA<Q>::BOX, TC_BM,
+                 CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  if (!make_tmap(&mBh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xh, (uint64_t)k, (uint64_t)nb, (uint64_t)k * 2, TC_BK, BN,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (PASSES == 3) {
+    if (!make_tmap(&mBl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xl, (uint64_t)k, (uint64_t)nb, (uint64_t)k * 2, TC_BK, BN,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  } else {
+    mBl = mBh;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((m + TC_BM - 1) / TC_BM, (nb + BN - 1) / BN);
-  cfg.blockDim = dim3(160);
+  cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute a[1];
@@ -346,20 +450,48 @@ static cudaError_t launch_gemm_tc_t(const void* w, const __nv_bfloat16* xh, cons
   a[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = a;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, xh, xl, out, m, k, nb);
+  return cudaLaunchKernelEx(&cfg, kern, mA, mBh, mBl, (const uint8_t*)w, out, m, k, nb);
+}
+
+// Largest stage count (<= SMAX) whose shared memory fits the 227 KiB per-CTA limit.
+template <int Q, int BN, int PASSES, bool TA, int SMAX>
+constexpr int fit_stages() {
+  if constexpr (SMAX <= 1) return 1;
+  else if constexpr (TcCfg<Q, BN, PASSES, SMAX, TA>::SMEM <= 227 * 1024) return SMAX;
+  else return fit_stages<Q, BN, PASSES, TA, SMAX - 1>();
+}
+
+template <int Q, int BN, int PASSES, bool TA>
+static cudaError_t launch_fit(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m, int k,
+                              int nb, cudaStream_t st) {
+  constexpr int S = fit_stages<Q, BN, PASSES, TA, 5>();
+  static_assert(TcCfg<Q, BN, PASSES, S, TA>::SMEM <= 227 * 1024, "GEMM tile does not fit in shared memory");
+  return launch_gemm_tc_t<Q, BN, PASSES, S, TA>(w, xh, xl, out, m, k, nb, st);
+}
+
+template <int Q, bool TA>
+static cudaError_t launch_gemm_tc_qt(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
+                                     int k, int nb, bool precise, cudaStream_t st) {
+  if (precise) {  // hi + lo tiles: twice the shared memory per stage
+    if (nb <= 64) return launch_fit<Q, 64, 3, TA>(w, xh, xl, out, m, k, nb, st);
+    if (nb <= 128) return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, st);
+    if constexpr (TcCfg<Q, 256, 3, 2, TA>::SMEM <= 227 * 1024)
+      return launch_fit<Q, 256, 3, TA>(w, xh, xl, out, m, k, nb, st);
+    else
+      return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, st);
+  }
+  if (nb <= 64) return launch_fit<Q, 64, 1, TA>(w, xh, xl, out, m, k, nb, st);
+  if (nb <= 128) return launch_fit<Q, 128, 1, TA>(w, xh, xl, out, m, k, nb, st);
+  return launch_fit<Q, 256, 1, TA>(w, xh, xl, out, m, k, nb, st);
 }
 
 template <int Q>
 static cudaError_t launch_gemm_tc_q(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
                                     int k, int nb, bool precise, cudaStream_t st) {
-  if (precise) {
-    if (nb <= 64) return launch_gemm_tc_t<Q, 64, 3, 4>(w, xh, xl, out, m, k, nb, st);
-    if (nb <= 128) return launch_gemm_tc_t<Q, 128, 3, 3>(w, xh, xl, out, m, k, nb, st);
-    return launch_gemm_tc_t<Q, 256, 3, 2>(w, xh, xl, out, m, k, nb, st);
-  }
-  if (nb <= 64) return launch_gemm_tc_t<Q, 64, 1, 6>(w, xh, xl, out, m, k, nb, st);
-  if (nb <= 128) return launch_gemm_tc_t<Q, 128, 1, 4>(w, xh, xl, out, m, k, nb, st);
-  return launch_gemm_tc_t<Q, 256, 1, 4>(w, xh, xl, out, m, k, nb, st);
+  // TMA weight staging needs 16-byte row pitches (all K-quant configs with k % 2048 == 0 qualify)
+  const bool ta = (Q != Q8_0) && host_row_bytes_dev<Q>(k) % 16 == 0;
+  if (ta) return launch_gemm_tc_qt<Q, true>(w, xh, xl, out, m, k, nb, precise, st);
+  return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, st);
 }
 
 // out[nb][m] = acts[nb][k] . W^T.  `ws` is bf16 scratch of nb*k*(precise ? 2 : 1) elements.
