@@ -894,9 +894,13 @@ static cudaError_t enqueue_final(VtbCudaState* s, bool last_only) {
   const int r0 = last_only ? s->rows - 1 : 0, n = last_only ? 1 : s->rows;
   if ((e = enqueue_norm(s, m->out_norm, r0, n))) return e;
   float* lg = tp ? s->logits_local : s->logits;
-  for (int r = 0; r < n; ++r)
-    if ((e = gemv_any(m->q_out, m->out_w, s->xb + (size_t)r * c.dim, lg + (size_t)r * m->V, m->V, c.dim, st, 0)))
-      return e;
+  if (n >= GEMM_MIN_ROWS && c.dim % 64 == 0) {  // batch decode: one GEMM reads the LM head once for all rows
+    if ((e = launch_gemm_tc(m->q_out, m->out_w, s->xb, lg, m->V, c.dim, n, true, s->ws, st))) return e;
+  } else {
+    for (int r = 0; r < n; ++r)
+      if ((e = gemv_any(m->q_out, m->out_w, s->xb + (size_t)r * c.dim, lg + (size_t)r * m->V, m->V, c.dim, st, 0)))
+        return e;
+  }
   if (tp) {  // all-gather the vocabulary slices, one row at a time (rank slices are contiguous vocab ranges)
     ncclResult_t rr = ncclGroupStart();
     for (int r = 0; r < n && rr == ncclSuccess; ++r)
