@@ -211,12 +211,14 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
         const int sb = b0 + bi;
         const uint8_t* blk = base + bi * C::BB;
         uint4 hd[4];
-        float dd[4], dm[4];
+        float dd[4], dm[4], nd[4], nm[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           hd[i] = *reinterpret_cast<const uint4*>(blk + 8 * i * C::SLOT);
           dd[i] = h2f((uint16_t)(hd[i].x & 0xffffu));
           dm[i] = h2f((uint16_t)(hd[i].x >> 16));
+          nd[i] = -dd[i] * 8388608.f;  // exact: power-of-two scaling of an f16 value
+          nm[i] = -dm[i] * 8388608.f;
         }
 #pragma unroll
         for (int grp = 0; grp < 2; ++grp) {
@@ -268,7 +270,10 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
               const unsigned wb = (hh.w >> (8 * t)) & 0xffu;
               sc = (wb & 15u) | ((yb >> 6) << 4); mn = (wb >> 4) | ((zb >> 6) << 4);
             }
-            acc[i] += (dd[i] * (float)sc) * sq - (dm[i] * (float)mn) * xs.y;
+            // 6-bit sc/mn -> float exactly via the 2^23 magic (keeps the int->float unit free):
+          // d * sc = fma(d, 2^23 + sc, -d * 2^23)
+          const float fsc = __uint_as_float(0x4B000000u | sc), fmn = __uint_as_float(0x4B000000u | mn);
+          acc[i] += fmaf(dd[i], fsc, nd[i]) * sq - fmaf(dm[i], fmn, nm[i]) * xs.y;
           }
         }
       }
@@ -338,6 +343,11 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
 
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                 int accumulate, const float* norm_w = nullptr, float eps = 0.f) {
+  // Large matrices stream best with 16 single-stage warps per CTA (more
+  // independent bulk copies in flight per SM); small ones, where the chain of
+  // dependent launches dominates, with 8 double-buffered warps.
+  if ((long long)m * k >= (1LL << 24))
+    return launch_q4k_mma_t<16, 1, 2>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
   return launch_q4k_mma_t<8, 2, 2>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
 }
 
