@@ -22,12 +22,11 @@
 //    the reference (greedy token identity).
 // Every wait is bounded; a timeout sets the device error word, and all warps
 // still reach the TMEM dealloc.
-#include <cuda.h>
-#include <cudaTypedefs.h>
 
 #include <cstring>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace vtb {
 
@@ -185,39 +184,6 @@ __global__ void acts_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* 
     if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
   }
   asm volatile("griddepcontrol.launch_dependents;");
-}
-
-// ---------------- tensor maps (TMA descriptors) ----------------
-static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-// 2-D map of a [rows][inner] array (inner contiguous, row pitch in bytes).
-static bool make_tmap(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
-                      uint64_t pitch, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
-  auto fn = tmap_encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {inner, rows};
-  const cuuint64_t strides[1] = {pitch};
-  const cuuint32_t box[2] = {box_inner, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
 }
 
 // TMA_A: raw weight super-blocks arrive by 2-D TMA (Q4_K / Q5_K: 16-byte

@@ -25,18 +25,21 @@
 //    reference's w = d1*q - m1 (simd.zig:221-243) distributed over the
 //    sub-block.  fp32 accumulation; tolerance-checked (<= 1e-4).
 //
-// Data movement: persistent CTAs; each warp streams tiles of 32 rows x CHB
-// super-blocks HBM -> shared with 1-D bulk copies (one per row, no
-// multicast) into an S-stage mbarrier ring; the copies for the first S tiles
-// are issued before griddepcontrol.wait, so with programmatic dependent
-// launch they overlap the kernel that produces x.
+// Data movement: persistent CTAs; each warp streams tiles of 32 rows x one
+// super-block HBM -> shared as one 2-D TMA box (no multicast) into an S-stage
+// mbarrier ring; the copies for the first S tiles are issued before
+// griddepcontrol.wait, so with programmatic dependent launch they overlap the
+// kernel that produces x.
+#include <cstring>
+
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace vtb {
 
 __device__ __forceinline__ void imma16832(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -114,19 +117,25 @@ __device__ __forceinline__ void build_x_shared(const float* __restrict__ x, int 
   }
 }
 
-template <int CHB>
+// TM: the tile arrives as one 2-D TMA box (32 rows x one super-block, rows
+// dense at 144 B = 4 (mod 32) words, conflict-free); otherwise as one 1-D
+// bulk copy per row into rows padded to 12 (mod 32) words.  Per-row copies of
+// a few hundred bytes cap the stream near 5 TB/s on their issue rate alone;
+// one box per tile moves the same bytes with 32x fewer copy operations.
+template <int CHB, bool TM>
 struct MmaQ4K {
-  static constexpr int ROWS = 32;            // two m16 MMA tiles per warp tile
+  static constexpr int ROWS = 32;  // two m16 MMA tiles per warp tile
   static constexpr int BB = 144;
-  static constexpr int SLOT = CHB * BB + 16;  // +16 B: row stride = 12 (mod 32) words -> conflict-free LDS
+  static constexpr int SLOT = TM ? CHB * BB : CHB * BB + 16;
   static constexpr int STAGE = ROWS * SLOT;
+  static_assert(!TM || CHB == 1, "2-D TMA tiles hold one super-block per row");
 };
 
-template <int WARPS, int S, int CHB>
+template <int WARPS, int S, int CHB, bool TM>
 __global__ void __launch_bounds__(WARPS * 32, 1)
-gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
+gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
                     int ksplit, int accumulate, const float* __restrict__ norm_w, float eps) {
-  using C = MmaQ4K<CHB>;
+  using C = MmaQ4K<CHB, TM>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -164,12 +173,19 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
     const int c = kpart + ksplit * (tt % my_chunks), st = tt % S;
     const int b0 = c * CHB, nblk = min(CHB, nb - b0);
     const int r0 = u * C::ROWS, nr = max(0, min(C::ROWS, M - r0));
-    const unsigned bytes = (unsigned)(nblk * C::BB);
-    if (lane == 0) mbar_expect_tx(&bars[st], bytes * (unsigned)nr);
-    __syncwarp();
-    if (lane < nr)
-      bulk_g2s(ring + st * C::STAGE + lane * C::SLOT, W + (long long)(r0 + lane) * rb + (long long)b0 * C::BB, bytes,
-               &bars[st]);
+    if constexpr (TM) {  // rows past M arrive zero-filled and count toward the box bytes
+      if (lane == 0) {
+        mbar_expect_tx(&bars[st], (unsigned)C::STAGE);
+        tma_load_2d(ring + st * C::STAGE, &wmap, b0 * (C::BB / 4), r0, &bars[st]);
+      }
+    } else {
+      const unsigned bytes = (unsigned)(nblk * C::BB);
+      if (lane == 0) mbar_expect_tx(&bars[st], bytes * (unsigned)nr);
+      __syncwarp();
+      if (lane < nr)
+        bulk_g2s(ring + st * C::STAGE + lane * C::SLOT, W + (long long)(r0 + lane) * rb + (long long)b0 * C::BB,
+                 bytes, &bars[st]);
+    }
   };
   for (int tt = 0; tt < min(S, ntiles); ++tt) issue(tt);
 
@@ -298,11 +314,24 @@ gemv_q4k_mma_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, 
   }
 }
 
-template <int WARPS, int S, int CHB>
+template <int WARPS, int S, int CHB, bool TM>
+constexpr int q4k_mma_smem(int k) {
+  return WARPS * S * MmaQ4K<CHB, TM>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
+}
+
+template <int WARPS, int S, int CHB, bool TM>
 static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                     int accumulate, const float* norm_w, float eps) {
-  auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB>;
-  const int smem = WARPS * S * MmaQ4K<CHB>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
+  auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB, TM>;
+  const int smem = q4k_mma_smem<WARPS, S, CHB, TM>(k);
+  CUtensorMap wmap;
+  memset(&wmap, 0, sizeof wmap);
+  if (TM) {  // [m rows][k/256 * 36 u32]: one box = 32 rows x 144 B
+    const uint64_t rbytes = (uint64_t)(k / 256) * 144;
+    if (!make_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, rbytes / 4, (uint64_t)m, rbytes, 36, 32,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  }
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   static int set_for = 0, sms = 0, per_sm = 0;
   if (smem > set_for) {
@@ -321,7 +350,7 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
     if (per_sm < 1) per_sm = 1;
     occ_smem = smem;
   }
-  const int units = (m + MmaQ4K<CHB>::ROWS - 1) / MmaQ4K<CHB>::ROWS;
+  const int units = (m + MmaQ4K<CHB, TM>::ROWS - 1) / MmaQ4K<CHB, TM>::ROWS;
   const int nch = (k / 256 + CHB - 1) / CHB;
   const int cap = sms * per_sm;
   int ksplit = 1;  // smallest power of two that gives every resident warp a unit
@@ -338,17 +367,20 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, y, m, k, ksplit, accumulate, norm_w, eps);
+  return cudaLaunchKernelEx(&cfg, kern, wmap, (const uint8_t*)w, x, y, m, k, ksplit, accumulate, norm_w, eps);
 }
 
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                 int accumulate, const float* norm_w = nullptr, float eps = 0.f) {
-  // Large matrices stream best with 16 single-stage warps per CTA (more
-  // independent bulk copies in flight per SM); small ones, where the chain of
-  // dependent launches dominates, with 8 double-buffered warps.
-  if ((long long)m * k >= (1LL << 24))
-    return launch_q4k_mma_t<16, 1, 2>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
-  return launch_q4k_mma_t<8, 2, 2>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+  // One 2-D TMA box per tile.  Matrices above 2^24 weights stream with two
+  // stages per warp; smaller ones (dominated by the dependent-launch chain)
+  // with one.  Very long rows (x staged in shared memory at 4.25 B per column)
+  // fall back to 8 warps.
+  if (q4k_mma_smem<16, 2, 1, true>(k) > 227 * 1024)
+    return launch_q4k_mma_t<8, 2, 1, true>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+  if ((long long)m * k > (1LL << 24))
+    return launch_q4k_mma_t<16, 2, 1, true>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+  return launch_q4k_mma_t<16, 1, 1, true>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
 }
 
 }  // namespace vtb

@@ -141,6 +141,28 @@ constexpr int ATT_CHUNK = 64;
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_GMAX = 8;  // GQA group sizes up to 8 keep their accumulators in registers
 
+constexpr int ATT_PAD = 8;  // floats of padding per staged K/V row: the score pass reads conflict-free
+static_assert(ATT_THREADS == 2 * ATT_CHUNK, "score pass: two threads per position");
+
+// Shared-memory floats of one attention CTA: q [G][hd], scores [G][CHUNK] (reused
+// as the PV reduction [slices][G][hd]), staged K and V [CHUNK][hd + PAD].
+__host__ __device__ inline int attn_smem_floats(int G, int hd) {
+  const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
+  const int scf = G * ATT_CHUNK > slices * G * hd ? G * ATT_CHUNK : slices * G * hd;
+  return G * hd + scf + 2 * ATT_CHUNK * (hd + ATT_PAD);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// One CTA per (kv head, row, split slot): partial softmax-attention of the G
+// query heads sharing the kv head (attention math of forward.zig's layer loop,
+// split flash-decoding style over 64-position chunks; the splits merge in
+// attn_combine_kernel).  The grid holds about one wave: a CTA walks the row's
+// live splits sp, sp + gridDim.z, ...  Each split's K and V rows go to shared
+// memory in one round of 16-byte async copies, so a CTA waits on DRAM once per
+// split instead of once per position.
 template <int GT>  // GT: compile-time group size, or 0 for the generic path
 __global__ void __launch_bounds__(ATT_THREADS)
 attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
@@ -149,30 +171,28 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
                     float rope_base) {
   // kcw / vcw non-null: decode step with RoPE + KV write fused in (rope_kv_kernel's
   // work): q is rotated in shared memory, and the split that holds the row's
-  // position rotates its K, writes K and V to the cache, then reads them back.
+  // position rotates its K and writes K and V to the cache and to its staged rows.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  extern __shared__ float sm[];
-  const int kvh = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
+  extern __shared__ __align__(16) float sm[];
+  const int kvh = blockIdx.x, r = blockIdx.y;
+  int sp = blockIdx.z;
   const int G = GT ? GT : n_heads / n_kv;
   const int qd = n_heads * hd, kvd = n_kv * hd;
   const int pos = ri.pos[r], seq = ri.seq[r];
-  const int len = pos + 1, t0 = sp * ATT_CHUNK, t1 = min(len, t0 + ATT_CHUNK);
-  float* qs = sm;                  // [G][hd]
-  float* sc = sm + G * hd;         // [G][ATT_CHUNK]
-  float* pr = part + (((long long)r * n_heads + kvh * G) * nsplit + sp) * (hd + 2);  // head stride nsplit*(hd+2)
-  if (t0 >= t1) {
-    if (threadIdx.x < G) {
-      float* p = pr + (long long)threadIdx.x * nsplit * (hd + 2);
-      p[0] = -INFINITY;
-      p[1] = 0.f;
-    }
-    return;
-  }
+  const int len = pos + 1, nsp = (len + ATT_CHUNK - 1) / ATT_CHUNK;
+  if (sp >= nsp) return;  // attn_combine_kernel reads only live splits
+  const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
+  const int scf = G * ATT_CHUNK > slices * G * hd ? G * ATT_CHUNK : slices * G * hd;
+  const int ks = hd + ATT_PAD, h4 = hd / 4;
+  float* qs = sm;           // [G][hd]
+  float* sc = sm + G * hd;  // [G][ATT_CHUNK]
+  float* kst = sc + scf;    // [ATT_CHUNK][ks]
+  float* vst = kst + ATT_CHUNK * ks;
+  const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
   const float inv_sqrt_hd = 1.0f / sqrtf((float)hd);
   const float* q = qkv + (long long)r * (qd + 2 * kvd) + kvh * G * hd;
   for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[i];
   __syncthreads();
-  const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
   if (kcw) {
     const float pos_f = (float)pos;
     const int half = hd / 2;
@@ -187,7 +207,26 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
       ptr[0] = a - b;
       ptr[1] = pp + qq;
     }
-    if (sp == pos / ATT_CHUNK) {  // this split owns position `pos`: write its K (rotated) and V
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float hm[64], hl[64];
+  for (; sp < nsp; sp += gridDim.z) {
+    const int t0 = sp * ATT_CHUNK, t1 = min(len, t0 + ATT_CHUNK), n = t1 - t0;
+    float* pr = part + (((long long)r * n_heads + kvh * G) * nsplit + sp) * (hd + 2);  // head stride nsplit*(hd+2)
+    const int own = (kcw && sp == pos / ATT_CHUNK) ? pos - t0 : -1;  // staged row this CTA writes itself
+    for (int i = threadIdx.x; i < n * h4; i += ATT_THREADS) {
+      const int t = i / h4, c4 = 4 * (i % h4);
+      if (t != own) cp_async16(kst + t * ks + c4, kc + (lbase + t0 + t) * kvd + kvh * hd + c4);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int i = threadIdx.x; i < n * h4; i += ATT_THREADS) {
+      const int t = i / h4, c4 = 4 * (i % h4);
+      if (t != own) cp_async16(vst + t * ks + c4, vc + (lbase + t0 + t) * kvd + kvh * hd + c4);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (own >= 0) {  // this split owns position `pos`: rotate its K, write K and V to cache and stage
+      const float pos_f = (float)pos;
+      const int half = hd / 2;
       const float* kr = qkv + (long long)r * (qd + 2 * kvd) + qd + kvh * hd;
       const float* vr = kr + kvd;
       const long long slot = (lbase + pos) * kvd + kvh * hd;
@@ -198,153 +237,328 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
         const float c = cosf(theta), sn = sinf(theta);
         const float x0 = kr[i], x1 = kr[i + 1];
         const float a = x0 * c, b = x1 * sn, pp = x0 * sn, qq = x1 * c;
-        kcw[slot + i] = a - b;
-        kcw[slot + i + 1] = pp + qq;
+        const float k0 = a - b, k1 = pp + qq;
+        kcw[slot + i] = k0;
+        kcw[slot + i + 1] = k1;
+        kst[own * ks + i] = k0;
+        kst[own * ks + i + 1] = k1;
       }
-      for (int i = threadIdx.x; i < hd; i += blockDim.x) vcw[slot + i] = vr[i];
+      for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        const float v = vr[i];
+        vcw[slot + i] = v;
+        vst[own * ks + i] = v;
+      }
     }
-    __syncthreads();  // block-wide: the cache writes above are visible to this CTA's reads below
-  }
-  const int n = t1 - t0;
-  // scores: one thread per position; the K row is read once, all G heads accumulate together
-  for (int tt = threadIdx.x; tt < n; tt += blockDim.x) {
-    const float4* kt = reinterpret_cast<const float4*>(kc + (lbase + t0 + tt) * kvd + kvh * hd);
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // K staged (V may still be in flight)
+    __syncthreads();
+    // scores: two threads per position, each over alternate float4 columns of the staged K row
+    {
+      const int tt = threadIdx.x >> 1, hf = threadIdx.x & 1;
+      const float4* kr = reinterpret_cast<const float4*>(kst + tt * ks);
+      const float4* q4 = reinterpret_cast<const float4*>(qs);
+      if constexpr (GT > 0) {
+        float acc[GT];
+#pragma unroll
+        for (int h = 0; h < GT; ++h) acc[h] = 0.f;
+        if (tt < n) {
+#pragma unroll 4
+          for (int j = hf; j < h4; j += 2) {
+            const float4 kv = kr[j];
+#pragma unroll
+            for (int h = 0; h < GT; ++h) {
+              const float4 b = q4[h * h4 + j];
+              acc[h] += kv.x * b.x + kv.y * b.y + kv.z * b.z + kv.w * b.w;
+            }
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < GT; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+        if (tt < n && hf == 0)
+#pragma unroll
+          for (int h = 0; h < GT; ++h) sc[h * ATT_CHUNK + tt] = acc[h] * inv_sqrt_hd;
+      } else {
+        for (int h = 0; h < G; ++h) {
+          float a = 0.f;
+          if (tt < n)
+            for (int j = hf; j < h4; j += 2) {
+              const float4 kv = kr[j], b = q4[h * h4 + j];
+              a += kv.x * b.x + kv.y * b.y + kv.z * b.z + kv.w * b.w;
+            }
+          a += __shfl_xor_sync(0xffffffffu, a, 1);
+          if (tt < n && hf == 0) sc[h * ATT_CHUNK + tt] = a * inv_sqrt_hd;
+        }
+      }
+    }
+    __syncthreads();
+    // per head: local max and exp-sum
+    for (int h = warp; h < G; h += ATT_THREADS / 32) {
+      float m = -INFINITY;
+      for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h * ATT_CHUNK + i]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float l = 0.f;
+      for (int i = lane; i < n; i += 32) {
+        const float e = expf(sc[h * ATT_CHUNK + i] - m);
+        sc[h * ATT_CHUNK + i] = e;
+        l += e;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        hm[h] = m;
+        hl[h] = l;
+      }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // V staged
+    __syncthreads();
+    // acc[h][d] = sum_t p[h][t] v[t][d]: thread (slice, d) reads staged v[t][d] once for every
+    // head of the group; `slices` threads share a dimension, split the positions, add through smem.
+    const int dd = threadIdx.x % hd, sl = threadIdx.x / hd;
     if constexpr (GT > 0) {
       float acc[GT];
 #pragma unroll
       for (int h = 0; h < GT; ++h) acc[h] = 0.f;
-#pragma unroll 2
-      for (int d4 = 0; d4 < hd / 4; d4 += 4) {
-        float4 k4[4];
+      if (sl < slices && dd < hd) {
+#pragma unroll 4
+        for (int t = sl; t < n; t += slices) {
+          const float v = vst[t * ks + dd];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) k4[u] = kt[d4 + u];
-#pragma unroll
-        for (int h = 0; h < GT; ++h) {
-          const float4* qh = reinterpret_cast<const float4*>(qs + h * hd) + d4;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float4 b = qh[u];
-            acc[h] += k4[u].x * b.x + k4[u].y * b.y + k4[u].z * b.z + k4[u].w * b.w;
-          }
+          for (int h = 0; h < GT; ++h) acc[h] += sc[h * ATT_CHUNK + t] * v;
         }
       }
+      __syncthreads();
+      float* red = sc;  // reuse the score buffer: [slices][GT][hd]
+      if (sl < slices && dd < hd)
 #pragma unroll
-      for (int h = 0; h < GT; ++h) sc[h * ATT_CHUNK + tt] = acc[h] * inv_sqrt_hd;
+        for (int h = 0; h < GT; ++h) red[(sl * GT + h) * hd + dd] = acc[h];
+      __syncthreads();
+      for (int i = threadIdx.x; i < GT * hd; i += blockDim.x) {
+        const int h = i / hd, d = i % hd;
+        float a = 0.f;
+        for (int z = 0; z < slices; ++z) a += red[(z * GT + h) * hd + d];
+        float* p = pr + (long long)h * nsplit * (hd + 2);
+        p[2 + d] = a;
+        if (d == 0) {
+          p[0] = hm[h];
+          p[1] = hl[h];
+        }
+      }
     } else {
-      for (int h = 0; h < G; ++h) {
-        const float4* qh = reinterpret_cast<const float4*>(qs + h * hd);
-        float s = 0.f;
-        for (int d = 0; d < hd / 4; ++d) {
-          const float4 a = kt[d], b = qh[d];
-          s += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+      for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        const int h = i / hd, d = i % hd;
+        const float* ph = sc + h * ATT_CHUNK;
+        float a = 0.f;
+        for (int t = 0; t < n; ++t) a += ph[t] * vst[t * ks + d];
+        float* p = pr + (long long)h * nsplit * (hd + 2);
+        p[2 + d] = a;
+        if (d == 0) {
+          p[0] = hm[h];
+          p[1] = hl[h];
         }
-        sc[h * ATT_CHUNK + tt] = s * inv_sqrt_hd;
       }
     }
+    __syncthreads();  // the next split reuses the staging and score buffers
   }
-  __syncthreads();
-  // per head: local max and exp-sum
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float hm[64], hl[64];
-  for (int h = warp; h < G; h += ATT_THREADS / 32) {
-    float m = -INFINITY;
-    for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h * ATT_CHUNK + i]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int i = lane; i < n; i += 32) {
-      const float e = expf(sc[h * ATT_CHUNK + i] - m);
-      sc[h * ATT_CHUNK + i] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      hm[h] = m;
-      hl[h] = l;
-    }
-  }
-  __syncthreads();
-  // acc[h][d] = sum_t p[h][t] v[t][d]: thread (slice, d) reads v[t][d] once for every head of the group;
-  // `slices` threads share a dimension and split the positions, then add through shared memory.
-  const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
-  const int dd = threadIdx.x % hd, sl = threadIdx.x / hd;
-  if constexpr (GT > 0) {
-    float acc[GT];
-#pragma unroll
-    for (int h = 0; h < GT; ++h) acc[h] = 0.f;
-    if (sl < slices && dd < hd) {
-      const float* vt = vc + (lbase + t0) * kvd + kvh * hd + dd;
-      int t = sl;
-      for (; t + 3 * slices < n; t += 4 * slices) {  // four independent loads in flight
-        float v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = vt[(long long)(t + u * slices) * kvd];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int h = 0; h < GT; ++h) acc[h] += sc[h * ATT_CHUNK + t + u * slices] * v[u];
-      }
-      for (; t < n; t += slices) {
-        const float v = vt[(long long)t * kvd];
-#pragma unroll
-        for (int h = 0; h < GT; ++h) acc[h] += sc[h * ATT_CHUNK + t] * v;
-      }
-    }
-    __syncthreads();
-    float* red = sc;  // reuse the score buffer: [slices][GT][hd]
-    if (sl < slices && dd < hd)
-#pragma unroll
-      for (int h = 0; h < GT; ++h) red[(sl * GT + h) * hd + dd] = acc[h];
-    __syncthreads();
-    for (int i = threadIdx.x; i < GT * hd; i += blockDim.x) {
-      const int h = i / hd, d = i % hd;
-      float a = 0.f;
-      for (int z = 0; z < slices; ++z) a += red[(z * GT + h) * hd + d];
-      float* p = pr + (long long)h * nsplit * (hd + 2);
-      p[2 + d] = a;
-      if (d == 0) {
-        p[0] = hm[h];
-        p[1] = hl[h];
-      }
-    }
-  } else {
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-      const int h = i / hd, d = i % hd;
-      const float* vt = vc + (lbase + t0) * kvd + kvh * hd + d;
-      const float* ph = sc + h * ATT_CHUNK;
-      float a = 0.f;
-      for (int t = 0; t < n; ++t) a += ph[t] * vt[(long long)t * kvd];
-      float* p = pr + (long long)h * nsplit * (hd + 2);
-      p[2 + d] = a;
-      if (d == 0) {
-        p[0] = hm[h];
-        p[1] = hl[h];
-      }
-    }
-  }
+  asm volatile("griddepcontrol.launch_dependents;");
 }
 
-// Merge the splits of each (row, q head): out = sum_s acc_s e^{m_s - M} / sum_s l_s e^{m_s - M}.
-__global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ att, int n_heads, int hd,
-                                    int nsplit) {
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();  // red may still be read by a previous reduction
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  v = red[0];
+  for (int w = 1; w < nw; ++w) v = is_max ? fmaxf(v, red[w]) : v + red[w];
+  return v;
+}
+
+// Merge the live splits of each (row, q head):
+// out = sum_s acc_s e^{m_s - M} / sum_s l_s e^{m_s - M}.  The split weights are
+// computed once into shared memory; each dimension's sum then has independent loads.
+__global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ att, RowInfo ri, int n_heads,
+                                    int hd, int nsplit) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  extern __shared__ float wsm[];  // [nsplit]
+  __shared__ float red[32];
   const int h = blockIdx.x, r = blockIdx.y;
+  const int na = min(nsplit, ri.pos[r] / ATT_CHUNK + 1);
   const float* p = part + ((long long)r * n_heads + h) * nsplit * (hd + 2);
   float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, p[s * (hd + 2)]);
+  for (int s = threadIdx.x; s < na; s += blockDim.x) M = fmaxf(M, p[s * (hd + 2)]);
+  M = block_reduce(M, true, red);
   float L = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const float m = p[s * (hd + 2)];
-    if (m != -INFINITY) L += p[s * (hd + 2) + 1] * expf(m - M);
+  for (int s = threadIdx.x; s < na; s += blockDim.x) {
+    const float e = expf(p[s * (hd + 2)] - M);
+    wsm[s] = e;
+    L += p[s * (hd + 2) + 1] * e;
   }
+  L = block_reduce(L, false, red);  // its barriers also publish wsm
   const float invL = 1.0f / L;
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float a = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float m = p[s * (hd + 2)];
-      if (m != -INFINITY) a += p[s * (hd + 2) + 2 + d] * expf(m - M);
-    }
+#pragma unroll 4
+    for (int s = 0; s < na; ++s) a += p[s * (hd + 2) + 2 + d] * wsm[s];
     att[((long long)r * n_heads + h) * hd + d] = a * invL;
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// Prefill attention: the rows are one prompt (one sequence, consecutive or
+// arbitrary positions).  One CTA per (kv head, tile of 64 query vectors =
+// 64/G rows x the G query heads of the kv head) walks the K/V chunks up to the
+// tile's last position with an online softmax, so each staged K/V chunk serves
+// 64 query vectors instead of one (the per-row kernel re-reads the whole
+// prefix for every row).  fp32 throughout; the output goes straight to `att`.
+constexpr int PA_QV = 64;       // query vectors per CTA
+constexpr int PA_THREADS = 256; // 16 groups of 4 query vectors x 16 lanes
+template <int HD>
+struct PaSmem {
+  static constexpr int QS = HD + 4, KS = HD + 4, PS = PA_QV + 4;  // padded row strides (floats)
+  static constexpr int FLOATS = PA_QV * QS + 2 * ATT_CHUNK * KS + ATT_CHUNK * PS + PA_QV;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(PA_THREADS)
+attn_prefill_kernel(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
+                    RowInfo ri, int rows, int layer, int n_layers, int max_seq, int n_heads, int n_kv,
+                    float* __restrict__ att) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  using P = PaSmem<HD>;
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                          // [64 qvec][QS]
+  float* kst = qs + PA_QV * P::QS;         // [CHUNK][KS]
+  float* vst = kst + ATT_CHUNK * P::KS;    // [CHUNK][KS]
+  float* ps = vst + ATT_CHUNK * P::KS;     // [CHUNK][PS]: probabilities, position-major
+  int* qpos = reinterpret_cast<int*>(ps + ATT_CHUNK * P::PS);  // [64] position of each query vector's row
+  const int G = n_heads / n_kv, QT = PA_QV / G;
+  const int kvh = blockIdx.x, row0 = blockIdx.y * QT;
+  const int qd = n_heads * HD, kvd = n_kv * HD;
+  const int seq = ri.seq[row0];
+  const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
+  const float inv_sqrt_hd = 1.0f / sqrtf((float)HD);
+  // q tile: vector v = (row v / G, head v % G); rows past the end get position 0 (never written)
+  for (int i = threadIdx.x; i < PA_QV * (HD / 4); i += PA_THREADS) {
+    const int v = i / (HD / 4), c4 = 4 * (i % (HD / 4)), rr = row0 + v / G;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (rr < rows) a = *reinterpret_cast<const float4*>(qkv + (long long)rr * (qd + 2 * kvd) + (kvh * G + v % G) * HD + c4);
+    *reinterpret_cast<float4*>(qs + v * P::QS + c4) = a;
+  }
+  int maxpos = 0;
+  for (int v = threadIdx.x; v < PA_QV; v += PA_THREADS) {
+    const int rr = row0 + v / G;
+    qpos[v] = rr < rows ? ri.pos[rr] : 0;
+  }
+  __syncthreads();
+  for (int v = 0; v < PA_QV; v += G) maxpos = max(maxpos, qpos[v]);
+  const int nch = maxpos / ATT_CHUNK + 1;
+  const int qg = threadIdx.x >> 4, pg = threadIdx.x & 15;  // query vectors 4qg..4qg+3; positions pg + 16j
+  int mypos[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mypos[i] = qpos[4 * qg + i];
+  float mrun[4], lrun[4];
+  constexpr int DPT = HD / 16;  // output dims per thread: dg*4 .. +4 (and +64 for HD = 128)
+  float o[4][DPT];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    mrun[i] = -INFINITY;
+    lrun[i] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DPT; ++d) o[i][d] = 0.f;
+  }
+  for (int ch = 0; ch < nch; ++ch) {
+    const int t0 = ch * ATT_CHUNK, n = min(ATT_CHUNK, maxpos + 1 - t0);
+    for (int i = threadIdx.x; i < n * (HD / 4); i += PA_THREADS) {
+      const int t = i / (HD / 4), c4 = 4 * (i % (HD / 4));
+      const long long src = (lbase + t0 + t) * kvd + kvh * HD + c4;
+      cp_async16(kst + t * P::KS + c4, kc + src);
+      cp_async16(vst + t * P::KS + c4, vc + src);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    // scores s[i][j] = q[4qg+i] . k[pg+16j] / sqrt(hd), causal per query row
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll 4
+    for (int d4 = 0; d4 < HD / 4; ++d4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(qs + (4 * qg + i) * P::QS + 4 * d4);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(kst + (pg + 16 * j) * P::KS + 4 * d4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          s[i][j] += qv[i].x * kv[j].x + qv[i].y * kv[j].y + qv[i].z * kv[j].z + qv[i].w * kv[j].w;
+    }
+    float alpha[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float mc = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = t0 + pg + 16 * j;
+        s[i][j] = (pg + 16 * j < n && t <= mypos[i]) ? s[i][j] * inv_sqrt_hd : -INFINITY;
+        mc = fmaxf(mc, s[i][j]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
+      const float mnew = fmaxf(mrun[i], mc);  // finite: chunk 0 holds position 0 for every row
+      alpha[i] = expf(mrun[i] - mnew);
+      float ls = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = expf(s[i][j] - mnew);
+        ps[(pg + 16 * j) * P::PS + 4 * qg + i] = p;
+        ls += p;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+      lrun[i] = lrun[i] * alpha[i] + ls;
+      mrun[i] = mnew;
+    }
+    __syncthreads();
+    // o[i][.] = o * alpha + sum_t p[t][4qg+i] v[t][.]
+    const int dg = pg;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int d = 0; d < DPT; ++d) o[i][d] *= alpha[i];
+    for (int t = 0; t < n; ++t) {
+      const float4 p4 = *reinterpret_cast<const float4*>(ps + t * P::PS + 4 * qg);
+      const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+      for (int h = 0; h < DPT / 4; ++h) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vst + t * P::KS + 64 * h + 4 * dg);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          o[i][4 * h] += pp[i] * v4.x;
+          o[i][4 * h + 1] += pp[i] * v4.y;
+          o[i][4 * h + 2] += pp[i] * v4.z;
+          o[i][4 * h + 3] += pp[i] * v4.w;
+        }
+      }
+    }
+    __syncthreads();  // the next chunk overwrites K, V and P
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = 4 * qg + i, rr = row0 + v / G;
+    if (rr >= rows) continue;
+    const float inv = 1.0f / lrun[i];
+    float* out = att + (long long)rr * qd + (kvh * G + v % G) * HD;
+#pragma unroll
+    for (int h = 0; h < DPT / 4; ++h)
+      *reinterpret_cast<float4*>(out + 64 * h + 4 * pg) =
+          make_float4(o[i][4 * h] * inv, o[i][4 * h + 1] * inv, o[i][4 * h + 2] * inv, o[i][4 * h + 3] * inv);
   }
   asm volatile("griddepcontrol.launch_dependents;");
 }
@@ -447,6 +661,8 @@ struct VtbCudaState {
   float* logits_local;      // [rows][V] LM-head slice under tensor parallelism
   bool pending = false;     // tmp holds an all-reduced partial still to be added to x
   bool decode_rows = false; // staged rows are distinct sequences (decode), not one prompt (prefill)
+  int max_pos = 0;          // largest staged position (sizes prefill attention grids)
+  bool one_seq = false;     // every staged row belongs to one sequence
   cudaGraphExec_t graph = nullptr;
   int graph_rows = -1;
 };
@@ -473,8 +689,8 @@ VtbCudaModel* vtb_cuda_model_create_tp(VtbCudaCtx* ctx, VtbCudaTp* tp, const Vtb
   }
   const VtbCudaLlamaConfig c = *cfg;
   if (c.dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads ||
-      c.head_dim % 4 || c.n_heads * c.head_dim != c.dim || c.ffn_dim <= 0 || c.vocab_size <= 0 || c.max_seq <= 0 ||
-      c.n_heads / c.n_kv_heads > 64) {
+      c.head_dim % 8 || c.n_heads * c.head_dim != c.dim || c.ffn_dim <= 0 || c.vocab_size <= 0 || c.max_seq <= 0 ||
+      c.n_heads / c.n_kv_heads > 64 || attn_smem_floats(c.n_heads / c.n_kv_heads, c.head_dim) * 4 > 227 * 1024) {
     merr(VTB_CUDA_ERR_INVALID_ARG, "inconsistent Llama config");
     return nullptr;
   }
@@ -652,6 +868,26 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   }
   s->n_seqs = n_seqs;
   s->max_rows = max_rows;
+  {  // attention stages K/V in shared memory: opt every instantiation in to the size this model needs
+    const int asmem = attn_smem_floats(c.n_heads / c.n_kv_heads, c.head_dim) * 4;
+    cudaError_t ea = cudaFuncSetAttribute(attn_partial_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
+    if (!ea) ea = cudaFuncSetAttribute(attn_partial_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
+    if (!ea) ea = cudaFuncSetAttribute(attn_partial_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
+    if (!ea) ea = cudaFuncSetAttribute(attn_partial_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
+    if (!ea) ea = cudaFuncSetAttribute(attn_partial_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
+    if (!ea)
+      ea = cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                PaSmem<64>::FLOATS * 4);
+    if (!ea)
+      ea = cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                PaSmem<128>::FLOATS * 4);
+    if (ea) {
+      mcuda(ea);
+      cudaStreamDestroy(s->st);
+      delete s;
+      return nullptr;
+    }
+  }
   s->nsplit = (c.max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
   const size_t R = max_rows, d = c.dim, hd = c.head_dim, qd = (size_t)m->H * hd, kvd = (size_t)m->KV * hd, f = m->F;
   const size_t qkvw = qd + 2 * kvd;
@@ -730,6 +966,10 @@ static int stage_rows(VtbCudaState* s, int rows, const int32_t* tok, const int32
   }
   s->rows = rows;
   s->pending = false;
+  s->max_pos = 0;
+  for (int r = 0; r < rows; ++r) s->max_pos = std::max(s->max_pos, (int)pos[r]);
+  s->one_seq = true;
+  for (int r = 1; r < rows; ++r) s->one_seq = s->one_seq && seq[r] == seq[0];
   s->decode_rows = true;
   for (int r = 1; r < rows && s->decode_rows; ++r)
     for (int q = 0; q < r; ++q)
@@ -844,28 +1084,43 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
     return e;
   float* kcw = fuse_rope ? s->kc : nullptr;
   float* vcw = fuse_rope ? s->vc : nullptr;
-  // shared: q [G][hd] + scores [G][CHUNK]; the PV reduction reuses the score area ([slices][G][hd])
-  const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
-  const size_t asmem = (size_t)(G * hd + std::max(G * ATT_CHUNK, slices * G * hd)) * 4;
-  const dim3 agrid(KV, R, s->nsplit);
-  switch (hd <= ATT_THREADS && hd % 16 == 0 ? G : 0) {  // register path needs hd <= 128, hd % 16 == 0
-#define VTB_ATT(g)                                                                                               \
-  case g:                                                                                                      \
-    e = pdl_launch(attn_partial_kernel<g>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,             \
-                   (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,     \
-                   s->nsplit, kcw, vcw, c.rope_base);                                                          \
-    break;
-    VTB_ATT(1) VTB_ATT(2) VTB_ATT(4) VTB_ATT(8)
-#undef VTB_ATT
-    default:
-      e = pdl_launch(attn_partial_kernel<0>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,
-                     (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,
-                     s->nsplit, kcw, vcw, c.rope_base);
+  if (!fuse_rope && s->one_seq && (hd == 64 || hd == 128) && PA_QV % G == 0) {
+    // prompt rows: query-tiled attention, no split/combine pass
+    const dim3 pgrid(KV, (R + PA_QV / G - 1) / (PA_QV / G));
+    e = hd == 64 ? pdl_launch(attn_prefill_kernel<64>, pgrid, dim3(PA_THREADS), (size_t)PaSmem<64>::FLOATS * 4, st,
+                              (const float*)s->qkv, (const float*)s->kc, (const float*)s->vc, ri, R, l, c.n_layers,
+                              c.max_seq, H, KV, s->att)
+                 : pdl_launch(attn_prefill_kernel<128>, pgrid, dim3(PA_THREADS), (size_t)PaSmem<128>::FLOATS * 4, st,
+                              (const float*)s->qkv, (const float*)s->kc, (const float*)s->vc, ri, R, l, c.n_layers,
+                              c.max_seq, H, KV, s->att);
+    if (e) return e;
+  } else {
+    const size_t asmem = (size_t)attn_smem_floats(G, hd) * 4;
+    // Decode (replayed as a graph while positions grow): about one wave of CTAs
+    // (3 resident per SM at these sizes), each walking its row's live splits.
+    // Prefill rows (enqueued directly): one CTA per live split of the longest row.
+    const int zdec = std::max(1, 3 * 148 / (KV * R));
+    const int z = s->decode_rows ? std::min(s->nsplit, zdec) : std::min(s->nsplit, s->max_pos / ATT_CHUNK + 1);
+    const dim3 agrid(KV, R, z);
+    switch (hd <= ATT_THREADS && hd % 16 == 0 ? G : 0) {  // register path needs hd <= 128, hd % 16 == 0
+  #define VTB_ATT(g)                                                                                               \
+    case g:                                                                                                      \
+      e = pdl_launch(attn_partial_kernel<g>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,             \
+                     (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,     \
+                     s->nsplit, kcw, vcw, c.rope_base);                                                          \
+      break;
+      VTB_ATT(1) VTB_ATT(2) VTB_ATT(4) VTB_ATT(8)
+  #undef VTB_ATT
+      default:
+        e = pdl_launch(attn_partial_kernel<0>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,
+                       (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,
+                       s->nsplit, kcw, vcw, c.rope_base);
+    }
+    if (e) return e;
+    if ((e = pdl_launch(attn_combine_kernel, dim3(H, R), dim3(128), (size_t)s->nsplit * 4, st, (const float*)s->part,
+                        s->att, ri, H, hd, s->nsplit)))
+      return e;
   }
-  if (e) return e;
-  if ((e = pdl_launch(attn_combine_kernel, dim3(H, R), dim3(128), 0, st, (const float*)s->part, s->att, H, hd,
-                      s->nsplit)))
-    return e;
   if ((e = residual(L.q_o, L.o, s->att, qd))) return e;  // x += W_o . att (addInto fused)
   if (fused_norm_gemv(L.ffn_norm, L.q_gate, L.gu, s->gu, 2 * f)) {
     if (e) return e;
