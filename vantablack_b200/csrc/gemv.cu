@@ -421,7 +421,9 @@ cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, i
   switch (q) {
     case Q4_K: return launch_gemv_t<Q4_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
     case Q5_K: return launch_gemv_t<Q5_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
-    case Q6_K: return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
+    case Q6_K:  // integer tensor cores when rows are whole 16-byte multiples
+      if (q6k_mma_ok(w, k)) return launch_gemv_q6k_mma(w, x, y, m, k, st, pdl, accumulate);
+      return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
     case Q8_0: return launch_gemv_t<Q8_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
     default: return cudaErrorInvalidValue;
   }

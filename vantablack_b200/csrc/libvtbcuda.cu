@@ -1,6 +1,7 @@
 // libvtbcuda.cu -- single translation unit of the backend library: the
 // kernels share device globals (the error word), so they are compiled
 // together without relocatable device code.
+#include "gemv_q6k_mma.cu"
 #include "gemv.cu"
 #include "gemv_mma.cu"
 #include "quant_aux.cu"
