@@ -372,6 +372,12 @@ def run_profile_case(case: str) -> None:
             x = torch.from_numpy(S.activations(rng, K)).cuda()
             ops.gemv(Q4_K, w, x, m, K)
             torch.cuda.synchronize()
+    elif case == "gemv_q6k":  # Q6_K ffn_down 4096 x 14336, then the LM head 128256 x 4096 (431 MB)
+        for m, k in ((4096, 14336), (128256, 4096)):
+            w = torch.from_numpy(S.quant_tensor(rng, S.Q6_K, m, k)).cuda()
+            x = torch.from_numpy(S.activations(rng, k)).cuda()
+            ops.gemv(S.Q6_K, w, x, m, k)
+            torch.cuda.synchronize()
     elif case == "gemm":  # config 3: Q4_K 14336 x 4096, B = 2048, bf16 mode, two launches
         m, k, b = 14336, 4096, 2048
         w = torch.from_numpy(S.quant_tensor(rng, Q4_K, m, k)).cuda()
@@ -401,7 +407,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--model-steps", type=int, default=32, help="decode steps of the 8B model metrics (0 = skip)")
-    ap.add_argument("--profile", choices=["gemv", "gemm", "decode", "decode8b"], help="run a small case for ncu and exit")
+    ap.add_argument("--profile", choices=["gemv", "gemv_q6k", "gemm", "decode", "decode8b"], help="run a small case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)

@@ -263,9 +263,12 @@ static cudaError_t launch_q6k_mma_t(const void* w, const float* x, float* y, int
   const int units = (m + Q6M_ROWS - 1) / Q6M_ROWS;
   const int nch = k / 512;
   const int cap = sms * per_sm;
-  int ksplit = 1;  // smallest power of two that gives every resident warp a unit
-  while (ksplit < WARPS && ksplit < nch && (long long)units * ksplit < (long long)cap * WARPS) ksplit *= 2;
-  while (WARPS % ksplit) ksplit /= 2;
+  int ksplit = 1;  // smallest divisor of WARPS (at most nch) that gives every resident warp a unit
+  for (int d = 1; d <= WARPS && d <= nch; ++d) {
+    if (WARPS % d) continue;
+    ksplit = d;
+    if ((long long)units * d >= (long long)cap * WARPS) break;
+  }
   const int groups = (units + WARPS / ksplit - 1) / (WARPS / ksplit);
   const int grid = groups < cap ? groups : cap;
   cudaLaunchConfig_t cfg = {};

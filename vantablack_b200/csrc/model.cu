@@ -577,30 +577,50 @@ __global__ void swiglu_kernel(const float* __restrict__ gu, float* __restrict__ 
 }
 
 // argmax (math.zig:190-201): first index of the maximum of each row.
-__global__ void argmax_kernel(const float* __restrict__ logits, int32_t* __restrict__ out, int n) {
-  const int r = blockIdx.x;
+// argmax (math.zig:190-201): first index of the maximum of each row (NaNs never
+// win; an all-NaN row gives 0).  Two passes so a 128K-entry vocabulary row is
+// scanned by ARGMAX_PARTS CTAs: each writes its slice's (max, first index),
+// then one warp per row keeps the largest value with the smallest index.
+constexpr int ARGMAX_PARTS = 64;
+
+__device__ __forceinline__ void argmax_merge(float& bv, int& bi, float ov, int oi) {
+  if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+}
+
+__global__ void argmax_partial_kernel(const float* __restrict__ logits, float* __restrict__ pv, int* __restrict__ pi,
+                                      int n) {
+  const int r = blockIdx.y, b = blockIdx.x;
+  const int slice = (n + ARGMAX_PARTS - 1) / ARGMAX_PARTS, i0 = b * slice, i1 = min(n, i0 + slice);
   const float* l = logits + (long long)r * n;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     const float v = l[i];
-    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    if (v > bv) { bv = v; bi = i; }  // ascending i per thread: the first maximum is kept
   }
   __shared__ float sv[32];
   __shared__ int si[32];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-  }
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
   if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
-    out[r] = bi == 0x7fffffff ? 0 : bi;
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) argmax_merge(bv, bi, sv[w], si[w]);
+    pv[r * ARGMAX_PARTS + b] = bv;
+    pi[r * ARGMAX_PARTS + b] = bi;
   }
+}
+
+__global__ void argmax_final_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int32_t* __restrict__ out) {
+  const int r = blockIdx.x, lane = threadIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int b = lane; b < ARGMAX_PARTS; b += 32) argmax_merge(bv, bi, pv[r * ARGMAX_PARTS + b], pi[r * ARGMAX_PARTS + b]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+  if (lane == 0) out[r] = bi == 0x7fffffff ? 0 : bi;
 }
 
 // Row-concatenate rows [r0, r1) of `n_parts` tensors (fuseRowConcat, model.zig:358-378).
@@ -1167,7 +1187,11 @@ static cudaError_t enqueue_final(VtbCudaState* s, bool last_only) {
       return cudaErrorUnknown;
     }
   }
-  argmax_kernel<<<n, 1024, 0, st>>>(s->logits, s->amax, c.vocab_size);
+  // the attention partials are dead after the last layer: reuse them for the argmax slices
+  float* apv = s->part;
+  int* api = reinterpret_cast<int*>(s->part + (size_t)n * ARGMAX_PARTS);
+  argmax_partial_kernel<<<dim3(ARGMAX_PARTS, n), 256, 0, st>>>(s->logits, apv, api, c.vocab_size);
+  argmax_final_kernel<<<n, 32, 0, st>>>(apv, api, s->amax);
   return cudaGetLastError();
 }
 
