@@ -287,8 +287,9 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# dram bytes per launch from the committed ncu capture (profiles/), or None.
-ALG_BYTES_TRAFFIC = None
+# DRAM bytes (read + write) of one config-1 launch, from the ncu capture summarised in
+# profiles/q4k_gemv_5632x2048.md (6,545,152 read, ~0 written; algorithmic 6,518,784).
+ALG_BYTES_TRAFFIC = 6545152
 
 
 def model_metrics(rank: int, world: int, local: int, dist, args) -> dict:
