@@ -215,6 +215,12 @@ int vtb_cuda_state_reset(VtbCudaState *s);
 /* KvCache.pos of sequence `seq` (host-authoritative). */
 int64_t vtb_cuda_state_pos(VtbCudaState *s, int32_t seq);
 
+/* 1 when this tensor-parallel state all-reduces over NVLink peer memory
+ * (partials summed by the following RMSNorm kernel), 0 when it uses NCCL or
+ * runs on one GPU.  No reference counterpart (the reference has no
+ * multi-device code). */
+int vtb_cuda_state_tp_p2p(const VtbCudaState *s);
+
 /* The vtable, slot by slot.  begin_token is stepWithBackend's preamble
  * (token checks + gatherEmbedding, forward.zig:158-163) for one token per
  * sequence; layer_step / final_step / finalize_token are the VTable slots.

@@ -23,5 +23,6 @@ def test_tp2_tinyllama_greedy_identical(tmp_path):
     assert r.returncode == 0, r.stderr[-3000:]
     res = json.loads(out.read_text())
     assert res["ranks_agree"]
+    assert res["p2p"], "the all-reduce fell back to NCCL instead of NVLink peer memory"
     assert res["match"], (res["ids"], res["ids_ref"])
     assert res["logits_rel"] <= 1e-3

@@ -32,7 +32,9 @@ def main():
     tp = TensorParallel(local, rank, world, exchange)
     st = CudaState(CudaModel(ctx, w, tp), 1, max_rows=128)
     ids, logits = st.generate_greedy(prompt, n_gen, use_prefill=True)
-    res = {"rank": rank, "ids": ids}
+    from vantablack_b200 import _lib
+    _lib.check(_lib.load().vtb_cuda_check_device_error(), "device error word")  # no peer wait timed out
+    res = {"rank": rank, "ids": ids, "p2p": st.tp_p2p()}
     if rank == 0:
         import oracle as O
         O.set_threads(os.cpu_count() or 8)

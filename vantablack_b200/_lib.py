@@ -59,6 +59,7 @@ SIGNATURES = {
     "vtb_cuda_state_destroy": (None, [_vp]),
     "vtb_cuda_state_reset": (_int, [_vp]),
     "vtb_cuda_state_pos": (_i64, [_vp, _i32]),
+    "vtb_cuda_state_tp_p2p": (_i32, [_vp]),
     "vtb_cuda_begin_token": (_int, [_vp, _vp]),
     "vtb_cuda_layer_step": (_int, [_vp, _i32]),
     "vtb_cuda_final_step": (_int, [_vp]),

@@ -40,7 +40,7 @@ inline bool host_quant_ok(int q) { return q == Q8_0 || q == Q4_K || q == Q5_K ||
 
 // Device-side error word.  Kernels that give up a bounded wait OR a code in
 // here and return; the host reads it with vtb_cuda_check_device_error().
-enum DevErr : unsigned { DEV_ERR_MBAR_TIMEOUT = 1u, DEV_ERR_BAD_ARG = 2u };
+enum DevErr : unsigned { DEV_ERR_MBAR_TIMEOUT = 1u, DEV_ERR_BAD_ARG = 2u, DEV_ERR_PEER_TIMEOUT = 4u };
 __device__ unsigned g_dev_error = 0;  // one definition: the library is a single translation unit
 
 __device__ __forceinline__ void flag_error(unsigned code) { atomicOr(&g_dev_error, code); }

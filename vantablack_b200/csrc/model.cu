@@ -91,6 +91,102 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
   for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = (xr[i] * w[i]) * inv;
 }
 
+// ---- tensor-parallel all-reduce over NVLink peer memory ----
+// Each rank's row-parallel projection (O, down) writes its partial into a
+// double-buffered slot of an IPC-shared block; tp_signal_kernel then raises
+// this rank's epoch flag in every peer's block; the consumer,
+// rmsnorm_tp_kernel, waits (bounded) for all peers' flags and sums the
+// partials straight out of peer memory, fused with the residual add and the
+// RMSNorm that follows the collective in the layer.  Every rank sums in rank
+// order, so all ranks hold bit-identical residuals.  Slot e % 2 is rewritten
+// only after every peer's flag for e + 1 was seen, which a peer raises after
+// its consumer of e has run: no overwrite while a peer still reads.
+constexpr int TP_MAX = 8;
+struct PeerPtrs {
+  float* p[TP_MAX];  // each rank's shared block (this rank's own included)
+};
+// Shared block: [2][max_rows * dim] partial slots | flags[TP_MAX] | epoch.
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void tp_signal_kernel(PeerPtrs peers, int world, int me, long long flag_off) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the partial of this rank is complete
+  if (threadIdx.x == 0) {
+    unsigned* mine = reinterpret_cast<unsigned*>(peers.p[me] + flag_off);
+    const unsigned e = mine[TP_MAX] + 1;  // epoch: one per all-reduce, identical on every rank
+    mine[TP_MAX] = e;
+    __threadfence_system();
+    for (int r = 0; r < world; ++r)
+      if (r != me) st_release_sys(reinterpret_cast<unsigned*>(peers.p[r] + flag_off) + me, e);
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// x[r] += sum over ranks of slot[r] (peer loads), then out = RMSNorm(x) as rmsnorm_kernel.
+__global__ void __launch_bounds__(1024) rmsnorm_tp_kernel(float* __restrict__ x, PeerPtrs peers, int world, int me, long long slot_off,
+                                  long long flag_off, const float* __restrict__ w, float* __restrict__ out, int n,
+                                  float eps) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) {
+    const unsigned* flags = reinterpret_cast<const unsigned*>(peers.p[me] + flag_off);
+    const unsigned e = flags[TP_MAX];
+    for (int r = 0; r < world; ++r) {
+      if (r == me) continue;
+      unsigned it = 0;
+      while ((int)(ld_acquire_sys(flags + r) - e) < 0) {  // bounded: a missing peer flags an error, never hangs
+        if (++it > (1u << 24)) {
+          flag_error(DEV_ERR_PEER_TIMEOUT);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+  const int r = blockIdx.x;
+  float* xr = x + (long long)r * n;
+  float ss = 0.f;
+  // One 16-byte load per rank per thread, all issued before any is used: the
+  // remote reads cost one NVLink round trip, not one per element.  (.cv: a
+  // slot's previous contents may sit in this SM's L1.)
+  for (int i4 = threadIdx.x; i4 < n / 4; i4 += blockDim.x) {
+    float4 pv[TP_MAX];
+#pragma unroll
+    for (int q = 0; q < TP_MAX; ++q)
+      if (q < world) pv[q] = __ldcv(reinterpret_cast<const float4*>(peers.p[q] + slot_off + (long long)r * n) + i4);
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < TP_MAX; ++q)
+      if (q < world) {
+        sum.x += pv[q].x; sum.y += pv[q].y; sum.z += pv[q].z; sum.w += pv[q].w;
+      }
+    float4 v = reinterpret_cast<float4*>(xr)[i4];
+    v.x += sum.x; v.y += sum.y; v.z += sum.z; v.w += sum.w;
+    reinterpret_cast<float4*>(xr)[i4] = v;
+    ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+  }
+  __shared__ float part[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) part[0] = v;
+  }
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(part[0] / (float)n + eps);
+  asm volatile("griddepcontrol.launch_dependents;");
+  float* o = out + (long long)r * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = (xr[i] * w[i]) * inv;
+}
+
 // rope (math.zig:88-104, interleaved pairs) on the row's Q and K heads, then
 // the KV-cache write of K and V at the row's position (forward.zig:268-269).
 struct RowInfo {
@@ -685,6 +781,12 @@ struct VtbCudaState {
   bool one_seq = false;     // every staged row belongs to one sequence
   cudaGraphExec_t graph = nullptr;
   int graph_rows = -1;
+  // tensor parallel over peer memory (rmsnorm_tp_kernel); false: NCCL all-reduce of tmp
+  bool p2p = false;
+  PeerPtrs peers = {};
+  int tp_rank = 0;
+  long long flag_off = 0;   // floats from a block's start to its flags
+  int par = 0;              // slot of the next all-reduce (host count mod 2; every call does an even number)
 };
 
 // Error text goes to the same thread-local buffer as the rest of the shim
@@ -696,6 +798,70 @@ static int mcuda(cudaError_t e) {
 }
 
 static bool q_ok(int q) { return host_quant_ok(q); }
+
+// Map every rank's shared block (IPC handles all-gathered over NCCL).  All
+// ranks agree on the outcome (NCCL min of the per-rank result), so either
+// every rank uses peer memory or every rank keeps the NCCL all-reduce.
+// Returns false only on an error that leaves the state unusable.
+static bool tp_p2p_setup(VtbCudaState* s) {
+  VtbCudaTp* tp = s->m->tp;
+  const int world = tp->world, me = tp->rank;
+  const size_t slot = (size_t)s->max_rows * s->m->c.dim;
+  s->flag_off = (long long)(2 * slot);
+  float* blk = nullptr;
+  if (cudaMalloc(&blk, (2 * slot + 2 * TP_MAX) * sizeof(float)) != cudaSuccess) {
+    mcuda(cudaGetLastError());
+    return false;
+  }
+  s->peers.p[me] = blk;
+  s->tp_rank = me;
+  uint8_t* dh = nullptr;  // [world][sizeof handle] + one int for the agreement
+  cudaIpcMemHandle_t h;
+  int ok = cudaMemsetAsync(blk, 0, (2 * slot + 2 * TP_MAX) * sizeof(float), s->st) == cudaSuccess &&
+           cudaIpcGetMemHandle(&h, blk) == cudaSuccess;
+  cudaGetLastError();
+  if (cudaMalloc(&dh, (size_t)world * sizeof h + 4) != cudaSuccess) {
+    mcuda(cudaGetLastError());
+    return false;
+  }
+  std::vector<uint8_t> hh((size_t)world * sizeof h);
+  bool fine = cudaMemcpyAsync(dh + (size_t)me * sizeof h, &h, sizeof h, cudaMemcpyHostToDevice, s->st) == cudaSuccess &&
+              ncclAllGather(dh + (size_t)me * sizeof h, dh, sizeof h, ncclUint8, tp->comm, s->st) == ncclSuccess &&
+              cudaMemcpyAsync(hh.data(), dh, hh.size(), cudaMemcpyDeviceToHost, s->st) == cudaSuccess &&
+              cudaStreamSynchronize(s->st) == cudaSuccess;
+  for (int r = 0; fine && ok && r < world; ++r) {
+    if (r == me) continue;
+    cudaIpcMemHandle_t hr;
+    memcpy(&hr, hh.data() + (size_t)r * sizeof h, sizeof h);
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+    } else {
+      s->peers.p[r] = static_cast<float*>(p);
+    }
+  }
+  int* dok = reinterpret_cast<int*>(dh + (size_t)world * sizeof h);
+  fine = fine && cudaMemcpyAsync(dok, &ok, 4, cudaMemcpyHostToDevice, s->st) == cudaSuccess &&
+         ncclAllReduce(dok, dok, 1, ncclInt32, ncclMin, tp->comm, s->st) == ncclSuccess &&
+         cudaMemcpyAsync(&ok, dok, 4, cudaMemcpyDeviceToHost, s->st) == cudaSuccess &&
+         cudaStreamSynchronize(s->st) == cudaSuccess;
+  cudaFree(dh);
+  if (!fine) {
+    merr(VTB_CUDA_ERR_COMM, "tensor parallel: peer-memory setup failed");
+    return false;
+  }
+  s->p2p = ok != 0;
+  return true;
+}
+
+static void tp_p2p_release(VtbCudaState* s) {
+  const int me = s->tp_rank;  // the model may already be gone
+  for (int r = 0; r < TP_MAX; ++r)
+    if (s->peers.p[r] && r != me) cudaIpcCloseMemHandle(s->peers.p[r]);
+  cudaFree(s->peers.p[me]);
+  s->peers = PeerPtrs{};
+}
 
 extern "C" {
 
@@ -938,6 +1104,10 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   s->tok = ib; s->seq = ib + R; s->pos = ib + 2 * R; s->amax = ib + 3 * R;
   cudaMemsetAsync(s->kc, 0, 2 * kvn * 4, s->st);
   s->seq_pos.assign(n_seqs, 0);
+  if (m->tp && m->tp->world > 1 && m->tp->world <= TP_MAX && !tp_p2p_setup(s)) {
+    vtb_cuda_state_destroy(s);
+    return nullptr;
+  }
   if (cudaStreamSynchronize(s->st) != cudaSuccess) {
     mcuda(cudaGetLastError());
     return nullptr;
@@ -950,6 +1120,7 @@ void vtb_cuda_state_destroy(VtbCudaState* s) {
   cudaSetDevice(s->device);
   cudaStreamSynchronize(s->st);
   if (s->graph) cudaGraphExecDestroy(s->graph);
+  tp_p2p_release(s);
   cudaStreamDestroy(s->st);
   cudaFree(s->x);
   cudaFree(s->tok);
@@ -963,6 +1134,8 @@ int vtb_cuda_state_reset(VtbCudaState* s) {
   for (auto& p : s->seq_pos) p = 0;
   return VTB_CUDA_OK;
 }
+
+int vtb_cuda_state_tp_p2p(const VtbCudaState* s) { return s && s->p2p ? 1 : 0; }
 
 int64_t vtb_cuda_state_pos(VtbCudaState* s, int32_t seq) {
   if (!s || seq < 0 || seq >= s->n_seqs) return -1;
@@ -1023,13 +1196,31 @@ static cudaError_t pdl_launch(K kern, dim3 grid, dim3 block, size_t smem, cudaSt
 // waiting in tmp is added to x first (addInto fused into the norm).
 static cudaError_t enqueue_norm(VtbCudaState* s, const float* w, int r0, int n) {
   const VtbCudaLlamaConfig& c = s->m->c;
+  if (s->pending && s->p2p) {  // the all-reduce itself happens here, over peer memory
+    s->pending = false;
+    const long long slot_off = (long long)(s->par ^ 1) * s->max_rows * c.dim + (long long)r0 * c.dim;
+    return pdl_launch(rmsnorm_tp_kernel, dim3(n), dim3(1024), 0, s->st, s->x + (size_t)r0 * c.dim, s->peers,
+                      s->m->tp->world, s->m->tp->rank, slot_off, s->flag_off, w, s->xb, c.dim, c.rms_eps);
+  }
   const float* res = s->pending ? s->tmp + (size_t)r0 * c.dim : nullptr;
   s->pending = false;
   return pdl_launch(rmsnorm_kernel, dim3(n), dim3(256), 0, s->st, s->x + (size_t)r0 * c.dim, res, w, s->xb, c.dim,
                     c.rms_eps);
 }
 
+// Destination of this rank's partial of the next all-reduce.
+static float* partial_out(VtbCudaState* s) {
+  return s->p2p ? s->peers.p[s->m->tp->rank] + (size_t)s->par * s->max_rows * s->m->c.dim : s->tmp;
+}
+
 static cudaError_t allreduce_tmp(VtbCudaState* s, size_t n) {
+  if (s->p2p) {  // publish this rank's partial; the next RMSNorm sums the ranks' slots
+    cudaError_t e = pdl_launch(tp_signal_kernel, dim3(1), dim3(32), 0, s->st, s->peers, s->m->tp->world,
+                               s->m->tp->rank, s->flag_off);
+    s->par ^= 1;
+    s->pending = true;
+    return e;
+  }
   const ncclResult_t r = ncclAllReduce(s->tmp, s->tmp, n, ncclFloat32, ncclSum, s->m->tp->comm, s->st);
   if (r != ncclSuccess) {
     nccl_status(r);
@@ -1079,7 +1270,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   // straight into x; tensor parallel writes the partial to tmp and all-reduces.
   auto residual = [&](int q, const uint8_t* w, const float* in, int k) -> cudaError_t {
     if (!tp) return proj(q, w, in, s->x, d, k, d, 1);
-    cudaError_t e2 = proj(q, w, in, s->tmp, d, k, d, 0);
+    cudaError_t e2 = proj(q, w, in, partial_out(s), d, k, d, 0);
     if (e2) return e2;
     return allreduce_tmp(s, (size_t)R * d);
   };

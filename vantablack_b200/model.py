@@ -240,6 +240,10 @@ class CudaState:
     def pos(self, seq: int = 0) -> int:
         return self.lib.vtb_cuda_state_pos(self.h, seq)
 
+    def tp_p2p(self) -> bool:
+        """True when tensor-parallel all-reduces go over NVLink peer memory."""
+        return bool(self.lib.vtb_cuda_state_tp_p2p(self.h))
+
     def step(self, tokens, want_logits: bool = True, graph: bool = True):
         """One token per sequence; returns (logits [n_seqs, vocab] or None, argmax [n_seqs])."""
         t = np.ascontiguousarray(np.atleast_1d(tokens), np.int32)
