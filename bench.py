@@ -385,6 +385,13 @@ def run_profile_case(case: str) -> None:
         acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
         for _ in range(2):
             ops.gemm(Q4_K, w, acts, m, k, precise=False)
+    elif case == "decode8b_b32":  # Llama-3-8B, 32 sequences: 3 decode steps of one token each
+        from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState, HostWeights
+        ctx = Context(0)
+        st = CudaState(CudaModel(ctx, HostWeights(LLAMA3_8B, seed=1)), 32, max_rows=32)
+        toks = np.arange(3, 35)
+        for _ in range(3):
+            _, toks = st.step(toks, want_logits=False)
     elif case in ("decode", "decode8b"):  # 128-token prefill + 5 decode steps (TinyLlama / Llama-3-8B)
         from vantablack_b200.model import LLAMA3_8B, TINYLLAMA, Context, CudaModel, CudaState, HostWeights
         ctx = Context(0)
@@ -408,7 +415,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--model-steps", type=int, default=32, help="decode steps of the 8B model metrics (0 = skip)")
-    ap.add_argument("--profile", choices=["gemv", "gemv_q6k", "gemm", "decode", "decode8b"], help="run a small case for ncu and exit")
+    ap.add_argument("--profile", choices=["gemv", "gemv_q6k", "gemm", "decode", "decode8b", "decode8b_b32"], help="run a small case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)

@@ -23,6 +23,7 @@
 // Every wait is bounded; a timeout sets the device error word, and all warps
 // still reach the TMEM dealloc.
 
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
@@ -227,7 +228,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int m0 = blockIdx.x * TC_BM, n0 = blockIdx.y * BN;
-  const int nk = K / TC_BK, nsb = K / 256;
+  // Split-K (gridDim.z > 1, K % 256 == 0): this CTA takes super-blocks [sb0, sb1) and
+  // writes its partial tile to out + z * NB * M; a reduce kernel sums the splits.
+  const int nsb = K / 256, z = blockIdx.z, ks = gridDim.z;
+  const int sb0 = ks > 1 ? z * nsb / ks : 0, sb1 = ks > 1 ? (z + 1) * nsb / ks : nsb;
+  const int kb0 = ks > 1 ? 4 * sb0 : 0, kb1 = ks > 1 ? 4 * sb1 : K / TC_BK;
+  out += (long long)z * NB * M;
   const long long rb = host_row_bytes_dev<Q>(K);
 
   if (tid == 0) {
@@ -257,20 +263,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       constexpr unsigned BBYTES = (unsigned)C::B_BYTES * (PASSES == 3 ? 2u : 1u);
-      int jr = 0;  // next raw weight super-block
-      for (int kb = 0; kb < nk && ok; ++kb) {
+      int jr = sb0;  // next raw weight super-block
+      for (int kb = kb0; kb < kb1 && ok; ++kb) {
+        const int i = kb - kb0;  // ring position
         if constexpr (TA) {  // weights run up to SR - 1 super-blocks ahead (independent of the activations)
-          while (jr < nsb && jr <= kb / 4 + C::SR - 1 && ok) {
-            const int rs = jr % C::SR;
-            if (jr >= C::SR && !mbar_wait_bounded(&rempty[rs], (unsigned)(((jr / C::SR) - 1) & 1))) { ok = false; break; }
+          while (jr < sb1 && jr - sb0 <= i / 4 + C::SR - 1 && ok) {
+            const int jl = jr - sb0, rs = jl % C::SR;
+            if (jl >= C::SR && !mbar_wait_bounded(&rempty[rs], (unsigned)(((jl / C::SR) - 1) & 1))) { ok = false; break; }
             mbar_expect_tx(&rfull[rs], (unsigned)C::RAW);
             tma_load_2d(raw + rs * C::RAW, &mapA, TmaA<Q>::x0(jr), m0, &rfull[rs]);
             ++jr;
           }
         }
-        if (kb == 0) asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
-        const int s = kb % S;
-        if (kb >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((kb / S) - 1) & 1))) { ok = false; break; }
+        if (i == 0) asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
+        const int s = i % S;
+        if (i >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((i / S) - 1) & 1))) { ok = false; break; }
         uint8_t* st = smem + s * C::STAGE;
         mbar_expect_tx(&full[s], BBYTES);
         tma_load_2d(st + C::A_BYTES, &mapBh, kb * TC_BK, n0, &full[s]);
@@ -282,18 +289,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
     const int r = tid;
     const bool row_ok = m0 + r < M;
     const uint8_t* wrow = W + (long long)(row_ok ? m0 + r : 0) * rb;
-    for (int kb = 0; kb < nk && ok; ++kb) {
-      const int s = kb % S, j = kb >> 2;
+    for (int kb = kb0; kb < kb1 && ok; ++kb) {
+      const int i = kb - kb0, s = i % S, j = kb >> 2, jl = j - sb0;
       if constexpr (TA) {
-        if ((kb & 3) == 0 && !mbar_wait_bounded(&rfull[j % C::SR], (unsigned)((j / C::SR) & 1))) { ok = false; break; }
+        if ((kb & 3) == 0 && !mbar_wait_bounded(&rfull[jl % C::SR], (unsigned)((jl / C::SR) & 1))) { ok = false; break; }
       }
-      if (kb >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((kb / S) - 1) & 1))) { ok = false; break; }
+      if (i >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((i / S) - 1) & 1))) { ok = false; break; }
       uint8_t* st = smem + s * C::STAGE;
       float v[64];
       if constexpr (TA) {  // this row's super-block sits at raw[j % SR] + r * BOX (out-of-range rows read as zeros)
-        dequant64<Q, true>(raw + (j % C::SR) * C::RAW + r * TmaA<Q>::BOX + (j * Fmt<Q>::bytes - TmaA<Q>::x0(j)),
+        dequant64<Q, true>(raw + (jl % C::SR) * C::RAW + r * TmaA<Q>::BOX + (j * Fmt<Q>::bytes - TmaA<Q>::x0(j)),
                            kb * TC_BK, v);
-        if ((kb & 3) == 3 || kb == nk - 1) mbar_arrive(&rempty[j % C::SR]);
+        if ((kb & 3) == 3 || kb == kb1 - 1) mbar_arrive(&rempty[jl % C::SR]);
       } else if (row_ok) {
         dequant64<Q>(wrow, kb * TC_BK, v);
       } else {
@@ -322,15 +329,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
   } else if (lane == 0) {
     // ---------------- MMA issuer (warp 4) ----------------
     const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
-    for (int kb = 0; kb < nk && ok; ++kb) {
-      const int s = kb % S;
-      if (!mbar_wait_bounded(&full[s], (unsigned)((kb / S) & 1))) { ok = false; break; }
+    for (int kb = kb0; kb < kb1 && ok; ++kb) {
+      const int i = kb - kb0, s = i % S;
+      if (!mbar_wait_bounded(&full[s], (unsigned)((i / S) & 1))) { ok = false; break; }
       tc_fence_after();
       const uint32_t a_hi = smem_u32(smem + s * C::STAGE), b_hi = a_hi + C::A_BYTES;
       const uint32_t a_lo = b_hi + C::B_BYTES, b_lo = a_lo + C::A_BYTES;
 #pragma unroll
       for (int kk = 0; kk < TC_BK / 16; ++kk) {  // K = 16 per MMA: +32 B within the swizzled row
-        const int acc = (kb | kk) != 0;
+        const int acc = (i | kk) != 0;
         mma_bf16(tmem, sw128_desc(a_hi + 32 * kk), sw128_desc(b_hi + 32 * kk), idesc, acc);
         if constexpr (PASSES == 3) {
           mma_bf16(tmem, sw128_desc(a_hi + 32 * kk), sw128_desc(b_lo + 32 * kk), idesc, 1);
@@ -380,7 +387,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
 
 template <int Q, int BN, int PASSES, int S, bool TA>
 static cudaError_t launch_gemm_tc_t(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
-                                    int k, int nb, cudaStream_t st) {
+                                    int k, int nb, int ks, cudaStream_t st) {
   using C = TcCfg<Q, BN, PASSES, S, TA>;
   auto kern = gemm_tc_kernel<Q, BN, PASSES, S, TA>;
   static bool attr = false;
@@ -407,7 +414,7 @@ static cudaError_t launch_gemm_tc_t(const void* w, const __nv_bfloat16* xh, cons
     mBl = mBh;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((m + TC_BM - 1) / TC_BM, (nb + BN - 1) / BN);
+  cfg.gridDim = dim3((m + TC_BM - 1) / TC_BM, (nb + BN - 1) / BN, ks);
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
@@ -429,40 +436,54 @@ constexpr int fit_stages() {
 
 template <int Q, int BN, int PASSES, bool TA>
 static cudaError_t launch_fit(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m, int k,
-                              int nb, cudaStream_t st) {
+                              int nb, int ks, cudaStream_t st) {
   constexpr int S = fit_stages<Q, BN, PASSES, TA, 5>();
   static_assert(TcCfg<Q, BN, PASSES, S, TA>::SMEM <= 227 * 1024, "GEMM tile does not fit in shared memory");
-  return launch_gemm_tc_t<Q, BN, PASSES, S, TA>(w, xh, xl, out, m, k, nb, st);
+  return launch_gemm_tc_t<Q, BN, PASSES, S, TA>(w, xh, xl, out, m, k, nb, ks, st);
 }
 
 template <int Q, bool TA>
 static cudaError_t launch_gemm_tc_qt(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
-                                     int k, int nb, bool precise, cudaStream_t st) {
+                                     int k, int nb, bool precise, int ks, cudaStream_t st) {
   if (precise) {  // hi + lo tiles: twice the shared memory per stage
-    if (nb <= 64) return launch_fit<Q, 64, 3, TA>(w, xh, xl, out, m, k, nb, st);
-    if (nb <= 128) return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, st);
+    if (nb <= 64) return launch_fit<Q, 64, 3, TA>(w, xh, xl, out, m, k, nb, ks, st);
+    if (nb <= 128) return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, ks, st);
     if constexpr (TcCfg<Q, 256, 3, 2, TA>::SMEM <= 227 * 1024)
-      return launch_fit<Q, 256, 3, TA>(w, xh, xl, out, m, k, nb, st);
+      return launch_fit<Q, 256, 3, TA>(w, xh, xl, out, m, k, nb, ks, st);
     else
-      return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, st);
+      return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, ks, st);
   }
-  if (nb <= 64) return launch_fit<Q, 64, 1, TA>(w, xh, xl, out, m, k, nb, st);
-  if (nb <= 128) return launch_fit<Q, 128, 1, TA>(w, xh, xl, out, m, k, nb, st);
-  return launch_fit<Q, 256, 1, TA>(w, xh, xl, out, m, k, nb, st);
+  if (nb <= 64) return launch_fit<Q, 64, 1, TA>(w, xh, xl, out, m, k, nb, ks, st);
+  if (nb <= 128) return launch_fit<Q, 128, 1, TA>(w, xh, xl, out, m, k, nb, ks, st);
+  return launch_fit<Q, 256, 1, TA>(w, xh, xl, out, m, k, nb, ks, st);
 }
 
 template <int Q>
 static cudaError_t launch_gemm_tc_q(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
-                                    int k, int nb, bool precise, cudaStream_t st) {
+                                    int k, int nb, bool precise, int ks, cudaStream_t st) {
   // TMA weight staging needs 16-byte row pitches (all K-quant configs with k % 2048 == 0 qualify)
   const bool ta = (Q != Q8_0) && host_row_bytes_dev<Q>(k) % 16 == 0;
-  if (ta) return launch_gemm_tc_qt<Q, true>(w, xh, xl, out, m, k, nb, precise, st);
-  return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, st);
+  if (ta) return launch_gemm_tc_qt<Q, true>(w, xh, xl, out, m, k, nb, precise, ks, st);
+  return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, ks, st);
+}
+
+// out[i] = sum over splits z of part[z][i], in split order (deterministic).
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, float* __restrict__ out, long long n, int ks) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    float v = part[i];
+    for (int z = 1; z < ks; ++z) v += part[(long long)z * n + i];
+    out[i] = v;
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // out[nb][m] = acts[nb][k] . W^T.  `ws` is bf16 scratch of nb*k*(precise ? 2 : 1) elements.
+// `part` (optional, `part_elems` floats): when the (M/128) x (B/BN) tile grid
+// leaves most SMs idle (small batches), K is split across up to 8 CTAs per
+// tile, each writing a partial tile there; splitk_reduce_kernel sums them.
 cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
-                           void* ws, cudaStream_t st) {
+                           void* ws, cudaStream_t st, float* part = nullptr, size_t part_elems = 0) {
   __nv_bfloat16* xh = static_cast<__nv_bfloat16*>(ws);
   __nv_bfloat16* xl = precise ? xh + (size_t)nb * k : nullptr;
   const long long n = (long long)nb * k;
@@ -478,13 +499,24 @@ cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, 
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, acts_to_bf16_kernel, acts, xh, xl, n);
   if (e != cudaSuccess) return e;
+  int ks = 1;
+  if (part && k % 256 == 0) {
+    const int bn = nb <= 64 ? 64 : nb <= 128 ? 128 : 256;
+    const long long tiles = (long long)((m + TC_BM - 1) / TC_BM) * ((nb + bn - 1) / bn);
+    while (ks < 8 && ks * 2 <= k / 256 && tiles * ks * 2 <= 148 && (size_t)ks * 2 * nb * m <= part_elems) ks *= 2;
+  }
+  float* dst = ks > 1 ? part : out;
   switch (q) {
-    case Q4_K: return launch_gemm_tc_q<Q4_K>(w, xh, xl, out, m, k, nb, precise, st);
-    case Q5_K: return launch_gemm_tc_q<Q5_K>(w, xh, xl, out, m, k, nb, precise, st);
-    case Q6_K: return launch_gemm_tc_q<Q6_K>(w, xh, xl, out, m, k, nb, precise, st);
-    case Q8_0: return launch_gemm_tc_q<Q8_0>(w, xh, xl, out, m, k, nb, precise, st);
+    case Q4_K: e = launch_gemm_tc_q<Q4_K>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
+    case Q5_K: e = launch_gemm_tc_q<Q5_K>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
+    case Q6_K: e = launch_gemm_tc_q<Q6_K>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
+    case Q8_0: e = launch_gemm_tc_q<Q8_0>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
     default: return cudaErrorInvalidValue;
   }
+  if (e != cudaSuccess || ks == 1) return e;
+  const long long on = (long long)nb * m;
+  cfg.gridDim = dim3((unsigned)std::min<long long>((on + 255) / 256, 148LL * 8));
+  return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, (const float*)part, out, on, ks);
 }
 
 }  // namespace vtb

@@ -34,7 +34,7 @@ cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, 
 cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* out, int dim, int n_tok,
                          cudaStream_t st);
 cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
-                           void* ws, cudaStream_t st);
+                           void* ws, cudaStream_t st, float* part, size_t part_elems);
 
 // Prefill steps with at least this many rows run their projections as one
 // tensor-core GEMM (precise mode) instead of one GEMV per row.
@@ -767,6 +767,8 @@ struct VtbCudaState {
   int n_seqs, max_rows;
   float *x, *xb, *qkv, *att, *gu, *h, *logits, *part, *tmp;
   void* ws;  // GEMM activation workspace (bf16 hi + lo)
+  float* gsplit = nullptr;  // split-K partial tiles of small-batch GEMMs
+  size_t gsplit_elems = 0;
   int32_t *tok, *seq, *pos, *amax;
   float *kc, *vc;
   int32_t* hbuf;            // pinned host staging: tok | seq | pos (3 * max_rows)
@@ -1078,8 +1080,10 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   const size_t R = max_rows, d = c.dim, hd = c.head_dim, qd = (size_t)m->H * hd, kvd = (size_t)m->KV * hd, f = m->F;
   const size_t qkvw = qd + 2 * kvd;
   const size_t kmax = d > f ? d : f;
+  // split-K partials for small-batch GEMMs: splits x rows <= 512 of the widest projection
+  const size_t gsplit = R >= (size_t)GEMM_MIN_ROWS ? 512 * std::max(std::max(qkvw, 2 * f), d) : 0;
   size_t fl = R * (d + d + qkvw + qd + 2 * f + f + (size_t)c.vocab_size + m->V + d + kmax) +
-              R * m->H * (size_t)s->nsplit * (hd + 2) + 64;
+              R * m->H * (size_t)s->nsplit * (hd + 2) + gsplit + 64;
   const size_t kvn = (size_t)n_seqs * c.n_layers * c.max_seq * kvd;
   float* base = nullptr;
   int32_t* ib = nullptr;
@@ -1100,6 +1104,8 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   s->part = carve(R * m->H * (size_t)s->nsplit * (hd + 2));
   s->tmp = carve(R * d);
   s->ws = carve(R * kmax);  // bf16 hi + lo = 4 bytes per activation
+  s->gsplit = gsplit ? carve(gsplit) : nullptr;
+  s->gsplit_elems = gsplit;
   s->kc = carve(kvn); s->vc = carve(kvn);
   s->tok = ib; s->seq = ib + R; s->pos = ib + 2 * R; s->amax = ib + 3 * R;
   cudaMemsetAsync(s->kc, 0, 2 * kvn * 4, s->st);
@@ -1253,12 +1259,12 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
     // out[r*ld_out + i] (+)= W . in[r]; GEMM rows need a dense out, so `acc` goes through tmp
     if (gemm && k % 64 == 0 && (acc || ld_out == mm)) {
       if (acc) {
-        cudaError_t e2 = launch_gemm_tc(q, w, in, s->tmp, mm, k, R, true, s->ws, st);
+        cudaError_t e2 = launch_gemm_tc(q, w, in, s->tmp, mm, k, R, true, s->ws, st, s->gsplit, s->gsplit_elems);
         if (e2) return e2;
         return pdl_launch(add_kernel, dim3(min(1184, (R * mm + 255) / 256)), dim3(256), 0, st, out,
                           (const float*)s->tmp, (long long)R * mm);
       }
-      return launch_gemm_tc(q, w, in, out, mm, k, R, true, s->ws, st);
+      return launch_gemm_tc(q, w, in, out, mm, k, R, true, s->ws, st, s->gsplit, s->gsplit_elems);
     }
     for (int r = 0; r < R; ++r) {
       cudaError_t e2 = gemv_any(q, w, in + (size_t)r * k, out + (size_t)r * ld_out, mm, k, st, acc);
@@ -1361,7 +1367,7 @@ static cudaError_t enqueue_final(VtbCudaState* s, bool last_only) {
   if ((e = enqueue_norm(s, m->out_norm, r0, n))) return e;
   float* lg = tp ? s->logits_local : s->logits;
   if (n >= GEMM_MIN_ROWS && c.dim % 64 == 0) {  // batch decode: one GEMM reads the LM head once for all rows
-    if ((e = launch_gemm_tc(m->q_out, m->out_w, s->xb, lg, m->V, c.dim, n, true, s->ws, st))) return e;
+    if ((e = launch_gemm_tc(m->q_out, m->out_w, s->xb, lg, m->V, c.dim, n, true, s->ws, st, s->gsplit, s->gsplit_elems))) return e;
   } else {
     for (int r = 0; r < n; ++r)
       if ((e = gemv_any(m->q_out, m->out_w, s->xb + (size_t)r * c.dim, lg + (size_t)r * m->V, m->V, c.dim, st, 0)))
