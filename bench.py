@@ -385,6 +385,12 @@ def run_profile_case(case: str) -> None:
         acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
         for _ in range(2):
             ops.gemm(Q4_K, w, acts, m, k, precise=False)
+    elif case == "gemm_b32":  # batch decode shape: Q6_K ffn_down 4096 x 14336, B = 32, precise mode, two launches
+        m, k, b = 4096, 14336, 32
+        w = torch.from_numpy(S.quant_tensor(rng, S.Q6_K, m, k)).cuda()
+        acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
+        for _ in range(2):
+            ops.gemm(S.Q6_K, w, acts, m, k, precise=True)
     elif case == "decode8b_b32":  # Llama-3-8B, 32 sequences: 3 decode steps of one token each
         from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState, HostWeights
         ctx = Context(0)
@@ -415,7 +421,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--model-steps", type=int, default=32, help="decode steps of the 8B model metrics (0 = skip)")
-    ap.add_argument("--profile", choices=["gemv", "gemv_q6k", "gemm", "decode", "decode8b", "decode8b_b32"], help="run a small case for ncu and exit")
+    ap.add_argument("--profile", choices=["gemv", "gemv_q6k", "gemm", "decode", "decode8b", "decode8b_b32", "gemm_b32"], help="run a small case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)
