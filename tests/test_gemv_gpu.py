@@ -134,6 +134,37 @@ def test_context_bridge_matmul():
     lib.vtb_cuda_destroy(ctx)
 
 
+def test_context_bridge_chained_matmuls():
+    """Context matmuls queued back to back: each output buffer feeds the next
+    matmul and the last one overwrites the chain's input buffer.  Each result
+    must match the oracle applied to the device's own previous output."""
+    from vantablack_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(9)
+    n = 2048
+    steps = [(S.Q4_K, lib.vtb_cuda_matmul_q4_k), (S.Q6_K, lib.vtb_cuda_matmul_q6_k), (S.Q5_K, lib.vtb_cuda_matmul_q5_k)]
+    ws = [S.quant_tensor(rng, q, n, n) for q, _ in steps]
+    x = S.activations(rng, n)
+    ctx = lib.vtb_cuda_init(0)
+    wb = [lib.vtb_cuda_upload(ctx, w.ctypes.data, w.nbytes) for w in ws]
+    bufs = [lib.vtb_cuda_upload(ctx, x.ctypes.data, x.nbytes), lib.vtb_cuda_alloc(ctx, n * 4, None),
+            lib.vtb_cuda_alloc(ctx, n * 4, None)]
+    chain = [(0, 1), (1, 2), (2, 0)]  # (input buffer, output buffer) per step
+    for (q, fn), b, (i, o) in zip(steps, wb, chain):
+        _lib.check(fn(ctx, bufs[o], b, 0, bufs[i], n, n), "matmul")
+    got = []
+    for o in (1, 2, 0):
+        y = np.empty(n, np.float32)
+        _lib.check(lib.vtb_cuda_copy_d2h(ctx, y.ctypes.data, bufs[o], 0, n * 4), "d2h")
+        got.append(y)
+    inputs = [x, got[0], got[1]]
+    for (q, _), w, xin, y in zip(steps, ws, inputs, got):
+        assert rel_err(y, O.matmul(q, w, xin, n, n)) <= TOL, S.NAMES[q]
+    for b in wb + bufs:
+        lib.vtb_cuda_release(b)
+    lib.vtb_cuda_destroy(ctx)
+
+
 @pytest.mark.parametrize("q", [S.Q4_K, S.Q6_K, S.Q8_0, S.Q5_K])
 @pytest.mark.parametrize("kind", ["huge", "tiny", "outliers", "zeros"])
 def test_gemv_activation_ranges(q, kind):

@@ -288,8 +288,11 @@ static int ctx_matmul(int q, VtbCudaCtx* c, VtbCudaBuf* out, VtbCudaBuf* w, size
   const int64_t rb = host_row_bytes(q, (int64_t)k);
   if (rb <= 0 || w_off + (size_t)rb * m > w->size || out->size < m * 4 || acts->size < k * 4)
     return set_err(VTB_CUDA_ERR_INVALID_ARG, "buffer too small for m x k");
+  // Programmatic dependent launch: consecutive matmuls on the context stream
+  // overlap launch and weight prefetch; each kernel reads acts and writes out
+  // only after waiting for its predecessor, so buffer reuse stays ordered.
   return vtb_cuda_gemv(q, (const char*)w->ptr + w_off, (const float*)acts->ptr, (float*)out->ptr, (int64_t)m,
-                       (int64_t)k, c->stream, 0);
+                       (int64_t)k, c->stream, 1);
 }
 
 int vtb_cuda_matmul_q8_0(VtbCudaCtx* c, VtbCudaBuf* o, VtbCudaBuf* w, size_t off, VtbCudaBuf* a, size_t m, size_t k) {

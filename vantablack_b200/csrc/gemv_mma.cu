@@ -189,6 +189,9 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
   };
   for (int tt = 0; tt < min(S, ntiles); ++tt) issue(tt);
 
+  // Let the next kernel in the stream launch now (its own wait still orders it
+  // after this grid completes): its CTAs start their weight prefetch on free SMs.
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   float inv = 1.f;
   if (norm_w) {  // sum of squares of the whole row (every CTA; x is L2-resident)
@@ -207,7 +210,6 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
   }
   build_x_shared(x, K, xsh, warp, lane, WARPS, norm_w, inv);
   __syncthreads();
-  asm volatile("griddepcontrol.launch_dependents;");
 
   const int gs = g >> 1;                  // sub-block (within a group of 4) whose B columns this lane holds
   const int boff = (g & 1) * 32 + t * 8;  // limb g&1, quad t

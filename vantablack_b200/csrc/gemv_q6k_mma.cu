@@ -145,10 +145,12 @@ gemv_q6k_mma_kernel(const __grid_constant__ CUtensorMap wmap, float* __restrict_
   };
   for (int tt = 0; tt < min(S, ntiles); ++tt) issue(tt);
 
+  // Let the next kernel in the stream launch now (its own wait still orders it
+  // after this grid completes): its CTAs start their weight prefetch on free SMs.
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   build_x_q6k(x, K, xq, xs, warp, lane, WARPS);
   __syncthreads();
-  asm volatile("griddepcontrol.launch_dependents;");
 
   bool ok = true;
   for (int ui = 0; ui < my_groups; ++ui) {
