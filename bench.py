@@ -234,8 +234,9 @@ def run_ours(args):
         _lib.check(lib.vtb_cuda_copy_h2d(ctx, xb, 0, hx.data_ptr(), K * 4), "h2d")
         for i in range(N_COPIES):
             _lib.check(lib.vtb_cuda_matmul_q4_k(ctx, ybufs[i], wbufs[i], 0, xb, M, K), "matmul")
-        for i in range(N_COPIES):
-            _lib.check(lib.vtb_cuda_copy_d2h(ctx, hy[i].data_ptr(), ybufs[i], 0, M * 4), "d2h")
+        for i in range(N_COPIES):  # read back after one wait, as the Metal bridge reads after waitIdle
+            _lib.check(lib.vtb_cuda_copy_d2h_async(ctx, hy[i].data_ptr(), ybufs[i], 0, M * 4), "d2h")
+        _lib.check(lib.vtb_cuda_wait_idle(ctx), "wait_idle")
 
     for _ in range(3):
         e2e_step()
@@ -253,7 +254,17 @@ def run_ours(args):
         lib.vtb_cuda_release(b)
     lib.vtb_cuda_destroy(ctx)
 
-    model = model_metrics(rank, world, local, dist, args) if args.model_steps > 0 else None
+    # The 8B model metrics build the whole seeded weight set (~5 GB host memory)
+    # on every rank, so they run at N <= 2 only; an error there is reported in
+    # the line instead of failing the GEMV measurement.
+    model = None
+    if args.model_steps > 0 and world <= 2:
+        try:
+            model = model_metrics(rank, world, local, dist, args)
+        except Exception as ex:  # noqa: BLE001 -- recorded in the JSON line
+            model = {"error": f"{type(ex).__name__}: {ex}"[:300]}
+    elif args.model_steps > 0:
+        model = {"skipped": "Llama-3-8B tensor-parallel metrics run at 1 or 2 GPUs (host memory per rank)"}
 
     if rank == 0:
         hbm, peak_kind = peaks()

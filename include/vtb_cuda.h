@@ -156,6 +156,11 @@ size_t vtb_cuda_buf_size(VtbCudaBuf *buf);
 int vtb_cuda_copy_h2d(VtbCudaCtx *ctx, VtbCudaBuf *dst, size_t dst_off, const void *src, size_t bytes);
 /* Waits for the context stream, then copies. */
 int vtb_cuda_copy_d2h(VtbCudaCtx *ctx, void *dst, VtbCudaBuf *src, size_t src_off, size_t bytes);
+/* Enqueues the copy on the context stream and returns at once; dst holds the
+ * data once vtb_cuda_wait_idle returns (the Metal bridge's read-after-
+ * waitIdle pattern, bridge.h, without a wait per buffer).  dst must stay valid
+ * until then; pinned host memory makes the copy asynchronous. */
+int vtb_cuda_copy_d2h_async(VtbCudaCtx *ctx, void *dst, VtbCudaBuf *src, size_t src_off, size_t bytes);
 /* Block until all work on the context stream is done (vtb_metal_wait_idle). */
 int vtb_cuda_wait_idle(VtbCudaCtx *ctx);
 

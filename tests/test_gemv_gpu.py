@@ -152,11 +152,10 @@ def test_context_bridge_chained_matmuls():
     chain = [(0, 1), (1, 2), (2, 0)]  # (input buffer, output buffer) per step
     for (q, fn), b, (i, o) in zip(steps, wb, chain):
         _lib.check(fn(ctx, bufs[o], b, 0, bufs[i], n, n), "matmul")
-    got = []
-    for o in (1, 2, 0):
-        y = np.empty(n, np.float32)
-        _lib.check(lib.vtb_cuda_copy_d2h(ctx, y.ctypes.data, bufs[o], 0, n * 4), "d2h")
-        got.append(y)
+    got = [np.empty(n, np.float32) for _ in range(3)]
+    for y, o in zip(got, (1, 2, 0)):  # asynchronous read-back, visible after one wait
+        _lib.check(lib.vtb_cuda_copy_d2h_async(ctx, y.ctypes.data, bufs[o], 0, n * 4), "d2h_async")
+    _lib.check(lib.vtb_cuda_wait_idle(ctx), "wait_idle")
     inputs = [x, got[0], got[1]]
     for (q, _), w, xin, y in zip(steps, ws, inputs, got):
         assert rel_err(y, O.matmul(q, w, xin, n, n)) <= TOL, S.NAMES[q]

@@ -47,6 +47,7 @@ SIGNATURES = {
     "vtb_cuda_buf_size": (_sz, [_vp]),
     "vtb_cuda_copy_h2d": (_int, [_vp, _vp, _sz, _vp, _sz]),
     "vtb_cuda_copy_d2h": (_int, [_vp, _vp, _vp, _sz, _sz]),
+    "vtb_cuda_copy_d2h_async": (_int, [_vp, _vp, _vp, _sz, _sz]),
     "vtb_cuda_wait_idle": (_int, [_vp]),
     "vtb_cuda_matmul_q8_0": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
     "vtb_cuda_matmul_q4_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),

@@ -277,6 +277,11 @@ int vtb_cuda_copy_d2h(VtbCudaCtx* c, void* dst, VtbCudaBuf* src, size_t off, siz
   return cuda_status(e);
 }
 
+int vtb_cuda_copy_d2h_async(VtbCudaCtx* c, void* dst, VtbCudaBuf* src, size_t off, size_t bytes) {
+  if (!use_ctx(c) || !dst || !src || off + bytes > src->size) return set_err(VTB_CUDA_ERR_INVALID_ARG, "bad d2h copy");
+  return cuda_status(cudaMemcpyAsync(dst, (const char*)src->ptr + off, bytes, cudaMemcpyDeviceToHost, c->stream));
+}
+
 int vtb_cuda_wait_idle(VtbCudaCtx* c) {
   if (!use_ctx(c)) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null context");
   return cuda_status(cudaStreamSynchronize(c->stream));

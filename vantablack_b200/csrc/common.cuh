@@ -6,6 +6,7 @@
 //   Q5_K 176 B / 256        : f16 d | f16 dmin | u8 scales[12] | u8 qh[32] | u8 qs[128]
 //   Q6_K 210 B / 256        : u8 ql[128] | u8 qh[64] | i8 sc[16] | f16 d
 #pragma once
+#include <atomic>
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -20,6 +21,51 @@ template <> struct Fmt<Q8_0> { static constexpr int bytes = 34, elems = 32; };
 template <> struct Fmt<Q4_K> { static constexpr int bytes = 144, elems = 256; };
 template <> struct Fmt<Q5_K> { static constexpr int bytes = 176, elems = 256; };
 template <> struct Fmt<Q6_K> { static constexpr int bytes = 210, elems = 256; };
+
+// ---- per-device launch facts ----
+// Kernel attributes (the dynamic shared-memory opt-in) and occupancy are per
+// device: a process that drives several GPUs must set them on each.  Caches
+// are lock-free (races only repeat an idempotent query).
+constexpr int VTB_MAX_DEVICES = 64;
+inline int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d >= 0 && d < VTB_MAX_DEVICES ? d : 0;
+}
+inline int sm_count(int dev) {
+  static std::atomic<int> cache[VTB_MAX_DEVICES];
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (!v) {
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (v < 1) v = 1;
+    cache[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+// Opt kernel KERN in to `bytes` of dynamic shared memory on device `dev` (once per size increase).
+template <auto KERN>
+cudaError_t ensure_smem_attr(int dev, int bytes) {
+  static std::atomic<int> set[VTB_MAX_DEVICES];
+  if (set[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(KERN, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) set[dev].store(bytes, std::memory_order_release);
+  return e;
+}
+// Resident CTAs per SM of KERN at (threads, smem) on device `dev`; the last answer is cached per device.
+template <auto KERN>
+int ctas_per_sm(int dev, int threads, int smem) {
+  static std::atomic<long long> cache[VTB_MAX_DEVICES];  // (smem << 16) | ctas
+  const long long c = cache[dev].load(std::memory_order_relaxed);
+  if (c && (c >> 16) == smem) return (int)(c & 0xffff);
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, KERN, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    n = 1;
+  }
+  if (n < 1) n = 1;
+  cache[dev].store(((long long)smem << 16) | n, std::memory_order_relaxed);
+  return n;
+}
 
 inline int64_t host_row_bytes(int q, int64_t k) {
   switch (q) {

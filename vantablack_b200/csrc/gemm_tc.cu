@@ -390,12 +390,8 @@ static cudaError_t launch_gemm_tc_t(const void* w, const __nv_bfloat16* xh, cons
                                     int k, int nb, int ks, cudaStream_t st) {
   using C = TcCfg<Q, BN, PASSES, S, TA>;
   auto kern = gemm_tc_kernel<Q, BN, PASSES, S, TA>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  cudaError_t ea = ensure_smem_attr<gemm_tc_kernel<Q, BN, PASSES, S, TA>>(current_device(), C::SMEM);
+  if (ea != cudaSuccess) return ea;
   CUtensorMap mA, mBh, mBl;
   memset(&mA, 0, sizeof mA);
   const uint64_t rbytes = (uint64_t)host_row_bytes_dev<Q>(k);

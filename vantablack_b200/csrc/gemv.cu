@@ -387,18 +387,10 @@ static cudaError_t launch_gemv_t(const void* w, const void* x, const float* dx, 
                                  cudaStream_t st, bool pdl, int accumulate = 0) {
   auto kern = gemv_kernel<Q, R, S, WARPS, XQ>;
   constexpr int smem = WARPS * S * R * Slot<Q>::BYTES + WARPS * S * 8;
-  static int max_ctas_per_sm = -1;
-  static int sms = 0;
-  if (max_ctas_per_sm < 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&max_ctas_per_sm, kern, WARPS * 32, smem);
-    if (e != cudaSuccess) return e;
-    if (max_ctas_per_sm < 1) max_ctas_per_sm = 1;
-  }
+  const int dev = current_device();
+  cudaError_t e = ensure_smem_attr<gemv_kernel<Q, R, S, WARPS, XQ>>(dev, smem);
+  if (e != cudaSuccess) return e;
+  const int sms = sm_count(dev), max_ctas_per_sm = ctas_per_sm<gemv_kernel<Q, R, S, WARPS, XQ>>(dev, WARPS * 32, smem);
   const int ngroups = (m + R - 1) / R;
   int grid = (ngroups + WARPS - 1) / WARPS;
   grid = grid < sms * max_ctas_per_sm ? grid : sms * max_ctas_per_sm;

@@ -335,23 +335,11 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
       return cudaErrorInvalidValue;
   }
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  static int set_for = 0, sms = 0, per_sm = 0;
-  if (smem > set_for) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    set_for = smem;
-  }
-  if (!sms) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  }
-  static int occ_smem = -1;
-  if (occ_smem != smem) {  // occupancy depends on k through the shared x buffer
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, smem);
-    if (per_sm < 1) per_sm = 1;
-    occ_smem = smem;
-  }
+  const int dev = current_device();
+  cudaError_t ea = ensure_smem_attr<gemv_q4k_mma_kernel<WARPS, S, CHB, TM>>(dev, 227 * 1024);
+  if (ea != cudaSuccess) return ea;
+  // occupancy depends on k through the shared x buffer
+  const int sms = sm_count(dev), per_sm = ctas_per_sm<gemv_q4k_mma_kernel<WARPS, S, CHB, TM>>(dev, WARPS * 32, smem);
   const int units = (m + MmaQ4K<CHB, TM>::ROWS - 1) / MmaQ4K<CHB, TM>::ROWS;
   const int nch = (k / 256 + CHB - 1) / CHB;
   const int cap = sms * per_sm;

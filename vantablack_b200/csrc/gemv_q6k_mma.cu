@@ -247,21 +247,10 @@ static cudaError_t launch_q6k_mma_t(const void* w, const float* x, float* y, int
   if (!make_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, rbytes / 4, (uint64_t)m, rbytes, Q6M_BOXB / 4, Q6M_ROWS,
                  CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
-  static bool attr_set = false;
-  static int sms = 0, per_sm = 0, occ_smem = -1;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    attr_set = true;
-  }
-  if (occ_smem != smem) {
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, smem);
-    if (per_sm < 1) per_sm = 1;
-    occ_smem = smem;
-  }
+  const int dev = current_device();
+  cudaError_t ea = ensure_smem_attr<gemv_q6k_mma_kernel<WARPS, S>>(dev, 227 * 1024);
+  if (ea != cudaSuccess) return ea;
+  const int sms = sm_count(dev), per_sm = ctas_per_sm<gemv_q6k_mma_kernel<WARPS, S>>(dev, WARPS * 32, smem);
   const int units = (m + Q6M_ROWS - 1) / Q6M_ROWS;
   const int nch = k / 512;
   const int cap = sms * per_sm;
