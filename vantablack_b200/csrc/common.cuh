@@ -42,6 +42,28 @@ inline int sm_count(int dev) {
   }
   return v;
 }
+// K-split of a persistent GEMV with `units` row units of `nch` K chunks each,
+// `warps` warps per CTA and `cap` resident CTAs: the divisor d of `warps`
+// (d <= nch) that minimises the per-warp critical path, rounds x ceil(nch/d),
+// where `warps/d` units share a CTA and rounds = ceil(groups / grid).  Ties go
+// to the larger grid (more SMs streaming), then to the smaller d.
+inline int pick_ksplit(int units, int nch, int warps, int cap) {
+  int best = 1;
+  long long best_cost = -1, best_grid = 0;
+  for (int d = 1; d <= warps && d <= nch; ++d) {
+    if (warps % d) continue;
+    const long long slots = warps / d, groups = (units + slots - 1) / slots;
+    const long long grid = groups < cap ? groups : cap, rounds = (groups + grid - 1) / grid;
+    const long long cost = rounds * ((nch + d - 1) / d);
+    if (best_cost < 0 || cost < best_cost || (cost == best_cost && grid > best_grid)) {
+      best = d;
+      best_cost = cost;
+      best_grid = grid;
+    }
+  }
+  return best;
+}
+
 // Opt kernel KERN in to `bytes` of dynamic shared memory on device `dev` (once per size increase).
 template <auto KERN>
 cudaError_t ensure_smem_attr(int dev, int bytes) {

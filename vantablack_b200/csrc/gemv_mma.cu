@@ -343,8 +343,7 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
   const int units = (m + MmaQ4K<CHB, TM>::ROWS - 1) / MmaQ4K<CHB, TM>::ROWS;
   const int nch = (k / 256 + CHB - 1) / CHB;
   const int cap = sms * per_sm;
-  int ksplit = 1;  // smallest power of two that gives every resident warp a unit
-  while (ksplit < WARPS && ksplit < nch && (long long)units * ksplit < (long long)cap * WARPS) ksplit *= 2;
+  int ksplit = pick_ksplit(units, nch, WARPS, cap);
   const int groups = (units + WARPS / ksplit - 1) / (WARPS / ksplit);
   const int grid = groups < cap ? groups : cap;
   cudaLaunchConfig_t cfg = {};

@@ -254,12 +254,7 @@ static cudaError_t launch_q6k_mma_t(const void* w, const float* x, float* y, int
   const int units = (m + Q6M_ROWS - 1) / Q6M_ROWS;
   const int nch = k / 512;
   const int cap = sms * per_sm;
-  int ksplit = 1;  // smallest divisor of WARPS (at most nch) that gives every resident warp a unit
-  for (int d = 1; d <= WARPS && d <= nch; ++d) {
-    if (WARPS % d) continue;
-    ksplit = d;
-    if ((long long)units * d >= (long long)cap * WARPS) break;
-  }
+  int ksplit = pick_ksplit(units, nch, WARPS, cap);
   const int groups = (units + WARPS / ksplit - 1) / (WARPS / ksplit);
   const int grid = groups < cap ? groups : cap;
   cudaLaunchConfig_t cfg = {};
