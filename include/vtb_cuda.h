@@ -34,6 +34,8 @@ extern "C" {
 
 #define VTB_CUDA_OK 0
 #define VTB_CUDA_ERR_INVALID_ARG (-1)
+#define VTB_CUDA_ERR_FILE_OPEN (-2) /* VTB_ERR_FILE_OPEN: a GGUF file cannot be opened or mapped */
+#define VTB_CUDA_ERR_PARSE (-3)     /* VTB_ERR_PARSE: malformed GGUF or missing model metadata */
 #define VTB_CUDA_ERR_OOM (-4)
 #define VTB_CUDA_ERR_DEVICE (-5)
 #define VTB_CUDA_ERR_DISPATCH (-6)
@@ -61,6 +63,9 @@ int vtb_cuda_available(void);
 const char *vtb_cuda_status_string(int status);
 /* Text of the last CUDA error this thread saw inside the library. */
 const char *vtb_cuda_last_error(void);
+/* Status of the last failure recorded with that text (for calls that return
+ * a NULL handle, e.g. vtb_cuda_gguf_open: -2 open / map, -3 malformed). */
+int vtb_cuda_last_status(void);
 /* Bytes per row of k weights in `quant` format (forward.zig rowBytes :629-641);
  * -1 if unsupported or k is not a whole number of blocks. */
 int64_t vtb_cuda_row_bytes(int quant, int64_t k);
@@ -283,6 +288,45 @@ VtbCudaModel *vtb_cuda_model_create_tp(VtbCudaCtx *ctx, VtbCudaTp *tp, const Vtb
                                        const VtbCudaLayerWeights *layers, const void *token_embd,
                                        int32_t q_token_embd, const float *output_norm, const void *output_w,
                                        int32_t q_output);
+
+/* ---- GGUF files (src/core/parser.zig, src/core/mapper.zig; src/runtime/
+ * model.zig LlamaConfig.fromCatalog and Model.init) ----
+ * vtb_cuda_gguf_open maps the file read-only and parses the v2/v3 header,
+ * the typed metadata and the tensor descriptors; tensor bytes stay in the
+ * map (zero-copy) until a model upload reads them.  Errors: -2 open / map,
+ * -3 malformed file (not GGUF, unsupported version, truncation, unknown
+ * metadata type, arrays nested deeper than 4, element counts that overflow
+ * or do not fill whole blocks, tensors outside the file). */
+typedef struct VtbCudaGguf VtbCudaGguf;
+#define VTB_CUDA_GGUF_MAX_DIMS 8
+VtbCudaGguf *vtb_cuda_gguf_open(const char *path);
+void vtb_cuda_gguf_close(VtbCudaGguf *g);
+int vtb_cuda_gguf_info(const VtbCudaGguf *g, uint32_t *version, uint32_t *alignment, uint64_t *data_offset,
+                       int64_t *n_tensors, int64_t *n_meta);
+/* Descriptor i (file order): name (NUL-terminated, owned by g), ggml type id,
+ * dims (ne0 = innermost; up to VTB_CUDA_GGUF_MAX_DIMS written), offset from
+ * the data segment and byte size (0 for types without a known block size). */
+int vtb_cuda_gguf_tensor_info(const VtbCudaGguf *g, int64_t i, const char **name, uint32_t *ggml_type,
+                              uint32_t *n_dims, uint64_t *dims, uint64_t *rel_offset, uint64_t *size_bytes);
+/* Bounds-checked pointer to a tensor's bytes inside the map (tensorSlice). */
+const void *vtb_cuda_gguf_tensor(const VtbCudaGguf *g, const char *name, uint32_t *ggml_type,
+                                 uint64_t *size_bytes);
+int vtb_cuda_gguf_meta_int(const VtbCudaGguf *g, const char *key, int64_t *out);
+int vtb_cuda_gguf_meta_float(const VtbCudaGguf *g, const char *key, double *out);
+int vtb_cuda_gguf_meta_string(const VtbCudaGguf *g, const char *key, const char **ptr, uint64_t *len);
+int vtb_cuda_gguf_meta_array(const VtbCudaGguf *g, const char *key, uint32_t *elem_type, uint64_t *count);
+/* The Llama configuration from `llama.*` metadata (head_count_kv defaults to
+ * head_count, rope.freq_base to 10000, layer_norm_rms_epsilon to 1e-5, the
+ * vocabulary to the token list's length); other architectures: -8. */
+int vtb_cuda_gguf_llama_config(const VtbCudaGguf *g, VtbCudaLlamaConfig *cfg);
+/* Model.init + upload: blk.N.{attn_norm,attn_q,attn_k,attn_v,attn_output,
+ * ffn_norm,ffn_gate,ffn_up,ffn_down}.weight, token_embd.weight,
+ * output_norm.weight, output.weight (absent: tied to token_embd).  Shapes and
+ * types are checked (norms f32; projections Q8_0/Q4_K/Q5_K/Q6_K).  max_seq > 0
+ * replaces the file's context_length (it sizes every state's KV cache).  The
+ * file may be closed once the model exists. */
+VtbCudaModel *vtb_cuda_model_create_gguf(VtbCudaCtx *ctx, const VtbCudaGguf *g, int32_t max_seq);
+VtbCudaModel *vtb_cuda_model_create_gguf_tp(VtbCudaCtx *ctx, VtbCudaTp *tp, const VtbCudaGguf *g, int32_t max_seq);
 
 #ifdef __cplusplus
 }

@@ -45,6 +45,28 @@ def test_llama3_8b_greedy_identical():
     assert float(np.abs(lg - lg_ref).max() / np.abs(lg_ref).max()) <= 1e-3
 
 
+def test_llama3_8b_full_config_vs_golden():
+    """BASELINE config 5 at full size — 2048-token prefill + 512 greedy steps —
+    against the oracle's token ids and final logits stored in
+    tests/golden/llama3_8b_p2048_g512.npz (tests/golden/make_llama3_8b_full.py)."""
+    import os
+    from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "llama3_8b_p2048_g512.npz")
+    if not os.path.exists(path):
+        pytest.skip("golden fixture not generated")
+    g = np.load(path)
+    n_prompt, n_gen = int(g["n_prompt"]), int(g["n_gen"])
+    w = HostWeights(LLAMA3_8B, seed=int(g["seed_w"]))
+    prompt = np.random.default_rng(int(g["seed_p"])).integers(3, LLAMA3_8B.vocab_size, n_prompt)
+    st = CudaState(CudaModel(Context(0), w), 1, max_rows=n_prompt)
+    ids, lg = st.generate_greedy(prompt, n_gen, use_prefill=True)
+    ids_ref = [int(v) for v in g["ids"]]
+    first_diff = next((i for i, (a, b) in enumerate(zip(ids, ids_ref)) if a != b), None)
+    assert first_diff is None, f"first differing decode step: {first_diff}"
+    lg_ref = g["logits"]
+    assert float(np.abs(lg - lg_ref).max() / np.abs(lg_ref).max()) <= 1e-3
+
+
 def test_llama3_8b_batch32_subset():
     """Batch-32 decode of the 8B architecture: all 32 sequences for the first
     steps, two of them checked against independent oracle runs."""

@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(HERE, "libvtbcuda.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "vtb_cuda.h")
 
 OK = 0
-STATUS = {0: "ok", -1: "invalid argument", -4: "out of device memory", -5: "no usable CUDA device",
+STATUS = {0: "ok", -1: "invalid argument", -2: "file cannot be opened", -3: "malformed model file", -4: "out of device memory", -5: "no usable CUDA device",
           -6: "kernel dispatch failed", -8: "unsupported quant type", -9: "device-side wait timed out",
           -10: "collective communication failed"}
 
@@ -26,6 +26,7 @@ SIGNATURES = {
     "vtb_cuda_available": (_int, []),
     "vtb_cuda_status_string": (C.c_char_p, [_int]),
     "vtb_cuda_last_error": (C.c_char_p, []),
+    "vtb_cuda_last_status": (_int, []),
     "vtb_cuda_row_bytes": (_i64, [_int, _i64]),
     "vtb_cuda_check_device_error": (_int, []),
     "vtb_cuda_gemv": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _int]),
@@ -75,6 +76,18 @@ SIGNATURES = {
     "vtb_cuda_tp_shard_plan": (_int, [_vp, _int, _int, _i32, _vp]),
     "vtb_cuda_tp_slice": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "vtb_cuda_model_create_tp": (_vp, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _i32]),
+    "vtb_cuda_gguf_open": (_vp, [C.c_char_p]),
+    "vtb_cuda_gguf_close": (None, [_vp]),
+    "vtb_cuda_gguf_info": (_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "vtb_cuda_gguf_tensor_info": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "vtb_cuda_gguf_tensor": (_vp, [_vp, C.c_char_p, _vp, _vp]),
+    "vtb_cuda_gguf_meta_int": (_int, [_vp, C.c_char_p, _vp]),
+    "vtb_cuda_gguf_meta_float": (_int, [_vp, C.c_char_p, _vp]),
+    "vtb_cuda_gguf_meta_string": (_int, [_vp, C.c_char_p, _vp, _vp]),
+    "vtb_cuda_gguf_meta_array": (_int, [_vp, C.c_char_p, _vp, _vp]),
+    "vtb_cuda_gguf_llama_config": (_int, [_vp, _vp]),
+    "vtb_cuda_model_create_gguf": (_vp, [_vp, _vp, _i32]),
+    "vtb_cuda_model_create_gguf_tp": (_vp, [_vp, _vp, _vp, _i32]),
 }
 
 

@@ -28,9 +28,11 @@ cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, 
 using namespace vtb;
 
 static thread_local char g_last_err[256] = "";
+static thread_local int g_last_status = 0;
 
 static int set_err(int status, const char* fmt, const char* detail = "") {
   snprintf(g_last_err, sizeof g_last_err, fmt, detail);
+  g_last_status = status;
   return status;
 }
 static int cuda_status(cudaError_t e) {
@@ -77,11 +79,14 @@ const char* vtb_cuda_status_string(int s) {
     case VTB_CUDA_ERR_UNSUPPORTED: return "unsupported quant type";
     case VTB_CUDA_ERR_TIMEOUT: return "device-side bounded wait timed out";
     case VTB_CUDA_ERR_COMM: return "collective communication failed";
+    case VTB_CUDA_ERR_FILE_OPEN: return "file cannot be opened";
+    case VTB_CUDA_ERR_PARSE: return "malformed model file";
     default: return "unknown status";
   }
 }
 
 const char* vtb_cuda_last_error(void) { return g_last_err; }
+int vtb_cuda_last_status(void) { return g_last_status; }
 
 int64_t vtb_cuda_row_bytes(int quant, int64_t k) {
   if (k < 0 || (quant != F32 && (!host_quant_ok(quant) || k % host_block_elems(quant)))) return -1;

@@ -9,4 +9,5 @@
 #include "api.cu"
 #include "tp.cu"
 #include "model.cu"
+#include "gguf.cu"
 #include "noalloc.cu"

@@ -197,6 +197,19 @@ class CudaModel:
         if not self.h:
             raise _lib.VtbError(-1, "vtb_cuda_model_create")
 
+    @classmethod
+    def from_gguf(cls, ctx: Context, gguf, max_seq: int = 0, tp: "TensorParallel | None" = None) -> "CudaModel":
+        """Model.init from a GGUF file (vtb_cuda_model_create_gguf[_tp]); `gguf` is a
+        vantablack_b200.gguf.GgufFile.  max_seq > 0 replaces the file's context length."""
+        self = cls.__new__(cls)
+        self.ctx, self.lib, self.tp = ctx, ctx.lib, tp
+        cfg = gguf.llama_config()
+        self.cfg = cfg.with_(max_seq=max_seq) if max_seq > 0 else cfg
+        self.h = self.lib.vtb_cuda_model_create_gguf_tp(ctx.h, tp.h if tp else None, gguf.h, max_seq)
+        if not self.h:
+            raise _lib.VtbError(self.lib.vtb_cuda_last_status(), "vtb_cuda_model_create_gguf")
+        return self
+
     @property
     def weight_bytes(self) -> int:
         return self.lib.vtb_cuda_model_weight_bytes(self.h)
