@@ -41,6 +41,7 @@ GEMV_SHAPES = [
     (S.Q5_K, 4096, 4096), (S.Q5_K, 1000, 2304),
     (S.Q4_K, 1, 256), (S.Q6_K, 3, 256), (S.Q8_0, 5, 32), (S.Q4_K, 7, 2560),  # tiny / ragged tails
     (S.Q4_K, 4111, 4608), (S.Q4_K, 96, 24576),  # ragged last 32-row tile at size; long-K fallback
+    (S.Q4_K, 6144, 4096), (S.Q4_K, 1000, 2048),  # 16-row tiles (large and small launch variants)
     (S.Q6_K, 1000, 6144), (S.Q6_K, 17, 2048),  # Q6_K tensor-core path: ragged last 16-row tile
 ]
 

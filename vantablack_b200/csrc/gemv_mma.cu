@@ -122,20 +122,21 @@ __device__ __forceinline__ void build_x_shared(const float* __restrict__ x, int 
 // bulk copy per row into rows padded to 12 (mod 32) words.  Per-row copies of
 // a few hundred bytes cap the stream near 5 TB/s on their issue rate alone;
 // one box per tile moves the same bytes with 32x fewer copy operations.
-template <int CHB, bool TM>
+template <int CHB, bool TM, int ROWS_ = 32>
 struct MmaQ4K {
-  static constexpr int ROWS = 32;  // two m16 MMA tiles per warp tile
+  static constexpr int ROWS = ROWS_;  // 32 (two m16 MMA tiles per warp tile) or 16 (one)
   static constexpr int BB = 144;
   static constexpr int SLOT = TM ? CHB * BB : CHB * BB + 16;
   static constexpr int STAGE = ROWS * SLOT;
   static_assert(!TM || CHB == 1, "2-D TMA tiles hold one super-block per row");
 };
 
-template <int WARPS, int S, int CHB, bool TM>
+template <int WARPS, int S, int CHB, bool TM, int ROWS>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
                     int ksplit, int accumulate, const float* __restrict__ norm_w, float eps) {
-  using C = MmaQ4K<CHB, TM>;
+  using C = MmaQ4K<CHB, TM, ROWS>;
+  constexpr int MT = ROWS / 16, NI = 2 * MT;  // m16 tiles; rows g + 8i this lane holds
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -219,7 +220,7 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
   for (int ui = 0; ui < my_groups; ++ui) {
     const int u = (blockIdx.x + ui * gridDim.x) * slots + slot;
     const int r0 = u * C::ROWS, nr = max(0, min(C::ROWS, M - r0));
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24; this lane's sub-blocks t and 4+t
+    float acc[NI] = {};  // rows g + 8i; this lane's sub-blocks t and 4+t
     for (int ci = 0; ci < my_chunks && ok; ++ci) {
       const int tt = ui * my_chunks + ci, st = tt % S;
       const int c = kpart + ksplit * ci, b0 = c * CHB, nblk = min(CHB, nb - b0);
@@ -228,10 +229,10 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
       for (int bi = 0; bi < nblk; ++bi) {
         const int sb = b0 + bi;
         const uint8_t* blk = base + bi * C::BB;
-        uint4 hd[4];
-        float dd[4], dm[4], nd[4], nm[4];
+        uint4 hd[NI];
+        float dd[NI], dm[NI], nd[NI], nm[NI];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < NI; ++i) {
           hd[i] = *reinterpret_cast<const uint4*>(blk + 8 * i * C::SLOT);
           dd[i] = h2f((uint16_t)(hd[i].x & 0xffffu));
           dm[i] = h2f((uint16_t)(hd[i].x >> 16));
@@ -243,8 +244,8 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
           const int8_t* xb = xsh.xq + (sb * 8 + 4 * grp + gs) * 128 + boff;
           const uint2 bx = *reinterpret_cast<const uint2*>(xb);        // limb (g&1)
           const uint2 bz = *reinterpret_cast<const uint2*>(xb + 64);   // limb 2 + (g&1)
-          int D[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // [m-tile][frag], limbs 0/1
-          int E[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // limbs 2/3
+          int D[MT][4] = {};  // [m-tile][frag], limbs 0/1
+          int E[MT][4] = {};  // limbs 2/3
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {
             const int p = 2 * grp + jj;  // nibble pair p: sub-blocks 2p (low), 2p+1 (high)
@@ -255,7 +256,7 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
             const uint32_t zh0 = mhi ? bz.x : 0u, zh1 = mhi ? bz.y : 0u;
             const int q0 = 16 + 32 * p + 4 * t;
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
+            for (int mt = 0; mt < MT; ++mt) {
               const uint8_t* r = blk + 16 * mt * C::SLOT;
               const uint32_t a0 = *reinterpret_cast<const uint32_t*>(r + q0);
               const uint32_t a1 = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + q0);
@@ -273,7 +274,7 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
           const float2 xs = xsh.xs[sb * 8 + 4 * grp + t];
           const float fx = xs.x * qscale;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < NI; ++i) {
             const int mt = i >> 1, e = (i & 1) * 2;
             // limbs combined exactly in int32 (|D0*254 + D1| < 2^27), then converted once
             const float hi = (float)(D[mt][e] * 254 + D[mt][e + 1]);
@@ -298,16 +299,16 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
       __syncwarp();
       if (tt + S < ntiles) issue(tt + S);
     }
-    // CTA reduction of the K-split partial sums for this unit's 32 rows.
+    // CTA reduction of the K-split partial sums for this unit's rows.
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < NI; ++i) {
       float v = acc[i];
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
       if (t == 0) red[warp * 32 + 16 * (i >> 1) + 8 * (i & 1) + g] = v;
     }
     __syncthreads();
-    if (kpart == 0) {
+    if (kpart == 0 && lane < ROWS) {
       float v = 0.f;
       for (int w = 0; w < min(ksplit, nch); ++w) v += red[(warp + w) * 32 + lane];
       if (lane < nr) y[r0 + lane] = accumulate ? y[r0 + lane] + v : v;
@@ -316,31 +317,32 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
   }
 }
 
-template <int WARPS, int S, int CHB, bool TM>
+template <int WARPS, int S, int CHB, bool TM, int ROWS = 32>
 constexpr int q4k_mma_smem(int k) {
-  return WARPS * S * MmaQ4K<CHB, TM>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
+  return WARPS * S * MmaQ4K<CHB, TM, ROWS>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
 }
 
-template <int WARPS, int S, int CHB, bool TM>
+template <int WARPS, int S, int CHB, bool TM, int ROWS>
 static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                     int accumulate, const float* norm_w, float eps) {
-  auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB, TM>;
-  const int smem = q4k_mma_smem<WARPS, S, CHB, TM>(k);
+  using C = MmaQ4K<CHB, TM, ROWS>;
+  constexpr auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB, TM, ROWS>;
+  const int smem = q4k_mma_smem<WARPS, S, CHB, TM, ROWS>(k);
   CUtensorMap wmap;
   memset(&wmap, 0, sizeof wmap);
-  if (TM) {  // [m rows][k/256 * 36 u32]: one box = 32 rows x 144 B
+  if (TM) {  // [m rows][k/256 * 36 u32]: one box = ROWS rows x 144 B
     const uint64_t rbytes = (uint64_t)(k / 256) * 144;
-    if (!make_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, rbytes / 4, (uint64_t)m, rbytes, 36, 32,
+    if (!make_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, rbytes / 4, (uint64_t)m, rbytes, 36, ROWS,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
       return cudaErrorInvalidValue;
   }
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   const int dev = current_device();
-  cudaError_t ea = ensure_smem_attr<gemv_q4k_mma_kernel<WARPS, S, CHB, TM>>(dev, 227 * 1024);
+  cudaError_t ea = ensure_smem_attr<kern>(dev, 227 * 1024);
   if (ea != cudaSuccess) return ea;
   // occupancy depends on k through the shared x buffer
-  const int sms = sm_count(dev), per_sm = ctas_per_sm<gemv_q4k_mma_kernel<WARPS, S, CHB, TM>>(dev, WARPS * 32, smem);
-  const int units = (m + MmaQ4K<CHB, TM>::ROWS - 1) / MmaQ4K<CHB, TM>::ROWS;
+  const int sms = sm_count(dev), per_sm = ctas_per_sm<kern>(dev, WARPS * 32, smem);
+  const int units = (m + C::ROWS - 1) / C::ROWS;
   const int nch = (k / 256 + CHB - 1) / CHB;
   const int cap = sms * per_sm;
   int ksplit = pick_ksplit(units, nch, WARPS, cap);
@@ -359,17 +361,33 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
   return cudaLaunchKernelEx(&cfg, kern, wmap, (const uint8_t*)w, x, y, m, k, ksplit, accumulate, norm_w, eps);
 }
 
+// Critical-path cost (in 32-row tile units) of a row-tile height: rounds x
+// chunks per warp from pick_ksplit; a 16-row tile costs ~0.6 of a 32-row one
+// (its MMAs and epilogue halve, its activation-fragment work does not).
+static double q4k_tile_cost(int m, int k, int rows, int warps, int cap) {
+  const int units = (m + rows - 1) / rows, nch = k / 256;
+  const int ks = pick_ksplit(units, nch, warps, cap);
+  const long long slots = warps / ks, groups = (units + slots - 1) / slots;
+  const long long grid = groups < cap ? groups : cap, rounds = (groups + grid - 1) / grid;
+  return (double)(rounds * ((nch + ks - 1) / ks)) * (rows == 16 ? 0.6 : 1.0);
+}
+
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                 int accumulate, const float* norm_w = nullptr, float eps = 0.f) {
   // One 2-D TMA box per tile.  Matrices above 2^24 weights stream with two
   // stages per warp; smaller ones (dominated by the dependent-launch chain)
   // with one.  Very long rows (x staged in shared memory at 4.25 B per column)
-  // fall back to 8 warps.
+  // fall back to 8 warps.  The row-tile height (32 or 16) is the one whose
+  // launch balances better over the SMs.
   if (q4k_mma_smem<16, 2, 1, true>(k) > 227 * 1024)
-    return launch_q4k_mma_t<8, 2, 1, true>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+    return launch_q4k_mma_t<8, 2, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+  const int sms = sm_count(current_device());
+  const bool r16 = q4k_tile_cost(m, k, 16, 16, sms) < q4k_tile_cost(m, k, 32, 16, sms);
   if ((long long)m * k > (1LL << 24))
-    return launch_q4k_mma_t<16, 2, 1, true>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
-  return launch_q4k_mma_t<16, 1, 1, true>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+    return r16 ? launch_q4k_mma_t<16, 2, 1, true, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps)
+               : launch_q4k_mma_t<16, 2, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+  return r16 ? launch_q4k_mma_t<16, 1, 1, true, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps)
+             : launch_q4k_mma_t<16, 1, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
 }
 
 }  // namespace vtb
