@@ -59,10 +59,17 @@ def test_llama3_8b_full_config_vs_golden():
     w = HostWeights(LLAMA3_8B, seed=int(g["seed_w"]))
     prompt = np.random.default_rng(int(g["seed_p"])).integers(3, LLAMA3_8B.vocab_size, n_prompt)
     st = CudaState(CudaModel(Context(0), w), 1, max_rows=n_prompt)
-    ids, lg = st.generate_greedy(prompt, n_gen, use_prefill=True)
+    lg, _ = st.prefill(prompt)
     ids_ref = [int(v) for v in g["ids"]]
-    first_diff = next((i for i, (a, b) in enumerate(zip(ids, ids_ref)) if a != b), None)
-    assert first_diff is None, f"first differing decode step: {first_diff}"
+    for step in range(n_gen):
+        # the oracle's 16 largest logits of this step, read back at the same indices
+        ti, tv = g["top_idx"][step], g["top_val"][step]
+        err = float(np.abs(lg[ti] - tv).max() / np.abs(tv).max())
+        assert err <= 1e-3, f"step {step}: top-16 logits differ by {err:.2e}"
+        nxt = int(np.argmax(lg))
+        assert nxt == ids_ref[step], f"step {step}: token {nxt} != oracle {ids_ref[step]}"
+        lgs, _ = st.step([nxt])
+        lg = lgs[0]
     lg_ref = g["logits"]
     assert float(np.abs(lg - lg_ref).max() / np.abs(lg_ref).max()) <= 1e-3
 
