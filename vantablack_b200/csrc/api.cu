@@ -13,7 +13,7 @@ namespace vtb {
 cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                         int accumulate = 0);
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                int accumulate, const float* norm_w, float eps);
+                                int accumulate, const float* norm_w, float eps, float* swi);
 cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* dx, float* y, int m, int k,
                                   cudaStream_t st, bool pdl);
 cudaError_t launch_dequant(int q, const void* w, float* out, long long n, cudaStream_t st);
@@ -114,7 +114,7 @@ int vtb_cuda_gemv(int quant, const void* w, const float* x, float* y, int64_t m,
   if (!x || !y) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null x or y");
   if (!aligned16(x)) return set_err(VTB_CUDA_ERR_INVALID_ARG, "x is not 16-byte aligned");
   if (quant == Q4_K)
-    return cuda_status(launch_gemv_q4k_mma(w, x, y, (int)m, (int)k, (cudaStream_t)stream, pdl != 0, 0, nullptr, 0.f));
+    return cuda_status(launch_gemv_q4k_mma(w, x, y, (int)m, (int)k, (cudaStream_t)stream, pdl != 0, 0, nullptr, 0.f, nullptr));
   return cuda_status(launch_gemv(quant, w, x, y, (int)m, (int)k, (cudaStream_t)stream, pdl != 0));
 }
 

@@ -134,7 +134,7 @@ struct MmaQ4K {
 template <int WARPS, int S, int CHB, bool TM, int ROWS>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
-                    int ksplit, int accumulate, const float* __restrict__ norm_w, float eps) {
+                    int ksplit, int accumulate, const float* __restrict__ norm_w, float eps, float* __restrict__ swi) {
   using C = MmaQ4K<CHB, TM, ROWS>;
   constexpr int MT = ROWS / 16, NI = 2 * MT;  // m16 tiles; rows g + 8i this lane holds
   extern __shared__ __align__(128) uint8_t smem[];
@@ -308,10 +308,21 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
       if (t == 0) red[warp * 32 + 16 * (i >> 1) + 8 * (i & 1) + g] = v;
     }
     __syncthreads();
-    if (kpart == 0 && lane < ROWS) {
+    if (kpart == 0) {  // warp-uniform
       float v = 0.f;
       for (int w = 0; w < min(ksplit, nch); ++w) v += red[(warp + w) * 32 + lane];
-      if (lane < nr) y[r0 + lane] = accumulate ? y[r0 + lane] + v : v;
+      if (swi) {
+        // rows interleave as [gate 8 | up 8] blocks: lane i < 8 of each 16-row block holds
+        // gate row i, lane i + 8 its up row; SwiGLU (math.zig:154-161) goes straight to h.
+        const float u = __shfl_down_sync(0xffffffffu, v, 8);
+        const int blk = lane >> 4, i = lane & 15;
+        if (i < 8 && lane < ROWS && r0 + lane + 8 < M) {
+          const float den = 1.0f + expf(-v);
+          swi[r0 / 2 + 8 * blk + i] = (v / den) * u;
+        }
+      } else if (lane < nr && lane < ROWS) {
+        y[r0 + lane] = accumulate ? y[r0 + lane] + v : v;
+      }
     }
     __syncthreads();
   }
@@ -324,7 +335,7 @@ constexpr int q4k_mma_smem(int k) {
 
 template <int WARPS, int S, int CHB, bool TM, int ROWS>
 static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                    int accumulate, const float* norm_w, float eps) {
+                                    int accumulate, const float* norm_w, float eps, float* swi) {
   using C = MmaQ4K<CHB, TM, ROWS>;
   constexpr auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB, TM, ROWS>;
   const int smem = q4k_mma_smem<WARPS, S, CHB, TM, ROWS>(k);
@@ -358,7 +369,7 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, wmap, (const uint8_t*)w, x, y, m, k, ksplit, accumulate, norm_w, eps);
+  return cudaLaunchKernelEx(&cfg, kern, wmap, (const uint8_t*)w, x, y, m, k, ksplit, accumulate, norm_w, eps, swi);
 }
 
 // Critical-path cost (in 32-row tile units) of a row-tile height: rounds x
@@ -372,22 +383,24 @@ static double q4k_tile_cost(int m, int k, int rows, int warps, int cap) {
   return (double)(rounds * ((nch + ks - 1) / ks)) * (rows == 16 ? 0.6 : 1.0);
 }
 
+// swi non-null: W's rows are [gate 8 | up 8] blocks (m % 16 == 0) and the
+// output is SwiGLU's h[m/2] in swi instead of y.
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                int accumulate, const float* norm_w = nullptr, float eps = 0.f) {
+                                int accumulate, const float* norm_w = nullptr, float eps = 0.f, float* swi = nullptr) {
   // One 2-D TMA box per tile.  Matrices above 2^24 weights stream with two
   // stages per warp; smaller ones (dominated by the dependent-launch chain)
   // with one.  Very long rows (x staged in shared memory at 4.25 B per column)
   // fall back to 8 warps.  The row-tile height (32 or 16) is the one whose
   // launch balances better over the SMs.
   if (q4k_mma_smem<16, 2, 1, true>(k) > 227 * 1024)
-    return launch_q4k_mma_t<8, 2, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+    return launch_q4k_mma_t<8, 2, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
   const int sms = sm_count(current_device());
   const bool r16 = q4k_tile_cost(m, k, 16, 16, sms) < q4k_tile_cost(m, k, 32, 16, sms);
   if ((long long)m * k > (1LL << 24))
-    return r16 ? launch_q4k_mma_t<16, 2, 1, true, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps)
-               : launch_q4k_mma_t<16, 2, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
-  return r16 ? launch_q4k_mma_t<16, 1, 1, true, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps)
-             : launch_q4k_mma_t<16, 1, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps);
+    return r16 ? launch_q4k_mma_t<16, 2, 1, true, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi)
+               : launch_q4k_mma_t<16, 2, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
+  return r16 ? launch_q4k_mma_t<16, 1, 1, true, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi)
+             : launch_q4k_mma_t<16, 1, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
 }
 
 }  // namespace vtb

@@ -30,7 +30,7 @@ namespace vtb {
 cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                         int accumulate);
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                int accumulate, const float* norm_w, float eps);
+                                int accumulate, const float* norm_w, float eps, float* swi);
 cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* out, int dim, int n_tok,
                          cudaStream_t st);
 cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
@@ -50,7 +50,7 @@ __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ t, l
 
 static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
                             int accumulate) {
-  if (q == Q4_K) return launch_gemv_q4k_mma(w, x, y, m, k, st, true, accumulate, nullptr, 0.f);
+  if (q == Q4_K) return launch_gemv_q4k_mma(w, x, y, m, k, st, true, accumulate, nullptr, 0.f, nullptr);
   return launch_gemv(q, w, x, y, m, k, st, true, accumulate);
 }
 
@@ -659,13 +659,15 @@ attn_prefill_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   asm volatile("griddepcontrol.launch_dependents;");
 }
 
-// swiglu (math.zig:154-161): h = (g / (1 + e^-g)) * u, gu = [gate | up] per row.
-__global__ void swiglu_kernel(const float* __restrict__ gu, float* __restrict__ h, int ffn, int rows) {
+// swiglu (math.zig:154-161): h = (g / (1 + e^-g)) * u.  gu per row is
+// [gate | up], or with `il` the fused weights' [gate 8 | up 8] row blocks.
+__global__ void swiglu_kernel(const float* __restrict__ gu, float* __restrict__ h, int ffn, int rows, int il) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long n = (long long)rows * ffn;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / ffn, j = i % ffn;
-    const float g = gu[r * 2 * ffn + j], u = gu[r * 2 * ffn + ffn + j];
+    const long long gi = il ? 16 * (j / 8) + j % 8 : j, ui = il ? gi + 8 : ffn + j;
+    const float g = gu[r * 2 * ffn + gi], u = gu[r * 2 * ffn + ui];
     const float den = 1.0f + expf(-g);
     h[i] = (g / den) * u;
   }
@@ -732,7 +734,8 @@ struct DevLayer {
   const uint8_t* qkv;  // fused Q|K|V rows (all three share quant and k)
   const uint8_t* q; const uint8_t* k; const uint8_t* v;  // unfused fallback
   const uint8_t* o;
-  const uint8_t* gu;   // fused gate|up rows
+  const uint8_t* gu;   // fused gate|up rows: [gate 8 | up 8] row blocks when gu_il
+  bool gu_il;
   const uint8_t* gate; const uint8_t* up;
   const uint8_t* down;
   const float* attn_norm;
@@ -988,7 +991,19 @@ VtbCudaModel* vtb_cuda_model_create_tp(VtbCudaCtx* ctx, VtbCudaTp* tp, const Vtb
     L.o = B + o.o;
     up_shard(o.o, L.q_o, lw[l].attn_o, d, 0, d, sh.o_col0, sh.o_cols);
     const size_t rg = rbytes(L.q_gate, d);
-    if (o.fg) {
+    L.gu_il = false;
+    if (o.fg && F % 8 == 0) {
+      // gate and up rows interleaved in blocks of 8 ([gate 8 | up 8], 16 rows): a
+      // row tile of the decode GEMV then holds both inputs of SwiGLU for its outputs
+      L.gu = B + o.gu;
+      L.gu_il = true;
+      const uint8_t* gs = static_cast<const uint8_t*>(lw[l].ffn_gate) + (size_t)sh.ffn_row0 * rg;
+      const uint8_t* us = static_cast<const uint8_t*>(lw[l].ffn_up) + (size_t)sh.ffn_row0 * rg;
+      ok = ok && cudaMemcpy2DAsync(B + o.gu, 16 * rg, gs, 8 * rg, 8 * rg, F / 8, cudaMemcpyHostToDevice, st) == cudaSuccess;
+      ok = ok && cudaMemcpy2DAsync(B + o.gu + 8 * rg, 16 * rg, us, 8 * rg, 8 * rg, F / 8, cudaMemcpyHostToDevice, st) ==
+                     cudaSuccess;
+      L.gate = L.up = nullptr;
+    } else if (o.fg) {
       L.gu = B + o.gu;
       up_shard(o.gu, L.q_gate, lw[l].ffn_gate, d, sh.ffn_row0, F, 0, d);
       up_shard(o.gu + rg * F, L.q_up, lw[l].ffn_up, d, sh.ffn_row0, F, 0, d);
@@ -1252,7 +1267,8 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   auto fused_norm_gemv = [&](const float* nw, int q, const uint8_t* w, float* out, int mm) -> bool {
     if (gemm || s->pending || q != Q4_K || !w) return false;
     for (int r = 0; r < R && e == cudaSuccess; ++r)
-      e = launch_gemv_q4k_mma(w, s->x + (size_t)r * d, out + (size_t)r * mm, mm, d, st, true, 0, nw, c.rms_eps);
+      e = launch_gemv_q4k_mma(w, s->x + (size_t)r * d, out + (size_t)r * mm, mm, d, st, true, 0, nw, c.rms_eps,
+                              nullptr);
     return true;
   };
   auto proj = [&](int q, const uint8_t* w, const float* in, float* out, int mm, int k, int ld_out, int acc) -> cudaError_t {
@@ -1339,6 +1355,14 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
       return e;
   }
   if ((e = residual(L.q_o, L.o, s->att, qd))) return e;  // x += W_o . att (addInto fused)
+  if (!gemm && !s->pending && L.gu && L.gu_il && L.q_gate == Q4_K) {
+    // FFN RMSNorm in the GEMV's prologue, SwiGLU in its epilogue: h directly
+    for (int r = 0; r < R && e == cudaSuccess; ++r)
+      e = launch_gemv_q4k_mma(L.gu, s->x + (size_t)r * d, nullptr, 2 * f, d, st, true, 0, L.ffn_norm, c.rms_eps,
+                              s->h + (size_t)r * f);
+    if (e) return e;
+    return residual(L.q_down, L.down, s->h, f);
+  }
   if (fused_norm_gemv(L.ffn_norm, L.q_gate, L.gu, s->gu, 2 * f)) {
     if (e) return e;
   } else if ((e = enqueue_norm(s, L.ffn_norm, 0, R))) {
@@ -1350,7 +1374,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
     if ((e = proj(L.q_up, L.up, s->xb, s->gu + f, f, d, 2 * f, 0))) return e;
   }
   if ((e = pdl_launch(swiglu_kernel, dim3(min(1184, (R * f + 255) / 256)), dim3(256), 0, st, (const float*)s->gu, s->h,
-                      f, R)))
+                      f, R, L.gu && L.gu_il ? 1 : 0)))
     return e;
   return residual(L.q_down, L.down, s->h, f);
 }
