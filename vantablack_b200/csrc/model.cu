@@ -1355,11 +1355,14 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
       return e;
   }
   if ((e = residual(L.q_o, L.o, s->att, qd))) return e;  // x += W_o . att (addInto fused)
-  if (!gemm && !s->pending && L.gu && L.gu_il && L.q_gate == Q4_K) {
-    // FFN RMSNorm in the GEMV's prologue, SwiGLU in its epilogue: h directly
+  if (!gemm && L.gu && L.gu_il && L.q_gate == Q4_K) {
+    // SwiGLU in the GEMV's epilogue (h directly); the FFN RMSNorm in its prologue,
+    // or, with a tensor-parallel partial pending, in the all-reduce kernel before it
+    const bool pend = s->pending;
+    if (pend && (e = enqueue_norm(s, L.ffn_norm, 0, R))) return e;
     for (int r = 0; r < R && e == cudaSuccess; ++r)
-      e = launch_gemv_q4k_mma(L.gu, s->x + (size_t)r * d, nullptr, 2 * f, d, st, true, 0, L.ffn_norm, c.rms_eps,
-                              s->h + (size_t)r * f);
+      e = launch_gemv_q4k_mma(L.gu, (pend ? s->xb : s->x) + (size_t)r * d, nullptr, 2 * f, d, st, true, 0,
+                              pend ? nullptr : L.ffn_norm, c.rms_eps, s->h + (size_t)r * f);
     if (e) return e;
     return residual(L.q_down, L.down, s->h, f);
   }
