@@ -1,6 +1,9 @@
-// gemv.cu -- decode GEMV y[m] = W[m,k] . x[k] for GGUF Q4_K / Q5_K / Q6_K /
-// Q8_0 weights and f32 activations (the reference's matmul_q*_* in
-// src/kernels/simd.zig:159-434, dispatched by forward.zig:552-627).
+// gemv.cu -- SIMT decode GEMV y[m] = W[m,k] . x[k] for GGUF Q5_K / Q8_0
+// weights, Q6_K rows that are not 16-byte multiples, and the Q8_0 x Q8_0
+// path, with f32 activations (the reference's matmul_q*_* in
+// src/kernels/simd.zig:159-434, dispatched by forward.zig:552-627).  Q4_K and
+// TMA-compatible Q6_K run on the integer tensor cores (gemv_mma.cu,
+// gemv_q6k_mma.cu); launch_gemv dispatches Q6_K itself.
 //
 // Design (B200):
 //  * Persistent CTAs of WARPS warps; each warp owns a stream of tiles.  A
@@ -10,7 +13,7 @@
 //    (cp.async.bulk, no multicast) into an S-stage per-warp ring guarded by
 //    mbarriers; the copies for the next S tiles are always in flight.
 //  * Lane l of the warp dequantizes 64 weights (32 for Q8_0) of each row of
-//    the tile straight from shared memory: nibbles become exact floats with
+//    the tile straight from shared memory: quantized values become exact floats with
 //    a byte-permute against the 0x4B000000 magic, and the products go
 //    through packed f32x2 FMAs.  Sub-block scales are applied once per
 //    sub-block: sum_l (d1*q_l - m1)*x_l = d1*sum_l q_l*x_l - m1*sum_l x_l.
@@ -27,7 +30,6 @@ namespace vtb {
 
 
 template <int Q> struct GemvCfg;
-template <> struct GemvCfg<Q4_K> { static constexpr int CH = 8; };
 template <> struct GemvCfg<Q5_K> { static constexpr int CH = 8; };
 template <> struct GemvCfg<Q6_K> { static constexpr int CH = 8; };
 template <> struct GemvCfg<Q8_0> { static constexpr int CH = 32; };
@@ -59,13 +61,14 @@ __device__ __forceinline__ float4 ldx4(const float* p) { return __ldg(reinterpre
 // sums the min/bias terms need.
 struct XSlice {
   f2 v[32];
-  float s0, s1;  // Q4_K/Q5_K: sums of the low / high 32
+  float s0, s1;  // Q5_K: sums of the low / high 32
 };
 
 // ---------------- per-format lane kernels ----------------
 // Each returns this lane's contribution to one row's dot for the chunk.
 
-// Q4_K: lane -> block b = lane>>2, sub-block pair j = lane&3 (simd.zig:221-243).
+// Q4_K-style blocks (the Q5_K path): lane -> block b = lane>>2, sub-block pair j = lane&3
+// (simd.zig:221-243).
 __device__ __forceinline__ void load_x_kq(const float* x, int col0, XSlice& xs) {
   float s0 = 0.f, s1 = 0.f;
 #pragma unroll
@@ -103,42 +106,7 @@ __device__ __forceinline__ void kq_scale_min(uint4 h, int j, float& d1, float& m
   d2 = d * (float)sb; m2 = dmin * (float)mb;
 }
 
-// Sum of q*x over 4 nibble words, given magic-biased bytes.  `lo` words hold
-// q in each byte, `hi` words hold 16*q in each byte (high nibble kept in
-// place); the caller rescales the high sum by 1/16.
-__device__ __forceinline__ void nib_dot(const uint32_t* qw, const XSlice& xs, int xoff, f2& acc_lo, f2& acc_hi) {
-  const f2 mg = pk(-8388608.f, -8388608.f);
-  f2 a0 = pk(0.f, 0.f), a1 = a0, b0 = a0, b1 = a0;
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    const uint32_t lo = qw[w] & 0x0F0F0F0Fu, hi = qw[w] & 0xF0F0F0F0u;
-    f2 l01 = add2(pk(byte_magic<0>(lo), byte_magic<1>(lo)), mg);
-    f2 l23 = add2(pk(byte_magic<2>(lo), byte_magic<3>(lo)), mg);
-    f2 h01 = add2(pk(byte_magic<0>(hi), byte_magic<1>(hi)), mg);
-    f2 h23 = add2(pk(byte_magic<2>(hi), byte_magic<3>(hi)), mg);
-    a0 = fma2(l01, xs.v[xoff + 2 * w], a0);
-    a1 = fma2(l23, xs.v[xoff + 2 * w + 1], a1);
-    b0 = fma2(h01, xs.v[16 + xoff + 2 * w], b0);
-    b1 = fma2(h23, xs.v[16 + xoff + 2 * w + 1], b1);
-  }
-  acc_lo = add2(acc_lo, add2(a0, a1));
-  acc_hi = add2(acc_hi, add2(b0, b1));
-}
-
-__device__ __forceinline__ float lane_dot_q4k(const uint8_t* blk, int j, const XSlice& xs) {
-  const uint4 h = *reinterpret_cast<const uint4*>(blk);
-  const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j);
-  const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * j);
-  float d1, m1, d2, m2;
-  kq_scale_min(h, j, d1, m1, d2, m2);
-  f2 lo = pk(0.f, 0.f), hi = lo;
-  const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
-  nib_dot(wa, xs, 0, lo, hi);
-  nib_dot(wb, xs, 8, lo, hi);
-  return (d1 * hsum(lo) - m1 * xs.s0) + ((d2 * 0.0625f) * hsum(hi) - m2 * xs.s1);
-}
-
-// Q5_K (simd.zig:290-319): as Q4_K plus bit 2j / 2j+1 of qh[l] worth 16.
+// Q5_K (simd.zig:290-319): the Q4_K nibble layout plus bit 2j / 2j+1 of qh[l] worth 16.
 __device__ __forceinline__ float lane_dot_q5k(const uint8_t* blk, int j, const XSlice& xs) {
   const uint4 h = *reinterpret_cast<const uint4*>(blk);
   const uint4 ha = *reinterpret_cast<const uint4*>(blk + 16);
@@ -360,8 +328,7 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
         const unsigned lead = (unsigned)(reinterpret_cast<uintptr_t>(src) & 15u);
         const uint8_t* blk = ring + st * STAGE + r * SLOT + lead + bl * BB;
         float v;
-        if constexpr (Q == Q4_K) v = lane_dot_q4k(blk, j, xs);
-        else if constexpr (Q == Q5_K) v = lane_dot_q5k(blk, j, xs);
+        if constexpr (Q == Q5_K) v = lane_dot_q5k(blk, j, xs);
         else if constexpr (Q == Q6_K) v = lane_dot_q6k(blk, j, xs);
         else if constexpr (XQ) v = lane_dot_q80_i8(blk, xqs);
         else v = lane_dot_q80(blk, xs);
@@ -411,7 +378,6 @@ static cudaError_t launch_gemv_t(const void* w, const void* x, const float* dx, 
 cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                         int accumulate) {
   switch (q) {
-    case Q4_K: return launch_gemv_t<Q4_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
     case Q5_K: return launch_gemv_t<Q5_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
     case Q6_K:  // integer tensor cores when rows are whole 16-byte multiples
       if (q6k_mma_ok(w, k)) return launch_gemv_q6k_mma(w, x, y, m, k, st, pdl, accumulate);

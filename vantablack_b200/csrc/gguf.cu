@@ -460,7 +460,8 @@ static int gguf_layers(const VtbCudaGguf* g, int32_t max_seq, VtbCudaLlamaConfig
     return rc;
   *out_norm = static_cast<const float*>(on);
   if (g->find_tensor("output.weight")) {
-    if ((rc = fetch("output.weight", d, v, false, out_w, q_out))) return rc;
+    rc = fetch("output.weight", d, v, false, out_w, q_out);
+    if (rc) return rc;
   } else {
     *out_w = *embd;
     *q_out = *q_embd;
