@@ -55,7 +55,7 @@ def test_reference_minimal_file(tmp_path):
 
 @pytest.mark.parametrize("kind,status", [
     ("bad_magic", -3), ("version1", -3), ("truncated", -3), ("missing", -2), ("empty", -2), ("too_small", -3),
-    ("partial_block", -3), ("deep_array", -3), ("bad_meta_type", -3), ("numel_overflow", -3)])
+    ("partial_block", -3), ("deep_array", -3), ("bad_meta_type", -3), ("numel_overflow", -3), ("size_overflow", -3)])
 def test_rejections(tmp_path, kind, status):
     p = tmp_path / f"{kind}.gguf"
     if kind == "bad_magic":
@@ -72,6 +72,8 @@ def test_rejections(tmp_path, kind, status):
         p.write_bytes(minimal_v3(n_dims=1, dims=(100,), ggml_type=12))
     elif kind == "numel_overflow":
         p.write_bytes(minimal_v3(dims=(1 << 40, 1 << 40)))
+    elif kind == "size_overflow":  # 2^62 f32 elements: the count fits, the byte size does not
+        p.write_bytes(minimal_v3(dims=(1 << 31, 1 << 31)))
     elif kind in ("deep_array", "bad_meta_type"):
         b = struct.pack("<IIQQ", 0x46554747, 3, 0, 1) + _s("k")
         if kind == "deep_array":  # 6 levels of arrays of arrays: nesting deeper than 4

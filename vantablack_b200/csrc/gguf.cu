@@ -212,7 +212,7 @@ static int parse(VtbCudaGguf* g) {
     uint64_t el, by;
     block_info(t.type, &el, &by);
     if (el) {
-      if (numel % el) return fail("unsupported tensor block shape");
+      if (numel % el || numel / el > UINT64_MAX / by) return fail("unsupported tensor block shape");
       t.size = numel / el * by;
     }
   }
