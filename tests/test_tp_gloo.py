@@ -101,3 +101,39 @@ def test_shard_plan_rejects_unaligned_or_indivisible():
                         max_seq=8)
     with pytest.raises(_lib.VtbError):
         shard_plan(small, 0, 4)         # O's K shard of 64 columns is not a whole 256-weight block
+
+
+def _partition(shards, start_attr, len_attr, total):
+    spans = sorted((getattr(s, start_attr), getattr(s, len_attr)) for s in shards)
+    pos = 0
+    for a, n in spans:
+        assert a == pos and n > 0
+        pos += n
+    assert pos == total
+
+
+def test_shard_plans_partition_every_tensor():
+    """The shard plan at 1, 2, 4 and 8 ranks for both model configurations:
+    heads, kv heads, ffn rows, O / down columns and vocabulary rows are each
+    split into contiguous, disjoint, covering ranges; K splits fall on whole
+    256-weight blocks, and configurations whose ffn split would not are refused."""
+    import pytest
+    from vantablack_b200 import _lib
+    from vantablack_b200.model import LLAMA3_8B, TINYLLAMA, shard_plan
+    for cfg in (LLAMA3_8B, TINYLLAMA):
+        for world in (1, 2, 4, 8):
+            kvd = cfg.n_kv_heads * cfg.head_dim
+            if (cfg.ffn_dim // world) % 256:
+                with pytest.raises(_lib.VtbError):
+                    shard_plan(cfg, 0, world)
+                continue
+            shards = [shard_plan(cfg, r, world) for r in range(world)]
+            for s in shards:
+                assert s.heads == cfg.n_heads // world and s.kv_heads == cfg.n_kv_heads // world
+                assert s.o_col0 % 256 == 0 and s.down_col0 % 256 == 0
+            _partition(shards, "q_row0", "q_rows", cfg.n_heads * cfg.head_dim)
+            _partition(shards, "kv_row0", "kv_rows", kvd)
+            _partition(shards, "ffn_row0", "ffn_rows", cfg.ffn_dim)
+            _partition(shards, "o_col0", "o_cols", cfg.n_heads * cfg.head_dim)
+            _partition(shards, "down_col0", "down_cols", cfg.ffn_dim)
+            _partition(shards, "vocab_row0", "vocab_rows", cfg.vocab_size)
