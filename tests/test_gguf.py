@@ -127,3 +127,20 @@ def test_defaults_and_unsupported_arch(tmp_path):
         with pytest.raises(_lib.VtbError) as e:
             g.llama_config()
         assert e.value.status == -8
+
+
+def test_status_codes_of_a_failed_open(tmp_path):
+    """A NULL handle leaves its status and message for vtb_cuda_last_status /
+    vtb_cuda_last_error (the -2 / -3 codes reuse the reference's
+    VTB_ERR_FILE_OPEN / VTB_ERR_PARSE)."""
+    lib = _lib.load()
+    assert not lib.vtb_cuda_gguf_open(str(tmp_path / "absent.gguf").encode())
+    assert lib.vtb_cuda_last_status() == -2
+    assert b"cannot open" in lib.vtb_cuda_last_error()
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(minimal_v3(magic=0x12345678))
+    assert not lib.vtb_cuda_gguf_open(str(bad).encode())
+    assert lib.vtb_cuda_last_status() == -3
+    assert b"not a GGUF file" in lib.vtb_cuda_last_error()
+    assert lib.vtb_cuda_status_string(-2) == b"file cannot be opened"
+    assert lib.vtb_cuda_status_string(-3) == b"malformed model file"
