@@ -1,23 +1,45 @@
-"""Benchmark of the Q4_K decode GEMV (TinyLlama-1.1B
-ffn_up, W = 5632 x 2048 Q4_K, x = f32[2048]).
+"""Benchmark of vantablack's quantized-matmul hot path on B200.
 
-One step = one GEMV over each of N_COPIES distinct, seeded copies of W
-(415 MB in total, > 3x the 126 MB L2, so every timed launch streams its
-weights from HBM), launched back to back with programmatic dependent launch
-and replayed as one CUDA graph.  `value` is algorithmic bytes (W + x + y per
-GEMV) per second with inputs resident in HBM; `e2e` is the same metric
-through the C-ABI context API with host buffers (x copied H2D from pinned
-memory, every y read back D2H, inside the timed region).
+Headline (the JSON line's `value`): the Q4_K decode GEMV at the TinyLlama-1.1B
+ffn_up shape (W = 5632 x 2048 Q4_K, x = f32[2048]), the reference's
+matmul_q4_k (src/kernels/simd.zig:245-273).  One step = one GEMV over each of
+N_COPIES distinct seeded copies of W (415 MB, > 3x the 126 MB L2, so every
+launch streams its weights from HBM), chained with programmatic dependent
+launch in one CUDA graph, i.e. each GEMV is timed as it runs in a dependent
+decode chain.  `e2e` is the same metric through the C-ABI context API with
+host buffers (x copied H2D from pinned memory, every y read back D2H).
+
+The same line carries, under `workloads`:
+  * gemv_sweep   -- Q6_K, Q8_0 and Q8_0xQ8_0 GEMVs at the Llama-3-8B decode
+                    shapes (GB/s, roofline fraction, oracle parity on sampled
+                    rows, the oracle's GB/s on the host cores);
+  * prefill_gemm -- the batched prefill GEMM (prefill.zig:325-378) for Q4_K
+                    14336x4096 and Q6_K 4096x14336 at B in {87, 512, 2048}, in
+                    bf16 and precise mode (TFLOP/s, fraction of the bf16 peak,
+                    oracle parity on sampled rows, oracle GFLOP/s);
+  * tinyllama    -- the TinyLlama-1.1B architecture end to end: 128-token
+                    prefill + 256 greedy decode steps, greedy ids checked
+                    against the oracle run on the same weights, GPU and oracle
+                    tok/s;
+  * llama3_8b    -- the Llama-3-8B architecture (Q4_K_M-style random init)
+                    tensor parallel over all ranks: 2048-token prefill, 512
+                    greedy decode steps at batch 1 whose ids and per-step top-16
+                    logits are checked against the committed oracle fixture
+                    tests/golden/llama3_8b_p2048_g512.npz, and batch-32 decode.
+                    Every rank maps one GGUF file written once by rank 0 and
+                    uploads only its shard.
+The first three run on one GPU (N = 1 only); llama3_8b runs at every N.
 
 `--impl reference` times the reference's CPU algorithm (the oracle port in
-oracle/; the Zig reference cannot be compiled here) on all host threads.
-Multi-GPU (torchrun): every rank runs an independent replica (the GEMV
-shards by rows with no exchange), value = all ranks' bytes / max rank time.
+oracle/; the Zig reference cannot be compiled here) on the host cores.
+Multi-GPU (torchrun): the headline GEMV runs as independent replicas (it has
+no exchange step), value = all ranks' bytes / max rank time.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import subprocess
 import sys
@@ -30,21 +52,36 @@ sys.path.insert(0, ROOT)
 
 M, K = 5632, 2048
 N_COPIES = 64
-Q4_K = 12
+Q8_0, Q4_K, Q6_K = 8, 12, 14
 W_BYTES = M * (K // 256) * 144
-ALG_BYTES = W_BYTES + 4 * K + 4 * M  # per GEMV (6,518,784 B)
+ALG_BYTES = W_BYTES + 4 * K + 4 * M  # per GEMV: W + x + y = 6,518,784 B
 METRIC = "Q4_K GEMV HBM GB/s (TinyLlama ffn_up 5632x2048, batch 1)"
 CONFIG = {"workload": "q4_k_gemv_5632x2048", "m": M, "k": K, "quant": "Q4_K", "weight_copies": N_COPIES,
           "l2": "inputs > L2: 64 distinct weight copies = 415 MB per step"}
+L2_BYTES = 126 * 2 ** 20
+FIXTURE = os.path.join(ROOT, "tests", "golden", "llama3_8b_p2048_g512.npz")
+GGUF_VERSION = 1  # bump when the synthetic weight generator changes
 
 
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, "fallback"
+
+
+def host_cores() -> int:
+    """Physical cores of this host (the reference's pool sizes itself from them)."""
+    try:
+        import psutil
+        n = psutil.cpu_count(logical=False)
+        if n:
+            return int(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
 
 
 def dist_env():
@@ -122,6 +159,10 @@ def cpu_gemv_rate(ws, x, budget_s: float, threads: int):
 
 
 def run_reference(args):
+    """The reference's CPU Q4_K GEMV (oracle port of simd.zig matmul_q4_k with
+    pool.zig row striping) on all physical host cores.  Each step is a bounded
+    sample of GEMVs over distinct weight copies, sized from a calibration run
+    so that the K timed steps together last at least ~2 s."""
     rank, ws_, _ = dist_env()
     if ws_ > 1:
         import torch.distributed as dist
@@ -131,30 +172,368 @@ def run_reference(args):
             return
     import oracle as O
     ws, x = make_weights(0)
-    threads = os.cpu_count() or 1
+    threads = host_cores()
     O.set_threads(threads)
-    per_step = 4  # bounded sample: 4 GEMVs (distinct copies) per step
+    O.matmul(Q4_K, ws[0], x, M, K)
+    t0 = time.perf_counter()
+    for i in range(8):
+        O.matmul(Q4_K, ws[i], x, M, K)
+    t_one = (time.perf_counter() - t0) / 8
+    steps = max(1, args.steps)
+    per_step = max(4, math.ceil(0.05 / t_one), math.ceil(2.0 / (steps * t_one)))
+    per_step = min(per_step, max(4, int(60.0 / (steps * t_one))))  # whole run within about a minute
     for s in range(args.warmup):
         for i in range(per_step):
             O.matmul(Q4_K, ws[(s * per_step + i) % N_COPIES], x, M, K)
     t0 = time.perf_counter()
-    for s in range(args.steps):
+    for s in range(steps):
         for i in range(per_step):
             O.matmul(Q4_K, ws[(s * per_step + i) % N_COPIES], x, M, K)
     el = time.perf_counter() - t0
-    v = args.steps * per_step * ALG_BYTES / el / 1e9
+    v = steps * per_step * ALG_BYTES / el / 1e9
     line = {"metric": METRIC, "value": v, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(CONFIG, per_step_sample=f"{per_step} GEMVs"),
+            "config": dict(CONFIG),
             "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": f"{per_step} GEMVs of 5632x2048 Q4_K per step, oracle port of "
-                                       "simd.zig matmul_q4_k with pool.zig row striping"},
+                             "sample": f"{per_step} GEMVs of 5632x2048 Q4_K per step ({el:.1f} s timed), oracle "
+                                       "port of simd.zig matmul_q4_k with pool.zig row striping",
+                             "reference_default_threads": (threads + 1) // 2},
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     if ws_ > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+# DRAM bytes (read + write) of one config-1 launch, from the ncu capture summarised in
+# profiles/q4k_gemv_5632x2048.md (6,545,152 read, ~0 written; algorithmic 6,518,784).
+ALG_BYTES_TRAFFIC = 6545152
+
+
+def time_graph(build, replays: int, stream):
+    """Captures build() into a CUDA graph on `stream`, replays it 3 times
+    untimed, then `replays` times between CUDA events; returns ms per replay."""
+    import torch
+    with torch.cuda.stream(stream):
+        build()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            build()
+        for _ in range(3):
+            g.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(replays):
+            g.replay()
+        e1.record(stream)
+        e1.synchronize()
+    del g
+    return e0.elapsed_time(e1) / replays
+
+
+def gemv_sweep(dev, hbm: float, cpu_threads: int) -> dict:
+    """Q6_K / Q8_0 / Q8_0xQ8_0 GEMVs at the Llama-3-8B decode shapes
+    (simd.zig:159-190, 406-434; dot_i8 :40-62 for the int8 variant), each a PDL
+    chain over distinct weight copies totalling > 4x L2.  The weights are one
+    seeded buffer per format (the largest shape's; smaller shapes use a prefix,
+    which is whole blocks), copied on the device."""
+    import torch
+    import oracle as O
+    from vantablack_b200 import ops, synth as S
+    shapes = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+    rng = np.random.default_rng(2)
+    stream = torch.cuda.Stream(device=dev)
+    O.set_threads(cpu_threads)
+    out = {}
+    for quant, name in ((Q6_K, "q6_k"), (Q8_0, "q8_0"), (-1, "q8_0xq8_0")):
+        q = Q8_0 if quant < 0 else quant
+        if quant != -1:
+            host = S.quant_tensor(rng, q, 128256, 4096)
+        base = torch.from_numpy(host).to(dev)
+        for m, k in shapes:
+            nbytes = m * S.row_bytes(q, k)
+            copies = max(1, min(64, math.ceil(4 * L2_BYTES / nbytes)))
+            ws = [base[:nbytes]] + [base[:nbytes].clone() for _ in range(copies - 1)]
+            x = torch.from_numpy(S.activations(rng, k)).to(dev)
+            ys = [torch.empty(m, dtype=torch.float32, device=dev) for _ in range(copies)]
+            xq = torch.empty(k, dtype=torch.int8, device=dev)
+            dx = torch.empty(k // 32, dtype=torch.float32, device=dev)
+            per = max(1, 32 // copies)
+
+            def build():
+                for _ in range(per):
+                    for i in range(copies):
+                        if quant == -1:
+                            ops.gemv_q8_0_q8_0(ws[i], x, m, k, out=ys[i], scratch=(xq, dx), pdl=True)
+                        else:
+                            ops.gemv(q, ws[i], x, m, k, out=ys[i], pdl=True)
+            ms = time_graph(build, 10, stream)
+            launches = per * copies
+            alg = nbytes + 4 * k + 4 * m
+            gbs = alg * launches / (ms / 1e3) / 1e9
+            # parity and the oracle's rate on a row sample (whole GEMV for small shapes)
+            rows = min(m, max(64, (48 << 20) // S.row_bytes(q, k)))
+            hw = host[:rows * S.row_bytes(q, k)]
+            hx = x.cpu().numpy()
+            fn = (lambda: O.matmul_q8_0_q8_0(hw, hx, rows, k)) if quant == -1 else (lambda: O.matmul(q, hw, hx, rows, k))
+            ref = fn()
+            n, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < 0.5:
+                fn()
+                n += 1
+            cpu_s = (time.perf_counter() - t0) / n
+            got = ys[0][:rows].cpu().numpy()
+            out[f"{name}_{m}x{k}"] = {
+                "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4), "us_per_launch": round(ms * 1e3 / launches, 3),
+                "chain_copies": copies, "max_rel_err_vs_oracle": float(np.abs(got - ref).max() / np.abs(ref).max()),
+                "oracle_rows_checked": rows,
+                "cpu_gbs": round((rows * S.row_bytes(q, k) + 4 * k + 4 * rows) / cpu_s / 1e9, 2)}
+            del ws, ys
+        del base
+        torch.cuda.empty_cache()
+    ops.check_device_error()
+    return out
+
+
+def prefill_gemm(dev, bf16_peak: float, cpu_threads: int) -> dict:
+    """The batched prefill GEMM (prefill.zig:325-378 matmulBatched) on tcgen05:
+    out[B, m] = acts[B, k] . W^T for Q4_K 14336x4096 and Q6_K 4096x14336."""
+    import torch
+    import oracle as O
+    from vantablack_b200 import ops, synth as S
+    rng = np.random.default_rng(3)
+    O.set_threads(cpu_threads)
+    out = {}
+    for q, name, m, k in ((Q4_K, "q4_k", 14336, 4096), (Q6_K, "q6_k", 4096, 14336)):
+        host = S.quant_tensor(rng, q, m, k)
+        w = torch.from_numpy(host).to(dev)
+        ws = [w] + [w.clone() for _ in range(3)]  # 4 copies: weights rotate through > L2
+        for B in (87, 512, 2048):
+            acts_h = S.activations(rng, B, k)
+            acts = torch.from_numpy(acts_h).to(dev)
+            o = torch.empty(B, m, dtype=torch.float32, device=dev)
+            # the oracle on a row sample (rows [0, r)): parity and its GFLOP/s
+            r = 64
+            t0 = time.perf_counter()
+            ref = O.matmul_batched(q, host[:r * S.row_bytes(q, k)], acts_h, r, k, B)
+            cpu_s = time.perf_counter() - t0
+            for precise in (False, True):
+                for i in range(2):
+                    ops.gemm(q, ws[i], acts, m, k, precise=precise, out=o)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = 20
+                e0.record()
+                for i in range(reps):
+                    ops.gemm(q, ws[i % 4], acts, m, k, precise=precise, out=o)
+                e1.record()
+                e1.synchronize()
+                ms = e0.elapsed_time(e1) / reps
+                tf = 2.0 * B * m * k / (ms / 1e3) / 1e12
+                got = o[:, :r].cpu().numpy()
+                out[f"{name}_{m}x{k}_b{B}_{'precise' if precise else 'bf16'}"] = {
+                    "tflops": round(tf, 1), "frac_bf16": round(tf / bf16_peak, 4), "ms": round(ms, 4),
+                    "max_rel_err_vs_oracle": float(np.abs(got - ref).max() / np.abs(ref).max()),
+                    "tolerance": 1e-4 if precise else 2e-2,
+                    "cpu_gflops": round(2.0 * B * r * k / cpu_s / 1e9, 2), "oracle_rows_checked": r}
+        del ws, w
+        torch.cuda.empty_cache()
+    ops.check_device_error()
+    return out
+
+
+def tinyllama(local: int, hbm: float, cpu_threads: int) -> dict:
+    """The TinyLlama-1.1B architecture end to end (forward.zig step +
+    prefill.zig prefillCpu): 128-token prompt, 256 greedy decode steps with
+    the logits read back every step, ids compared with the oracle's."""
+    import oracle as O
+    from vantablack_b200.model import TINYLLAMA, Context, CudaModel, CudaState, HostWeights
+    cfg = TINYLLAMA
+    w = HostWeights(cfg, seed=4)
+    prompt = np.random.default_rng(44).integers(3, cfg.vocab_size, 128)
+    ctx = Context(local)
+    m = CudaModel(ctx, w)
+    st = CudaState(m, 1, max_rows=128)
+    st.prefill(prompt[:16])
+    st.reset()
+    t0 = time.perf_counter()
+    lg, nxt = st.prefill(prompt)
+    t_pre = time.perf_counter() - t0
+    ids = []
+    t0 = time.perf_counter()
+    for _ in range(256):
+        ids.append(nxt)
+        lgs, am = st.step([nxt])
+        nxt = int(am[0])
+    t_dec = time.perf_counter() - t0
+    lg = lgs[0]
+    st.close(); m.close(); ctx.close()
+    O.set_threads(cpu_threads)
+    om = O.Model(w)
+    t0 = time.perf_counter()
+    lgr = om.prefill(prompt)
+    cpu_pre = time.perf_counter() - t0
+    ids_ref = []
+    t0 = time.perf_counter()
+    for _ in range(256):
+        nr = O.argmax(lgr)
+        ids_ref.append(nr)
+        lgr = om.step(nr)
+    cpu_dec = time.perf_counter() - t0
+    wbytes = w.nbytes() - w.token_embd[1].nbytes  # the embedding is gathered one row per token
+    ctx_mid = 128 + 128
+    kv = 2 * cfg.n_layers * ctx_mid * cfg.n_kv_heads * cfg.head_dim * 4
+    dec = 256 / t_dec
+    return {"prefill_128_tok_s": round(128 / t_pre, 1), "decode_b1_tok_s": round(dec, 1),
+            "decode_frac_hbm": round(dec * (wbytes + kv) / 1e9 / hbm, 4),
+            "ids_equal_oracle": ids == ids_ref,
+            "first_diff": next((i for i, (a, b) in enumerate(zip(ids, ids_ref)) if a != b), None),
+            "final_logits_rel_err": float(np.abs(lg - lgr).max() / np.abs(lgr).max()),
+            "cpu_prefill_128_tok_s": round(128 / cpu_pre, 2), "cpu_decode_b1_tok_s": round(256 / cpu_dec, 2),
+            "cpu_threads": cpu_threads, "timing": "wall clock per call; each decode step reads its logits back"}
+
+
+def shared_gguf_path(name: str) -> str:
+    d = "/dev/shm" if os.path.isdir("/dev/shm") and os.access("/dev/shm", os.W_OK) else None
+    if d:
+        st = os.statvfs(d)
+        if st.f_bavail * st.f_frsize < 8 << 30:
+            d = None
+    import tempfile
+    return os.path.join(d or tempfile.gettempdir(), name)
+
+
+def llama3_8b(rank: int, world: int, local: int, dist, args, hbm: float, cpu_threads: int) -> dict:
+    """Llama-3-8B architecture (Q4_K_M-style random init, the committed oracle
+    fixture's weights) tensor parallel over all ranks: QKV and gate/up split by
+    output rows, O and down along K with the all-reduce over NVLink peer
+    memory, the LM head by vocabulary rows.  Rank 0 writes the GGUF file once
+    (tensor by tensor); every rank maps it and uploads only its shard."""
+    import torch
+    from vantablack_b200.gguf import GgufFile
+    from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState, TensorParallel, \
+        write_synthetic_gguf
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def tmax(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    g = np.load(FIXTURE)
+    seed_w, seed_p = int(g["seed_w"]), int(g["seed_p"])
+    n_prompt, n_fix = int(g["n_prompt"]), int(g["n_gen"])
+    n_gen = max(1, min(args.model_steps, n_fix))
+    path = shared_gguf_path(f"vtb_bench_llama3_8b_s{seed_w}_v{GGUF_VERSION}.gguf")
+    res = {"model": "llama3_8b_random_init_q4_k_m", "tp": world, "gguf": path}
+    t0 = time.perf_counter()
+    if rank == 0 and not os.path.exists(path):
+        write_synthetic_gguf(path, LLAMA3_8B, seed=seed_w)
+    barrier()
+    res["gguf_write_s"] = round(time.perf_counter() - t0, 1)
+
+    def exchange(b: bytes) -> bytes:
+        if world == 1:
+            return b
+        obj = [b]
+        dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    ctx = Context(local)
+    tp = TensorParallel(local, rank, world, exchange) if world > 1 else None
+    t0 = time.perf_counter()
+    with GgufFile(path) as gf:
+        m = CudaModel.from_gguf(ctx, gf, max_seq=LLAMA3_8B.max_seq, tp=tp)
+    res["upload_s"] = round(tmax(time.perf_counter() - t0), 1)
+    prompt = np.random.default_rng(seed_p).integers(3, LLAMA3_8B.vocab_size, n_prompt)
+    st = CudaState(m, 1, max_rows=n_prompt)
+    res["p2p"] = bool(st.tp_p2p()) if world > 1 else None
+    st.prefill(prompt[:64])
+    st.reset()
+    barrier()
+    t0 = time.perf_counter()
+    lg, _ = st.prefill(prompt)
+    res["prefill_2048_tok_s"] = round(n_prompt / tmax(time.perf_counter() - t0), 1)
+    # batch-1 decode over the fixture's steps; the logits come back to the host every
+    # step (the sampler reads them there), and are checked after the timed loop
+    ids, tops = [], []
+    barrier()
+    t0 = time.perf_counter()
+    for step in range(n_gen):
+        tops.append(lg[g["top_idx"][step]])
+        nxt = int(np.argmax(lg))
+        ids.append(nxt)
+        lgs, _ = st.step([nxt])
+        lg = lgs[0]
+    dt = tmax(time.perf_counter() - t0)
+    res["decode_b1_tok_s"] = round(n_gen / dt, 1)
+    res["decode_b1_steps"] = n_gen
+    ctx_mid = n_prompt + n_gen // 2
+    wb = m.weight_bytes
+    kv = 2 * LLAMA3_8B.n_layers * ctx_mid * LLAMA3_8B.n_kv_heads * LLAMA3_8B.head_dim * 4 / world
+    res["decode_b1_frac_hbm_per_gpu"] = round((n_gen / dt) * (wb + kv) / 1e9 / hbm, 4)
+    ref_ids = [int(v) for v in g["ids"][:n_gen]]
+    errs = [float(np.abs(t - g["top_val"][i]).max() / np.abs(g["top_val"][i]).max()) for i, t in enumerate(tops)]
+    res["parity"] = {"ids_equal": ids == ref_ids,
+                     "first_diff": next((i for i, (a, b) in enumerate(zip(ids, ref_ids)) if a != b), None),
+                     "max_top16_rel_err": max(errs), "tolerance": 1e-3,
+                     "reference": "oracle fixture tests/golden/llama3_8b_p2048_g512.npz"}
+    if n_gen == n_fix:
+        lr = g["logits"]
+        res["parity"]["final_logits_rel_err"] = float(np.abs(lg - lr).max() / np.abs(lr).max())
+    st.close()
+    # batch-32 decode: 32 independent sequences, one token each per step
+    st = CudaState(m, 32, max_rows=32)
+    toks = np.random.default_rng(1).integers(3, LLAMA3_8B.vocab_size, 32)
+    for _ in range(3):
+        _, toks = st.step(toks, want_logits=False)
+    nb = 64
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(nb):
+        _, toks = st.step(toks, want_logits=False)
+    dt32 = tmax(time.perf_counter() - t0)
+    res["decode_b32_tok_s"] = round(32 * nb / dt32, 1)
+    res["decode_b32_frac_hbm_per_gpu"] = round((nb / dt32) * wb / 1e9 / hbm, 4)
+    st.close()
+    m.close()
+    if tp:
+        tp.close()
+    ctx.close()
+    res["timing"] = "wall clock per call, max over ranks; decode reads logits (b1) or argmax ids (b32) back per step"
+    if rank == 0 and world == 1:
+        res["cpu_baseline"] = llama3_8b_cpu(path, cpu_threads)
+    return res
+
+
+def llama3_8b_cpu(path: str, threads: int) -> dict:
+    """The oracle's 8B forward on the host cores over the same GGUF (memmap):
+    decode tok/s at batch 1 over a few steps after a 16-token prompt, and
+    prefill tok/s of that prompt."""
+    import oracle as O
+    from vantablack_b200.model import HostWeights
+    O.set_threads(threads)
+    w = HostWeights.from_gguf(path)
+    om = O.Model(w)
+    prompt = np.arange(3, 19)
+    t0 = time.perf_counter()
+    lg = om.prefill(prompt)
+    t_pre = time.perf_counter() - t0
+    n = 4
+    t0 = time.perf_counter()
+    for _ in range(n):
+        lg = om.step(O.argmax(lg))
+    t_dec = time.perf_counter() - t0
+    return {"decode_b1_tok_s": round(n / t_dec, 3), "prefill_16_tok_s": round(16 / t_pre, 2), "threads": threads,
+            "kind": "port", "sample": f"16-token prompt + {n} decode steps (context < 32)"}
 
 
 def run_ours(args):
@@ -168,6 +547,8 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", init_method="env://", device_id=dev)
     lib = _lib.load()
+    hbm, bf16, peak_kind = peaks()
+    cores = host_cores()
 
     ws, x = make_weights(rank)
     dws = [torch.from_numpy(w).to(dev) for w in ws]
@@ -216,10 +597,12 @@ def run_ours(args):
         # Correctness spot check of the timed outputs (one copy) vs the oracle.
         import oracle as O
         if rank == 0:
+            O.set_threads(cores)
             ref = O.matmul(Q4_K, ws[0], x, M, K)
             err = float(np.abs(dys[0].cpu().numpy() - ref).max() / np.abs(ref).max())
         else:
             err = None
+    del g
 
     # End-to-end through the C-ABI context API with host buffers.
     ctx = lib.vtb_cuda_init(local)
@@ -253,26 +636,29 @@ def run_ours(args):
     for b in wbufs + ybufs + [xb]:
         lib.vtb_cuda_release(b)
     lib.vtb_cuda_destroy(ctx)
+    del dws, dys
+    torch.cuda.empty_cache()
 
-    # The 8B model metrics build the whole seeded weight set (~5 GB host memory)
-    # on every rank, so they run at N <= 2 only; an error there is reported in
-    # the line instead of failing the GEMV measurement.
-    model = None
-    if args.model_steps > 0 and world <= 2:
+    work = {}
+
+    def leg(name, fn):
         try:
-            model = model_metrics(rank, world, local, dist, args)
+            work[name] = fn()
         except Exception as ex:  # noqa: BLE001 -- recorded in the JSON line
-            model = {"error": f"{type(ex).__name__}: {ex}"[:300]}
-    elif args.model_steps > 0:
-        model = {"skipped": "Llama-3-8B tensor-parallel metrics run at 1 or 2 GPUs (host memory per rank)"}
+            work[name] = {"error": f"{type(ex).__name__}: {ex}"[:300]}
+
+    if world == 1 and not args.no_sweeps:
+        leg("gemv_sweep", lambda: gemv_sweep(dev, hbm, cores))
+        leg("prefill_gemm", lambda: prefill_gemm(dev, bf16, cores))
+        leg("tinyllama", lambda: tinyllama(local, hbm, cores))
+    if args.model_steps > 0:
+        leg("llama3_8b", lambda: llama3_8b(rank, world, local, dist, args, hbm, cores))
 
     if rank == 0:
-        hbm, peak_kind = peaks()
         launches = args.steps * N_COPIES
         value = world * launches * ALG_BYTES / (ms_max / 1e3) / 1e9
         per_launch_ms = ms / launches
         achieved = ALG_BYTES / (per_launch_ms / 1e3) / 1e9
-        cpu_v, cpu_n = cpu_gemv_rate(ws, x, args.cpu_budget, os.cpu_count() or 1) if world == 1 else (None, 0)
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -286,91 +672,19 @@ def run_ours(args):
                     "h2d_bytes_per_step": K * 4, "d2h_bytes_per_step": N_COPIES * M * 4},
             "clocks": clk.summary(),
             "max_rel_err_vs_oracle": err,
+            "workloads": work,
         }
-        if model:
-            line["config"]["model_8b"] = model
-        if cpu_v is not None:
-            line["cpu_baseline"] = {"value": cpu_v, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+        if world == 1:
+            cpu_v, cpu_n = cpu_gemv_rate(ws, x, args.cpu_budget, cores)
+            cpu_half, _ = cpu_gemv_rate(ws, x, min(args.cpu_budget, 3.0), (cores + 1) // 2)
+            line["cpu_baseline"] = {"value": cpu_v, "unit": "GB/s", "cores": cores, "kind": "port",
                                     "sample": f"{cpu_n} GEMVs of 5632x2048 Q4_K over {args.cpu_budget:.0f} s, "
-                                              "oracle port of simd.zig matmul_q4_k + pool.zig row striping"}
+                                              "oracle port of simd.zig matmul_q4_k + pool.zig row striping",
+                                    "reference_default_threads": (cores + 1) // 2,
+                                    "value_at_reference_default_threads": cpu_half}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
-
-
-# DRAM bytes (read + write) of one config-1 launch, from the ncu capture summarised in
-# profiles/q4k_gemv_5632x2048.md (6,545,152 read, ~0 written; algorithmic 6,518,784).
-ALG_BYTES_TRAFFIC = 6545152
-
-
-def model_metrics(rank: int, world: int, local: int, dist, args) -> dict:
-    """BASELINE config 5 (Llama-3-8B architecture, random init, Q4_K_M-style):
-    decode tok/s at batch 1 and 32 and prefill tok/s of a 2048-token prompt,
-    tensor parallel over all ranks (NCCL).  Wall-clocked per call (each call
-    ends with its logits/argmax on the host), max over ranks."""
-    import torch
-    from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState, HostWeights, TensorParallel
-
-    def exchange(b: bytes) -> bytes:
-        if world == 1:
-            return b
-        obj = [b]
-        dist.broadcast_object_list(obj, src=0)
-        return obj[0]
-
-    def tmax(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    cfg = LLAMA3_8B
-    w = HostWeights(cfg, seed=8)
-    ctx = Context(local)
-    tp = TensorParallel(local, rank, world, exchange) if world > 1 else None
-    m = CudaModel(ctx, w, tp)
-    del w
-    res = {"model": "llama3_8b_random_init_q4_k_m", "tp": world}
-    rng = np.random.default_rng(1)
-    # prefill: 2048-token prompt
-    st = CudaState(m, 1, max_rows=2048)
-    prompt = rng.integers(3, cfg.vocab_size, 2048)
-    st.prefill(prompt[:64]); st.reset()  # warm-up
-    barrier(); t0 = time.perf_counter()
-    st.prefill(prompt)
-    res["prefill_2048_tok_s"] = 2048 / tmax(time.perf_counter() - t0)
-    # decode, batch 1, continuing after the prompt
-    nxt = 5
-    for _ in range(3):
-        _, am = st.step([nxt], want_logits=False); nxt = int(am[0])
-    n = args.model_steps
-    barrier(); t0 = time.perf_counter()
-    for _ in range(n):
-        _, am = st.step([nxt], want_logits=False); nxt = int(am[0])
-    res["decode_b1_tok_s"] = n / tmax(time.perf_counter() - t0)
-    res["decode_b1_ctx"] = int(st.pos())
-    st.close()
-    # decode, batch 32 (32 independent sequences, one token each per step)
-    st = CudaState(m, 32, max_rows=32)
-    toks = rng.integers(3, cfg.vocab_size, 32)
-    for _ in range(3):
-        _, toks = st.step(toks, want_logits=False)
-    nb = max(2, n // 4)
-    barrier(); t0 = time.perf_counter()
-    for _ in range(nb):
-        _, toks = st.step(toks, want_logits=False)
-    res["decode_b32_tok_s"] = 32 * nb / tmax(time.perf_counter() - t0)
-    st.close()
-    m.close()
-    if tp:
-        tp.close()
-    ctx.close()
-    return res
 
 
 def run_profile_case(case: str) -> None:
@@ -384,18 +698,31 @@ def run_profile_case(case: str) -> None:
             x = torch.from_numpy(S.activations(rng, K)).cuda()
             ops.gemv(Q4_K, w, x, m, K)
             torch.cuda.synchronize()
+    elif case == "gemv_chain":  # the bench's chained config-1 launches, 3 replays of 64
+        ws = [torch.from_numpy(S.quant_tensor(rng, Q4_K, M, K)).cuda() for _ in range(N_COPIES)]
+        x = torch.from_numpy(S.activations(rng, K)).cuda()
+        ys = [torch.empty(M, device="cuda") for _ in range(N_COPIES)]
+        for _ in range(3):
+            for i in range(N_COPIES):
+                ops.gemv(Q4_K, ws[i], x, M, K, out=ys[i], pdl=True)
     elif case == "gemv_q6k":  # Q6_K ffn_down 4096 x 14336, then the LM head 128256 x 4096 (431 MB)
         for m, k in ((4096, 14336), (128256, 4096)):
             w = torch.from_numpy(S.quant_tensor(rng, S.Q6_K, m, k)).cuda()
             x = torch.from_numpy(S.activations(rng, k)).cuda()
             ops.gemv(S.Q6_K, w, x, m, k)
             torch.cuda.synchronize()
-    elif case == "gemm":  # config 3: Q4_K 14336 x 4096, B = 2048, bf16 mode, two launches
+    elif case == "gemm":  # Q4_K 14336 x 4096, B = 2048, bf16 mode, two launches
         m, k, b = 14336, 4096, 2048
         w = torch.from_numpy(S.quant_tensor(rng, Q4_K, m, k)).cuda()
         acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
         for _ in range(2):
             ops.gemm(Q4_K, w, acts, m, k, precise=False)
+    elif case == "gemm_precise":  # the model prefill's mode: Q4_K 14336 x 4096, B = 2048, precise, two launches
+        m, k, b = 14336, 4096, 2048
+        w = torch.from_numpy(S.quant_tensor(rng, Q4_K, m, k)).cuda()
+        acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
+        for _ in range(2):
+            ops.gemm(Q4_K, w, acts, m, k, precise=True)
     elif case == "gemm_b32":  # batch decode shape: Q6_K ffn_down 4096 x 14336, B = 32, precise mode, two launches
         m, k, b = 4096, 14336, 32
         w = torch.from_numpy(S.quant_tensor(rng, S.Q6_K, m, k)).cuda()
@@ -424,15 +751,21 @@ def run_profile_case(case: str) -> None:
     print("ok", case)
 
 
+PROFILE_CASES = ["gemv", "gemv_chain", "gemv_q6k", "gemm", "gemm_precise", "gemm_b32", "decode", "decode8b",
+                 "decode8b_b32"]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
-    ap.add_argument("--model-steps", type=int, default=32, help="decode steps of the 8B model metrics (0 = skip)")
-    ap.add_argument("--profile", choices=["gemv", "gemv_q6k", "gemm", "decode", "decode8b", "decode8b_b32", "gemm_b32"], help="run a small case for ncu and exit")
+    ap.add_argument("--model-steps", type=int, default=512,
+                    help="batch-1 decode steps of the Llama-3-8B workload (<= 512; 0 = skip it)")
+    ap.add_argument("--no-sweeps", action="store_true", help="skip the single-GPU workload sweeps")
+    ap.add_argument("--profile", choices=PROFILE_CASES, help="run a small case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)

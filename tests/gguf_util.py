@@ -3,10 +3,7 @@ writer), the independent producer the library's reader is tested against."""
 import numpy as np
 from gguf import GGMLQuantizationType, GGUFWriter
 
-from vantablack_b200.model import MATS
-
-GGUF_NAMES = {"attn_q": "attn_q", "attn_k": "attn_k", "attn_v": "attn_v", "attn_o": "attn_output",
-              "ffn_gate": "ffn_gate", "ffn_up": "ffn_up", "ffn_down": "ffn_down"}
+from vantablack_b200.model import GGUF_NAMES, MATS  # noqa: F401 -- GGUF_NAMES re-exported for the tests
 
 
 def _rows(cfg, n):

@@ -144,3 +144,33 @@ def test_status_codes_of_a_failed_open(tmp_path):
     assert b"not a GGUF file" in lib.vtb_cuda_last_error()
     assert lib.vtb_cuda_status_string(-2) == b"file cannot be opened"
     assert lib.vtb_cuda_status_string(-3) == b"malformed model file"
+
+
+def test_library_writer_streams_the_seeded_model(tmp_path):
+    """write_synthetic_gguf (the library's own streaming writer) produces a file
+    that gguf-py reads back to the HostWeights bytes, and that the library's
+    reader maps to the same arrays (HostWeights.from_gguf)."""
+    import gguf
+    from vantablack_b200.model import write_synthetic_gguf
+    quants = {"attn_v": S.Q6_K, "ffn_gate": S.Q5_K, "ffn_up": S.Q8_0}
+    w = HostWeights(SMALL, seed=21, quants=quants)
+    p = str(tmp_path / "w.gguf")
+    write_synthetic_gguf(p, SMALL, seed=21, quants=quants)
+    r = gguf.GGUFReader(p)
+    by_name = {t.name: t for t in r.tensors}
+    for i, lw in enumerate(w.layers):
+        for n in MATS:
+            q, arr = lw[n]
+            t = by_name[f"blk.{i}.{GGUF_NAMES[n]}.weight"]
+            assert int(t.tensor_type) == q
+            assert np.array_equal(np.asarray(t.data).reshape(-1).view(np.uint8), arr)
+        assert np.array_equal(np.asarray(by_name[f"blk.{i}.ffn_norm.weight"].data), lw["ffn_norm"])
+    assert np.array_equal(np.asarray(by_name["output.weight"].data).reshape(-1).view(np.uint8), w.output[1])
+    g = HostWeights.from_gguf(p)
+    assert g.cfg.dim == SMALL.dim and g.cfg.vocab_size == SMALL.vocab_size and g.cfg.n_kv_heads == 2
+    for i in range(SMALL.n_layers):
+        for n in MATS:
+            assert g.layers[i][n][0] == w.layers[i][n][0]
+            assert np.array_equal(g.layers[i][n][1], w.layers[i][n][1])
+        assert np.array_equal(g.layers[i]["attn_norm"], w.layers[i]["attn_norm"])
+    assert np.array_equal(g.token_embd[1], w.token_embd[1]) and np.array_equal(g.output_norm, w.output_norm)

@@ -320,7 +320,13 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
       }
       x_chunk = c;
     }
-    if (!mbar_wait_bounded(&bars[st], (unsigned)((t / S) & 1))) return;
+    if (!mbar_wait_bounded(&bars[st], (unsigned)((t / S) & 1))) {
+      // Gave up (error word set).  Do not leave the CTA while copies into its
+      // shared memory may still land: drain every stage issued so far with a
+      // short bounded wait, compute nothing more, then return.
+      for (int u = t + 1; u < min(t + S, ntiles); ++u) mbar_wait_bounded(&bars[u % S], (unsigned)((u / S) & 1), 1u << 16);
+      return;
+    }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       if (r < nr && active) {

@@ -48,29 +48,111 @@ DEFAULT_QUANTS = {"attn_q": Q4_K, "attn_k": Q4_K, "attn_v": Q4_K, "attn_o": Q4_K
                   "ffn_up": Q4_K, "ffn_down": Q6_K, "token_embd": Q4_K, "output": Q6_K}
 
 
+# GGUF tensor names of the per-layer matrices (llama.cpp convention, read by
+# Model.init in src/runtime/model.zig:201-243).
+GGUF_NAMES = {"attn_q": "attn_q", "attn_k": "attn_k", "attn_v": "attn_v", "attn_o": "attn_output",
+              "ffn_gate": "ffn_gate", "ffn_up": "ffn_up", "ffn_down": "ffn_down"}
+
+
+def mat_shapes(cfg: LlamaConfig) -> dict:
+    """(rows, k) of each per-layer matrix."""
+    d, kvd, f = cfg.dim, cfg.n_kv_heads * cfg.head_dim, cfg.ffn_dim
+    return {"attn_q": (d, d), "attn_k": (kvd, d), "attn_v": (kvd, d), "attn_o": (d, d),
+            "ffn_gate": (f, d), "ffn_up": (f, d), "ffn_down": (d, f)}
+
+
+def synth_tensors(cfg: LlamaConfig, seed: int = 0, quants: dict | None = None, emit: bool = True):
+    """The seeded random-init tensors of a Llama config, in generation order.
+
+    Yields (gguf_name, key, layer, quant, rows, k, array): per layer the seven
+    matrices (MATS order), then attn_norm and ffn_norm (f32, quant 0); then
+    token_embd, output_norm and output.  One PCG64 stream, so the bytes depend
+    only on (cfg, seed, quants).  With emit=False only the metadata is yielded
+    (array None, nothing generated)."""
+    q = dict(DEFAULT_QUANTS, **(quants or {}))
+    rng = np.random.default_rng(seed) if emit else None
+    shp = mat_shapes(cfg)
+    d = cfg.dim
+    for i in range(cfg.n_layers):
+        for n in MATS:
+            rows, k = shp[n]
+            yield (f"blk.{i}.{GGUF_NAMES[n]}.weight", n, i, q[n], rows, k,
+                   quant_tensor(rng, q[n], rows, k) if emit else None)
+        for n in ("attn_norm", "ffn_norm"):
+            yield f"blk.{i}.{n}.weight", n, i, 0, 1, d, norm_weight(rng, d) if emit else None
+    yield ("token_embd.weight", "token_embd", -1, q["token_embd"], cfg.vocab_size, d,
+           quant_tensor(rng, q["token_embd"], cfg.vocab_size, d) if emit else None)
+    yield "output_norm.weight", "output_norm", -1, 0, 1, d, norm_weight(rng, d) if emit else None
+    yield ("output.weight", "output", -1, q["output"], cfg.vocab_size, d,
+           quant_tensor(rng, q["output"], cfg.vocab_size, d) if emit else None)
+
+
 class HostWeights:
     """Seeded random-init weights of a Llama config (numpy, host memory)."""
 
     def __init__(self, cfg: LlamaConfig, seed: int = 0, quants: dict | None = None):
-        q = dict(DEFAULT_QUANTS, **(quants or {}))
-        rng = np.random.default_rng(seed)
-        d, kvd, f = cfg.dim, cfg.n_kv_heads * cfg.head_dim, cfg.ffn_dim
-        shapes = {"attn_q": (d, d), "attn_k": (kvd, d), "attn_v": (kvd, d), "attn_o": (d, d),
-                  "ffn_gate": (f, d), "ffn_up": (f, d), "ffn_down": (d, f)}
         self.cfg = cfg
-        self.layers = []
-        for _ in range(cfg.n_layers):
-            lw = {n: (q[n], quant_tensor(rng, q[n], *shapes[n])) for n in MATS}
-            lw["attn_norm"] = norm_weight(rng, d)
-            lw["ffn_norm"] = norm_weight(rng, d)
-            self.layers.append(lw)
-        self.token_embd = (q["token_embd"], quant_tensor(rng, q["token_embd"], cfg.vocab_size, d))
-        self.output_norm = norm_weight(rng, d)
-        self.output = (q["output"], quant_tensor(rng, q["output"], cfg.vocab_size, d))
+        self.layers = [{} for _ in range(cfg.n_layers)]
+        self._absorb(synth_tensors(cfg, seed, quants))
+
+    def _absorb(self, items):
+        for _, key, layer, q, _, _, arr in items:
+            if layer >= 0:
+                self.layers[layer][key] = (q, arr) if key in MATS else arr
+            elif key == "output_norm":
+                self.output_norm = arr
+            else:
+                setattr(self, key, (q, arr))
+
+    @classmethod
+    def from_gguf(cls, path: str) -> "HostWeights":
+        """Zero-copy numpy views of a llama GGUF file (np.memmap over the file,
+        offsets from the library's own reader), e.g. for the CPU oracle."""
+        from .gguf import GgufFile
+        with GgufFile(path) as g:
+            cfg = g.llama_config()
+            base = g.info()["data_offset"]
+            ts = {t["name"]: t for t in g.tensors()}
+        mm = np.memmap(path, np.uint8, "r")
+        self = cls.__new__(cls)
+        self.cfg = cfg
+        self.layers = [{} for _ in range(cfg.n_layers)]
+        self._mm = mm
+        items = []
+        for name, key, layer, _, _, _, _ in synth_tensors(cfg, emit=False):
+            t = ts.get(name) or (ts["token_embd.weight"] if name == "output.weight" else None)
+            if t is None:
+                raise KeyError(name)
+            a = mm[base + t["rel_offset"]: base + t["rel_offset"] + t["size"]]
+            if t["type"] == 0:
+                a = a.view(np.float32)
+            items.append((name, key, layer, t["type"], 0, 0, a))
+        self._absorb(items)
+        return self
 
     def nbytes(self) -> int:
         n = sum(a.nbytes for lw in self.layers for k, v in lw.items() for a in ([v[1]] if k in MATS else [v]))
         return n + self.token_embd[1].nbytes + self.output[1].nbytes + self.output_norm.nbytes
+
+
+def write_synthetic_gguf(path: str, cfg: LlamaConfig, seed: int = 0, quants: dict | None = None) -> None:
+    """Streams synth_tensors(cfg, seed, quants) into a llama GGUF file tensor by
+    tensor (host memory holds one tensor at a time); the file loads through
+    vtb_cuda_model_create_gguf[_tp] to the same weights as HostWeights(cfg, seed, quants)."""
+    from .gguf import write_gguf
+    meta = [("general.architecture", "str", "llama"),
+            ("llama.context_length", "u32", cfg.max_seq),
+            ("llama.embedding_length", "u32", cfg.dim),
+            ("llama.block_count", "u32", cfg.n_layers),
+            ("llama.feed_forward_length", "u32", cfg.ffn_dim),
+            ("llama.attention.head_count", "u32", cfg.n_heads),
+            ("llama.attention.head_count_kv", "u32", cfg.n_kv_heads),
+            ("llama.rope.freq_base", "f32", cfg.rope_base),
+            ("llama.attention.layer_norm_rms_epsilon", "f32", cfg.rms_eps),
+            ("llama.vocab_size", "u32", cfg.vocab_size)]
+    infos = [(name, q, [k] if q == 0 else [k, rows]) for name, _, _, q, rows, k, _ in
+             synth_tensors(cfg, seed, quants, emit=False)]
+    write_gguf(path, meta, infos, (a for *_, a in synth_tensors(cfg, seed, quants)))
 
 
 class _CConfig(C.Structure):
