@@ -59,6 +59,21 @@ const char *vtb_cuda_version_string(void);
 /* 1 when a CUDA device of compute capability 10.x is visible (cf. vtb_has_metal,
  * include/vantablack.h:131). */
 int vtb_cuda_available(void);
+/* The vtable's `capabilities` slot (src/runtime/backend.zig:43-55, :93):
+ * what this backend reports to the forward loop.  supports_fused_qkv = 1
+ * (Q|K|V and gate|up rows are concatenated at upload), supports_kquant_gpu =
+ * 1, supports_mlx_q4 = 0, unified_memory = 0 (weights and state live in HBM;
+ * finalize_token copies the logits to the host).  `name` is a static string.
+ * `ctx` may be NULL; with a context the device is checked to be sm_100. */
+typedef struct VtbCudaCapabilities {
+  int32_t supports_fused_qkv;
+  int32_t supports_kquant_gpu;
+  int32_t supports_mlx_q4;
+  int32_t unified_memory;
+  const char *name;
+} VtbCudaCapabilities;
+struct VtbCudaCtx;
+int vtb_cuda_capabilities(const struct VtbCudaCtx *ctx, VtbCudaCapabilities *out);
 /* Human-readable text for a status code. */
 const char *vtb_cuda_status_string(int status);
 /* Text of the last CUDA error this thread saw inside the library. */

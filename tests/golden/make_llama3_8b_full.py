@@ -1,5 +1,5 @@
 """Generates tests/golden/llama3_8b_p2048_g512.npz: the CPU oracle's greedy
-run of BASELINE config 5 at full size — Llama-3-8B architecture, Q4_K_M-style
+run of the full-size Llama-3-8B workload — Llama-3-8B architecture, Q4_K_M-style
 random init (HostWeights seed 5), a seeded 2048-token prompt (batched
 prefill) and 512 greedy decode steps.  Stored: the 512 token ids, the
 16 largest logits (indices and values) of each of the 512 logit vectors the

@@ -49,3 +49,16 @@ def test_argument_checks_without_launch(lib):
     assert b"aligned" in lib.vtb_cuda_last_error() or lib.vtb_cuda_last_error()
     assert lib.vtb_cuda_dequant(14, p, p, 100, None) == -1
     assert lib.vtb_cuda_quantize_q8_0(p, 33, p, p, None) == -1
+
+
+def test_capabilities_slot_without_a_device(lib):
+    """vtb_cuda_capabilities fills the vtable's Capabilities (backend.zig:43-55)."""
+    class Caps(ctypes.Structure):
+        _fields_ = [("supports_fused_qkv", ctypes.c_int32), ("supports_kquant_gpu", ctypes.c_int32),
+                    ("supports_mlx_q4", ctypes.c_int32), ("unified_memory", ctypes.c_int32),
+                    ("name", ctypes.c_char_p)]
+    c = Caps()
+    assert lib.vtb_cuda_capabilities(None, ctypes.byref(c)) == 0
+    assert (c.supports_fused_qkv, c.supports_kquant_gpu, c.supports_mlx_q4, c.unified_memory) == (1, 1, 0, 0)
+    assert b"b200" in c.name
+    assert lib.vtb_cuda_capabilities(None, None) == -1

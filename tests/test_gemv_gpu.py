@@ -34,7 +34,7 @@ def test_dequant_bit_exact(q):
 
 
 GEMV_SHAPES = [
-    (S.Q4_K, 5632, 2048),   # config 1 (TinyLlama ffn_up)
+    (S.Q4_K, 5632, 2048),   # TinyLlama ffn_up (the headline GEMV shape)
     (S.Q4_K, 1024, 4096), (S.Q4_K, 14336, 4096),
     (S.Q6_K, 4096, 4096), (S.Q6_K, 4096, 14336), (S.Q6_K, 2048, 5632),  # ragged Q6_K rows (4620 B)
     (S.Q8_0, 4096, 4096), (S.Q8_0, 14336, 4096), (S.Q8_0, 4096, 14336),

@@ -38,6 +38,7 @@ SIGNATURES = {
     "vtb_cuda_gemv_q8_0_q8_0_noalloc": (_int, [_vp, _vp, _vp, _i64, _i64, _vp, _int]),
     "vtb_cuda_gemm_workspace_bytes": (_sz, [_i64, _i64, _int]),
     "vtb_cuda_gemm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _vp]),
+    "vtb_cuda_capabilities": (_int, [_vp, _vp]),
     "vtb_cuda_init": (_vp, [_int]),
     "vtb_cuda_destroy": (None, [_vp]),
     "vtb_cuda_stream": (_vp, [_vp]),

@@ -203,6 +203,24 @@ static bool use_ctx(VtbCudaCtx* c) { return c && cudaSetDevice(c->device) == cud
 
 extern "C" {
 
+int vtb_cuda_capabilities(const VtbCudaCtx* ctx, VtbCudaCapabilities* out) {
+  if (!out) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null output");
+  out->supports_fused_qkv = 1;
+  out->supports_kquant_gpu = 1;
+  out->supports_mlx_q4 = 0;
+  out->unified_memory = 0;
+  out->name = "cuda-b200 (sm_100a)";
+  if (ctx) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, ctx->device) != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(VTB_CUDA_ERR_DEVICE, "cannot query the context's device");
+    }
+    if (major != 10) return set_err(VTB_CUDA_ERR_DEVICE, "the context's device is not sm_100");
+  }
+  return VTB_CUDA_OK;
+}
+
 VtbCudaCtx* vtb_cuda_init(int device_ordinal) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess || device_ordinal < 0 || device_ordinal >= n) {

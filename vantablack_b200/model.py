@@ -36,10 +36,10 @@ class LlamaConfig:
         return replace(self, **kw)
 
 
-# BASELINE config 4: TinyLlama-1.1B architecture.
+# TinyLlama-1.1B architecture.
 TINYLLAMA = LlamaConfig(dim=2048, n_layers=22, n_heads=32, n_kv_heads=4, head_dim=64, ffn_dim=5632,
                         vocab_size=32000, max_seq=2048, rope_base=10000.0)
-# Llama-3-8B architecture (context 2048 prefill + 512 decode).
+# Llama-3-8B architecture (max_seq covers a 2048-token prefill + 512 decode steps).
 LLAMA3_8B = LlamaConfig(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336,
                         vocab_size=128256, max_seq=2560, rope_base=500000.0)
 
