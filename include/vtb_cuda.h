@@ -49,6 +49,9 @@ extern "C" {
 #define VTB_CUDA_Q4_K 12
 #define VTB_CUDA_Q5_K 13
 #define VTB_CUDA_Q6_K 14
+/* TQ2_0 (66 B / 256 weights) with the reference's GgmlType id (parser.zig:62) and
+ * its block layout (simd.zig:436-472), which differs from ggml's. */
+#define VTB_CUDA_TQ2_0 32
 
 /* ------------------------------------------------------------------ */
 /* Introspection                                                        */
@@ -199,6 +202,10 @@ int vtb_cuda_matmul_q5_k(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf
                          VtbCudaBuf *acts_buf, size_t m, size_t k);
 int vtb_cuda_matmul_q6_k(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
                          VtbCudaBuf *acts_buf, size_t m, size_t k);
+/* TQ2_0: the reference's matmul_ternary158 (simd.zig:474-498), which it runs
+ * on the CPU only; same signature as the bridge matmuls above. */
+int vtb_cuda_matmul_tq2_0(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                          VtbCudaBuf *acts_buf, size_t m, size_t k);
 
 /* ------------------------------------------------------------------ */
 /* Llama forward loop (the backend vtable, src/runtime/backend.zig:67-97) */

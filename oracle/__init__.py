@@ -20,7 +20,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libvtb_oracle.so")
 
-F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
+F32, Q8_0, Q4_K, Q5_K, Q6_K, TQ2_0 = 0, 8, 12, 13, 14, 32
 
 _u8p = C.POINTER(C.c_uint8)
 _f32p = C.POINTER(C.c_float)
@@ -50,6 +50,7 @@ def _load():
         "vtbo_matmul_q4_k": (None, [_f32p, _u8p, _f32p, _sz, _sz]),
         "vtbo_matmul_q5_k": (None, [_f32p, _u8p, _f32p, _sz, _sz]),
         "vtbo_matmul_q6_k": (None, [_f32p, _u8p, _f32p, _sz, _sz]),
+        "vtbo_matmul_tq2_0": (None, [_f32p, _u8p, _f32p, _sz, _sz]),
         "vtbo_pool_init": (C.c_int, [C.c_int]),
         "vtbo_pool_threads": (C.c_int, []),
         "vtbo_pool_shutdown": (None, []),
@@ -127,7 +128,8 @@ def dot_i8(a: np.ndarray, b: np.ndarray) -> int:
     return lib.vtbo_dot_i8(_p(a, _i8p), _p(b, _i8p), a.size)
 
 
-_SINGLE = {Q8_0: "vtbo_matmul_q8_0", Q4_K: "vtbo_matmul_q4_k", Q5_K: "vtbo_matmul_q5_k", Q6_K: "vtbo_matmul_q6_k"}
+_SINGLE = {Q8_0: "vtbo_matmul_q8_0", Q4_K: "vtbo_matmul_q4_k", Q5_K: "vtbo_matmul_q5_k", Q6_K: "vtbo_matmul_q6_k",
+           TQ2_0: "vtbo_matmul_tq2_0"}
 
 
 def matmul_single(quant: int, w: np.ndarray, x: np.ndarray, m: int, k: int) -> np.ndarray:

@@ -199,6 +199,23 @@ void vtbo_dequant_q6_k_block(const uint8_t *blk, float *out) {
     }
 }
 
+/* dequantBlockTQ2_0, simd.zig:457-472, exactly as the reference writes it:
+ * weight 64g + l of a 256-weight block is (((qs[16g + l % 16] >> 2g) & 3) - 1)
+ * times the f16 scale at bytes 64..65.  (ggml's own TQ2_0 layout differs; the
+ * reference's is the one restated here, pinned by its test at simd.zig:734-768.) */
+#define TQ2_0_BYTES 66
+void vtbo_dequant_tq2_0_block(const uint8_t *blk, float *out) {
+    const float scale = vtbo_f16_to_f32((uint16_t)(blk[64] | (blk[65] << 8)));
+    for (int g = 0; g < 4; g++) {
+        const int shift = 2 * g, base = g * 16;
+        for (int l = 0; l < 64; l++) {
+            const uint8_t raw = (uint8_t)((blk[base + (l % 16)] >> shift) & 0x03u);
+            const float tern = (float)(int32_t)raw - 1.0f;
+            out[g * 64 + l] = scale * tern;
+        }
+    }
+}
+
 size_t vtbo_row_bytes(int quant, size_t k) {
     switch (quant) {
     case VTBO_F32: return k * 4;
@@ -206,6 +223,7 @@ size_t vtbo_row_bytes(int quant, size_t k) {
     case VTBO_Q4_K: return (k / QK_K) * Q4_K_BYTES;
     case VTBO_Q5_K: return (k / QK_K) * Q5_K_BYTES;
     case VTBO_Q6_K: return (k / QK_K) * Q6_K_BYTES;
+    case VTBO_TQ2_0: return (k / QK_K) * TQ2_0_BYTES;
     default: return 0;
     }
 }
@@ -225,6 +243,9 @@ int vtbo_dequant(int quant, const uint8_t *w, float *out, size_t n) {
         return 0;
     case VTBO_Q6_K:
         for (size_t b = 0; b < n / QK_K; b++) vtbo_dequant_q6_k_block(w + b * Q6_K_BYTES, out + b * QK_K);
+        return 0;
+    case VTBO_TQ2_0:
+        for (size_t b = 0; b < n / QK_K; b++) vtbo_dequant_tq2_0_block(w + b * TQ2_0_BYTES, out + b * QK_K);
         return 0;
     default: return -1;
     }
@@ -257,6 +278,10 @@ static void matmul_kquant(dq_fn dq, size_t bbytes, float *out, const uint8_t *w,
 
 void vtbo_matmul_q4_k(float *out, const uint8_t *w, const float *acts, size_t m, size_t k) {
     matmul_kquant(vtbo_dequant_q4_k_block, Q4_K_BYTES, out, w, acts, m, k);
+}
+/* matmul_ternary158, simd.zig:474-498: the same per-block structure. */
+void vtbo_matmul_tq2_0(float *out, const uint8_t *w, const float *acts, size_t m, size_t k) {
+    matmul_kquant(vtbo_dequant_tq2_0_block, TQ2_0_BYTES, out, w, acts, m, k);
 }
 void vtbo_matmul_q5_k(float *out, const uint8_t *w, const float *acts, size_t m, size_t k) {
     matmul_kquant(vtbo_dequant_q5_k_block, Q5_K_BYTES, out, w, acts, m, k);
@@ -413,6 +438,7 @@ static void matmul_worker(int wid, int nw, void *p) {
     case VTBO_Q4_K: vtbo_matmul_q4_k(c->out + s, w, c->acts, e - s, c->k); break;
     case VTBO_Q5_K: vtbo_matmul_q5_k(c->out + s, w, c->acts, e - s, c->k); break;
     case VTBO_Q6_K: vtbo_matmul_q6_k(c->out + s, w, c->acts, e - s, c->k); break;
+    case VTBO_TQ2_0: vtbo_matmul_tq2_0(c->out + s, w, c->acts, e - s, c->k); break;
     case MM_Q8_0_Q8_0: matmul_q8_0_q8_0_rows(c->out + s, w, c->xq, c->dx, e - s, c->k); break;
     default: break;
     }

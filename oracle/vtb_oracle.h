@@ -37,6 +37,7 @@ enum {
     VTBO_Q4_K = 12,
     VTBO_Q5_K = 13,
     VTBO_Q6_K = 14,
+    VTBO_TQ2_0 = 32, /* the reference's GgmlType id (parser.zig:62) */
 };
 
 float vtbo_f16_to_f32(uint16_t bits);
@@ -47,6 +48,7 @@ void vtbo_dequant_q8_0_block(const uint8_t *blk, float *out32);
 void vtbo_dequant_q4_k_block(const uint8_t *blk, float *out256);
 void vtbo_dequant_q5_k_block(const uint8_t *blk, float *out256);
 void vtbo_dequant_q6_k_block(const uint8_t *blk, float *out256);
+void vtbo_dequant_tq2_0_block(const uint8_t *blk, float *out256);
 /* Dequantize n elements (a whole number of blocks) of type `quant`. */
 int vtbo_dequant(int quant, const uint8_t *w, float *out, size_t n);
 
@@ -57,6 +59,7 @@ void vtbo_matmul_q8_0(float *out, const uint8_t *w, const float *acts, size_t m,
 void vtbo_matmul_q4_k(float *out, const uint8_t *w, const float *acts, size_t m, size_t k);
 void vtbo_matmul_q5_k(float *out, const uint8_t *w, const float *acts, size_t m, size_t k);
 void vtbo_matmul_q6_k(float *out, const uint8_t *w, const float *acts, size_t m, size_t k);
+void vtbo_matmul_tq2_0(float *out, const uint8_t *w, const float *acts, size_t m, size_t k);
 
 /* Thread pool with the reference's row striping (chunk = ceil(m/n)). */
 int vtbo_pool_init(int n_threads);

@@ -26,6 +26,7 @@ def rel(a, b):
     (S.Q6_K, 4096, 14336, 87),   # Llama-3-8B ffn_down, B = 87
     (S.Q4_K, 512, 4096, 512), (S.Q6_K, 256, 14336, 512), (S.Q4_K, 384, 4096, 2048),
     (S.Q5_K, 300, 2048, 17), (S.Q8_0, 200, 1024, 33), (S.Q6_K, 130, 5632, 1), (S.Q4_K, 1, 256, 300),
+    (S.TQ2_0, 300, 2304, 40), (S.TQ2_0, 256, 4096, 512),
 ])
 @pytest.mark.parametrize("precise", [False, True])
 def test_gemm_matches_oracle(q, m, k, B, precise):

@@ -23,7 +23,7 @@ def rel_err(got, ref):
     return float(np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))
 
 
-@pytest.mark.parametrize("q", [S.Q8_0, S.Q4_K, S.Q5_K, S.Q6_K])
+@pytest.mark.parametrize("q", [S.Q8_0, S.Q4_K, S.Q5_K, S.Q6_K, S.TQ2_0])
 def test_dequant_bit_exact(q):
     rng = np.random.default_rng(100 + q)
     m, k = 33, 2048
@@ -43,6 +43,7 @@ GEMV_SHAPES = [
     (S.Q4_K, 4111, 4608), (S.Q4_K, 96, 24576),  # ragged last 32-row tile at size; long-K fallback
     (S.Q4_K, 6144, 4096), (S.Q4_K, 1000, 2048),  # 16-row tiles (large and small launch variants)
     (S.Q6_K, 1000, 6144), (S.Q6_K, 17, 2048),  # Q6_K tensor-core path: ragged last 16-row tile
+    (S.TQ2_0, 4096, 4096), (S.TQ2_0, 14336, 4096), (S.TQ2_0, 1000, 2304), (S.TQ2_0, 3, 256),  # 594 B rows: ragged
 ]
 
 
@@ -97,16 +98,31 @@ def test_gemv_q8_0_q8_0_matches_oracle(m, k):
     assert rel_err(y, O.matmul_q8_0_q8_0(w, x, m, k)) <= TOL
 
 
-def test_embed_rows_bit_exact():
+@pytest.mark.parametrize("q", [S.Q4_K, S.TQ2_0])
+def test_embed_rows_bit_exact(q):
     rng = np.random.default_rng(4)
     vocab, dim = 100, 2048
-    t = S.quant_tensor(rng, S.Q4_K, vocab, dim)
+    t = S.quant_tensor(rng, q, vocab, dim)
     ids = np.array([0, 99, 3, 3, 57], np.int32)
-    got = ops().embed(S.Q4_K, torch.from_numpy(t).cuda(), torch.from_numpy(ids).cuda(), dim).cpu().numpy()
-    rb = S.row_bytes(S.Q4_K, dim)
+    got = ops().embed(q, torch.from_numpy(t).cuda(), torch.from_numpy(ids).cuda(), dim).cpu().numpy()
+    rb = S.row_bytes(q, dim)
     for i, r in enumerate(ids):
-        exp = O.dequant(S.Q4_K, t[r * rb:(r + 1) * rb], dim)
+        exp = O.dequant(q, t[r * rb:(r + 1) * rb], dim)
         assert np.array_equal(got[i].view(np.uint32), exp.view(np.uint32))
+
+
+def test_tq2_0_reference_kat_on_gpu():
+    """The reference's TQ2_0 known-answer block (simd.zig:734-768) through the
+    GPU dequantizer and GEMV."""
+    blk = np.zeros(66, np.uint8)
+    blk[64:66] = np.array([0.25], np.float16).view(np.uint8)
+    for i in range(64):
+        blk[i] = (i % 3) | (((i + 1) % 3) << 2) | (((i + 2) % 3) << 4) | ((i % 3) << 6)
+    dq = ops().dequant(S.TQ2_0, torch.from_numpy(blk).cuda(), 256).cpu().numpy()
+    assert np.array_equal(dq.view(np.uint32), O.dequant(S.TQ2_0, blk, 256).view(np.uint32))
+    x = (np.arange(256) % 5).astype(np.float32) * np.float32(0.2) - np.float32(0.1)
+    y = ops().gemv(S.TQ2_0, torch.from_numpy(blk).cuda(), torch.from_numpy(x).cuda(), 1, 256).cpu().numpy()
+    assert abs(float(y[0]) - float((dq.astype(np.float64) * x).sum())) <= 1e-3
 
 
 def test_context_bridge_matmul():
@@ -165,7 +181,7 @@ def test_context_bridge_chained_matmuls():
     lib.vtb_cuda_destroy(ctx)
 
 
-@pytest.mark.parametrize("q", [S.Q4_K, S.Q6_K, S.Q8_0, S.Q5_K])
+@pytest.mark.parametrize("q", [S.Q4_K, S.Q6_K, S.Q8_0, S.Q5_K, S.TQ2_0])
 @pytest.mark.parametrize("kind", ["huge", "tiny", "outliers", "zeros"])
 def test_gemv_activation_ranges(q, kind):
     """Activation magnitudes far from N(0,1): per-sub-block scaling must hold

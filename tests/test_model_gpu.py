@@ -113,12 +113,16 @@ def test_errors(small):
         CudaModel(ctx, bad)
 
 
-def test_q8_0_and_q5_k_models(small):
+def test_q8_0_q5_k_and_tq2_0_models(small):
     from vantablack_b200.model import Context, CudaModel, CudaState
     w, ctx, _ = small
-    for q in (S.Q8_0, S.Q5_K):
+    for q in (S.Q8_0, S.Q5_K, S.TQ2_0):
         qs = {n: q for n in ("attn_q", "attn_k", "attn_v", "attn_o", "ffn_gate", "ffn_up", "ffn_down")}
         hw = HostWeights(SMALL, seed=9, quants=dict(qs, token_embd=q, output=q))
         ids_ref, lr = O.Model(hw).generate_greedy([5, 6, 7], 8, use_prefill=False)
         ids, lg = CudaState(CudaModel(ctx, hw), 1).generate_greedy([5, 6, 7], 8, use_prefill=False)
         assert ids == ids_ref and rel(lg, lr) <= LTOL
+        # batched prefill (the tcgen05 GEMM path) of the same model
+        ids_p, lgp = CudaState(CudaModel(ctx, hw), 1, max_rows=16).generate_greedy(list(range(5, 21)), 4)
+        ids_pr, lpr = O.Model(hw).generate_greedy(list(range(5, 21)), 4, use_prefill=True)
+        assert ids_p == ids_pr and rel(lgp, lpr) <= LTOL, S.NAMES[q]

@@ -87,6 +87,37 @@ def test_q6_k_kat():  # simd.zig:699-732
     assert abs(got - float(np.dot(dq.astype(np.float64), x))) <= 1e-3
 
 
+def _tq2_kat_block():
+    """simd.zig:735-746: scale 0.25; byte i packs (i%3, (i+1)%3, (i+2)%3, i%3)."""
+    blk = np.zeros(66, np.uint8)
+    blk[64:66] = np.array([0.25], np.float16).view(np.uint8)
+    for i in range(64):
+        blk[i] = (i % 3) | (((i + 1) % 3) << 2) | (((i + 2) % 3) << 4) | ((i % 3) << 6)
+    return blk
+
+
+def test_tq2_0_kat():  # simd.zig:734-768 ("TQ2_0 dequant + matmul self-consistent")
+    blk = _tq2_kat_block()
+    dq = O.dequant(S.TQ2_0, blk, 256)
+    for g, idx in enumerate((0, 64, 128, 192)):  # spot checks at g*64 + l, l = idx - 64g
+        l = idx - g * 64
+        raw = (int(blk[g * 16 + (l % 16)]) >> (2 * g)) & 3
+        assert abs(dq[idx] - 0.25 * (raw - 1)) <= 1e-5
+    x = (np.arange(256) % 5).astype(np.float32) * np.float32(0.2) - np.float32(0.1)
+    got = O.matmul_single(S.TQ2_0, blk, x, 1, 256)[0]
+    assert abs(got - float((dq.astype(np.float64) * x).sum())) <= 1e-3
+    # the reference's layout: weights l, l+16, l+32, l+48 of a group share one field
+    assert np.array_equal(dq[0:16], dq[16:32]) and np.array_equal(dq[64:80], dq[112:128])
+
+
+def test_tq2_0_threaded_matmul_equals_single():
+    rng = np.random.default_rng(35)
+    m, k = 37, 1024
+    w = S.quant_tensor(rng, S.TQ2_0, m, k)
+    x = S.activations(rng, k)
+    assert np.array_equal(O.matmul(S.TQ2_0, w, x, m, k), O.matmul_single(S.TQ2_0, w, x, m, k))
+
+
 def test_matmul_q8_0_kat():  # simd.zig:770-806
     got = O.matmul(S.Q8_0, GOLD["mm_q8_0_w"], GOLD["mm_q8_0_x"], 4, 64)
     assert np.allclose(got, GOLD["mm_q8_0_y"], atol=1e-3)

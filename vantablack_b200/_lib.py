@@ -55,6 +55,7 @@ SIGNATURES = {
     "vtb_cuda_matmul_q4_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
     "vtb_cuda_matmul_q5_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
     "vtb_cuda_matmul_q6_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_matmul_tq2_0": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
     "vtb_cuda_model_create": (_vp, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _i32]),
     "vtb_cuda_model_destroy": (None, [_vp]),
     "vtb_cuda_model_weight_bytes": (_sz, [_vp]),

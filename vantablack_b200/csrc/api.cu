@@ -335,5 +335,8 @@ int vtb_cuda_matmul_q5_k(VtbCudaCtx* c, VtbCudaBuf* o, VtbCudaBuf* w, size_t off
 int vtb_cuda_matmul_q6_k(VtbCudaCtx* c, VtbCudaBuf* o, VtbCudaBuf* w, size_t off, VtbCudaBuf* a, size_t m, size_t k) {
   return ctx_matmul(Q6_K, c, o, w, off, a, m, k);
 }
+int vtb_cuda_matmul_tq2_0(VtbCudaCtx* c, VtbCudaBuf* o, VtbCudaBuf* w, size_t off, VtbCudaBuf* a, size_t m, size_t k) {
+  return ctx_matmul(TQ2_0, c, o, w, off, a, m, k);
+}
 
 }  // extern "C"

@@ -5,6 +5,8 @@
 //   Q4_K 144 B / 256        : f16 d | f16 dmin | u8 scales[12] | u8 qs[128]
 //   Q5_K 176 B / 256        : f16 d | f16 dmin | u8 scales[12] | u8 qh[32] | u8 qs[128]
 //   Q6_K 210 B / 256        : u8 ql[128] | u8 qh[64] | i8 sc[16] | f16 d
+//   TQ2_0 66 B / 256        : u8 qs[64] (2-bit fields) | f16 d   (the reference's layout,
+//                             src/kernels/simd.zig:436-472)
 #pragma once
 #include <atomic>
 #include <cstdint>
@@ -14,13 +16,15 @@
 
 namespace vtb {
 
-enum Quant : int { F32 = 0, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14 };
+// Type ids are the reference's GgmlType values (src/core/parser.zig:31-64); TQ2_0 is 32 there.
+enum Quant : int { F32 = 0, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, TQ2_0 = 32 };
 
 template <int Q> struct Fmt;
 template <> struct Fmt<Q8_0> { static constexpr int bytes = 34, elems = 32; };
 template <> struct Fmt<Q4_K> { static constexpr int bytes = 144, elems = 256; };
 template <> struct Fmt<Q5_K> { static constexpr int bytes = 176, elems = 256; };
 template <> struct Fmt<Q6_K> { static constexpr int bytes = 210, elems = 256; };
+template <> struct Fmt<TQ2_0> { static constexpr int bytes = 66, elems = 256; };
 
 // ---- per-device launch facts ----
 // Kernel attributes (the dynamic shared-memory opt-in) and occupancy are per
@@ -96,6 +100,7 @@ inline int64_t host_row_bytes(int q, int64_t k) {
     case Q4_K: return (k / 256) * 144;
     case Q5_K: return (k / 256) * 176;
     case Q6_K: return (k / 256) * 210;
+    case TQ2_0: return (k / 256) * 66;
     default: return -1;
   }
 }
@@ -104,7 +109,7 @@ __host__ __device__ __forceinline__ long long host_row_bytes_dev(long long k) {
   return (k / Fmt<Q>::elems) * Fmt<Q>::bytes;
 }
 inline int host_block_elems(int q) { return q == Q8_0 ? 32 : (q == F32 ? 1 : 256); }
-inline bool host_quant_ok(int q) { return q == Q8_0 || q == Q4_K || q == Q5_K || q == Q6_K; }
+inline bool host_quant_ok(int q) { return q == Q8_0 || q == Q4_K || q == Q5_K || q == Q6_K || q == TQ2_0; }
 
 // Device-side error word.  Kernels that give up a bounded wait OR a code in
 // here and return; the host reads it with vtb_cuda_check_device_error().
@@ -128,6 +133,12 @@ __device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
 }
 __device__ __forceinline__ f2 add2(f2 a, f2 b) {
   f2 r; asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v)); return r;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 r; asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v)); return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 r; asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v)); return r;
 }
 __device__ __forceinline__ float hsum(f2 a) { float x, y; unpk(a, x, y); return x + y; }
 

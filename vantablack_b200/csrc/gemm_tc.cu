@@ -93,8 +93,14 @@ __device__ __forceinline__ uint4 ld16(const uint8_t* p) {
   else return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
+// Weights [k0, k0 + 64) of one row as 32 packed pairs v[i] = (w[2i], w[2i+1]),
+// bit-identical to dequantToF32 (forward.zig:654-736).  Every format's product
+// is exact in f32 (an f16 scale times a small integer), so the packed
+// multiplies and the fused multiply-subtract of Q4_K/Q5_K (d1 * q - m1, the
+// product exact, one rounding) equal the reference's separately rounded ops.
+// Quantized values become exact floats with the 2^23 byte-magic.
 template <int Q, bool SMEM = false>
-__device__ __forceinline__ void dequant64(const uint8_t* row, int k0, float* v) {
+__device__ __forceinline__ void dequant64(const uint8_t* row, int k0, f2* v) {
   if constexpr (Q == Q4_K || Q == Q5_K) {
     constexpr int BB = Q == Q4_K ? 144 : 176;
     const uint8_t* blk = SMEM ? row : row + (k0 >> 8) * BB;  // SMEM: `row` is the staged super-block itself
@@ -115,6 +121,8 @@ __device__ __forceinline__ void dequant64(const uint8_t* row, int k0, float* v) 
     }
     const float d1 = __fmul_rn(d, (float)sc[0]), m1 = __fmul_rn(dmin, (float)mn[0]);
     const float d2 = __fmul_rn(d, (float)sc[1]), m2 = __fmul_rn(dmin, (float)mn[1]);
+    const f2 D1 = pk(d1, d1), N1 = pk(-m1, -m1), D2 = pk(d2, d2), N2 = pk(-m2, -m2);
+    const f2 MG = pk(-8388608.f, -8388608.f);
     const uint8_t* qs = blk + (Q == Q4_K ? 16 : 48) + 32 * j;
     uint32_t q[8];
     const uint4 qa = ld16<SMEM>(qs), qb = ld16<SMEM>(qs + 16);
@@ -125,14 +133,16 @@ __device__ __forceinline__ void dequant64(const uint8_t* row, int k0, float* v) 
       qh[0] = ha.x; qh[1] = ha.y; qh[2] = ha.z; qh[3] = ha.w; qh[4] = hb.x; qh[5] = hb.y; qh[6] = hb.z; qh[7] = hb.w;
     }
 #pragma unroll
-    for (int l = 0; l < 32; ++l) {
-      unsigned lo = byte_of(q, l) & 15u, hi = byte_of(q, l) >> 4;
+    for (int w = 0; w < 8; ++w) {  // weights l = 4w..4w+3 (low nibbles) and 32 + l (high nibbles)
+      uint32_t lo = q[w] & 0x0F0F0F0Fu, hi = (q[w] >> 4) & 0x0F0F0F0Fu;
       if constexpr (Q == Q5_K) {
-        lo += (byte_of(qh, l) >> (2 * j)) & 1u ? 16u : 0u;
-        hi += (byte_of(qh, l) >> (2 * j + 1)) & 1u ? 16u : 0u;
+        lo |= ((qh[w] >> (2 * j)) & 0x01010101u) << 4;
+        hi |= ((qh[w] >> (2 * j + 1)) & 0x01010101u) << 4;
       }
-      v[l] = __fsub_rn(__fmul_rn(d1, (float)lo), m1);
-      v[32 + l] = __fsub_rn(__fmul_rn(d2, (float)hi), m2);
+      v[2 * w] = fma2(D1, add2(pk(byte_magic<0>(lo), byte_magic<1>(lo)), MG), N1);
+      v[2 * w + 1] = fma2(D1, add2(pk(byte_magic<2>(lo), byte_magic<3>(lo)), MG), N1);
+      v[16 + 2 * w] = fma2(D2, add2(pk(byte_magic<0>(hi), byte_magic<1>(hi)), MG), N2);
+      v[16 + 2 * w + 1] = fma2(D2, add2(pk(byte_magic<2>(hi), byte_magic<3>(hi)), MG), N2);
     }
   } else if constexpr (Q == Q6_K) {
     const uint8_t* blk = SMEM ? row : row + (k0 >> 8) * 210;
@@ -144,35 +154,69 @@ __device__ __forceinline__ void dequant64(const uint8_t* row, int k0, float* v) 
     uint32_t dw[1];
     ldg_words_a2<1, SMEM>(blk + 208, dw);
     const float d = h2f((uint16_t)(dw[0] & 0xffffu));
+    const f2 MG = pk(-8388640.f, -8388640.f);  // 2^23 + 32: field q -> q - 32
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int n = nb + u;
 #pragma unroll
-      for (int l = 0; l < 32; ++l) {
-        unsigned b = byte_of(ql, (n & 1) ? l + 32 : l);
-        b = (n & 2) ? (b >> 4) : (b & 15u);
-        const int qv = (int)(b | (((byte_of(qh, l) >> (2 * n)) & 3u) << 4)) - 32;
-        const float s = (float)(int8_t)byte_of(sc, (l >> 4) + 2 * n);
-        v[32 * u + l] = __fmul_rn(__fmul_rn(d, s), (float)qv);
+      for (int w = 0; w < 8; ++w) {  // weights l = 4w..4w+3 of group n
+        const uint32_t b = ql[(n & 1) * 8 + w];
+        const uint32_t qv = (((n & 2) ? (b >> 4) : b) & 0x0F0F0F0Fu) | (((qh[w] >> (2 * n)) << 4) & 0x30303030u);
+        const float ds = __fmul_rn(d, (float)(int8_t)byte_of(sc, (w >> 2) + 2 * n));
+        const f2 DS = pk(ds, ds);
+        v[16 * u + 2 * w] = mul2(DS, add2(pk(byte_magic<0>(qv), byte_magic<1>(qv)), MG));
+        v[16 * u + 2 * w + 1] = mul2(DS, add2(pk(byte_magic<2>(qv), byte_magic<3>(qv)), MG));
+      }
+    }
+  } else if constexpr (Q == TQ2_0) {  // group g = (k0 & 255) >> 6 of a 66-byte block (simd.zig:457-472)
+    const uint8_t* blk = row + (k0 >> 8) * 66;
+    const int g = (k0 & 255) >> 6;
+    uint32_t qw[4], dw[1];
+    ldg_words_a2<4, SMEM>(blk + 16 * g, qw);
+    ldg_words_a2<1, SMEM>(blk + 64, dw);
+    const float d = h2f((uint16_t)(dw[0] & 0xffffu));
+    const f2 D = pk(d, d), MG = pk(-8388609.f, -8388609.f);  // 2^23 + 1: field r -> r - 1
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {  // weights l = 4t..4t+3, repeated at l + 16, l + 32, l + 48
+      const uint32_t r = (qw[t] >> (2 * g)) & 0x03030303u;
+      const f2 a = mul2(D, add2(pk(byte_magic<0>(r), byte_magic<1>(r)), MG));
+      const f2 b = mul2(D, add2(pk(byte_magic<2>(r), byte_magic<3>(r)), MG));
+#pragma unroll
+      for (int rep = 0; rep < 4; ++rep) {
+        v[8 * rep + 2 * t] = a;
+        v[8 * rep + 2 * t + 1] = b;
       }
     }
   } else {  // Q8_0: two 34-byte blocks
+    const f2 MG = pk(-8388736.f, -8388736.f);  // 2^23 + 128: (i8 ^ 0x80) -> i8
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const uint8_t* blk = row + ((k0 >> 5) + u) * 34;
       uint32_t w[9];
       ldg_words_a2<9>(blk, w);
       const float d = h2f((uint16_t)(w[0] & 0xffffu));
+      const f2 D = pk(d, d);
 #pragma unroll
-      for (int l = 0; l < 32; ++l) v[32 * u + l] = __fmul_rn(d, (float)(int8_t)byte_of(w, l + 2));
+      for (int t = 0; t < 8; ++t) {
+        const uint32_t qv = __funnelshift_r(w[t], w[t + 1], 16) ^ 0x80808080u;
+        v[16 * u + 2 * t] = mul2(D, add2(pk(byte_magic<0>(qv), byte_magic<1>(qv)), MG));
+        v[16 * u + 2 * t + 1] = mul2(D, add2(pk(byte_magic<2>(qv), byte_magic<3>(qv)), MG));
+      }
     }
   }
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
+// Packed bf16 pair of (v.x, v.y): v.x in the low half (round to nearest even).
+__device__ __forceinline__ uint32_t cvt_bf16x2(f2 v) {
+  float a, b;
+  unpk(v, a, b);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
 }
+// The f32 values of a packed bf16 pair.
+__device__ __forceinline__ f2 bf16x2_to_f2(uint32_t h) { return pk(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u)); }
+
 
 // Activations f32 [B][K] -> bf16 hi [B][K] (and lo = bf16(x - hi)).
 __global__ void acts_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
@@ -296,7 +340,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
       }
       if (i >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((i / S) - 1) & 1))) { ok = false; break; }
       uint8_t* st = smem + s * C::STAGE;
-      float v[64];
+      f2 v[32];
       if constexpr (TA) {  // this row's super-block sits at raw[j % SR] + r * BOX (out-of-range rows read as zeros)
         dequant64<Q, true>(raw + (jl % C::SR) * C::RAW + r * TmaA<Q>::BOX + (j * Fmt<Q>::bytes - TmaA<Q>::x0(j)),
                            kb * TC_BK, v);
@@ -305,21 +349,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
         dequant64<Q>(wrow, kb * TC_BK, v);
       } else {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = 0.f;
+        for (int i = 0; i < 32; ++i) v[i] = pk(0.f, 0.f);
       }
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        uint4 hv, lv;
-        float h[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) h[e] = __bfloat162float(__float2bfloat16_rn(v[8 * c + e]));
-        hv.x = pack_bf16(h[0], h[1]); hv.y = pack_bf16(h[2], h[3]); hv.z = pack_bf16(h[4], h[5]); hv.w = pack_bf16(h[6], h[7]);
+        uint4 hv;
+        hv.x = cvt_bf16x2(v[4 * c]); hv.y = cvt_bf16x2(v[4 * c + 1]);
+        hv.z = cvt_bf16x2(v[4 * c + 2]); hv.w = cvt_bf16x2(v[4 * c + 3]);
         *reinterpret_cast<uint4*>(st + sw128_off(r, c)) = hv;
-        if constexpr (PASSES == 3) {
-          lv.x = pack_bf16(v[8 * c + 0] - h[0], v[8 * c + 1] - h[1]);
-          lv.y = pack_bf16(v[8 * c + 2] - h[2], v[8 * c + 3] - h[3]);
-          lv.z = pack_bf16(v[8 * c + 4] - h[4], v[8 * c + 5] - h[5]);
-          lv.w = pack_bf16(v[8 * c + 6] - h[6], v[8 * c + 7] - h[7]);
+        if constexpr (PASSES == 3) {  // lo = bf16(v - hi); v - hi is exact in f32
+          uint4 lv;
+          lv.x = cvt_bf16x2(sub2(v[4 * c], bf16x2_to_f2(hv.x)));
+          lv.y = cvt_bf16x2(sub2(v[4 * c + 1], bf16x2_to_f2(hv.y)));
+          lv.z = cvt_bf16x2(sub2(v[4 * c + 2], bf16x2_to_f2(hv.z)));
+          lv.w = cvt_bf16x2(sub2(v[4 * c + 3], bf16x2_to_f2(hv.w)));
           *reinterpret_cast<uint4*>(st + C::A_BYTES + C::B_BYTES + sw128_off(r, c)) = lv;
         }
       }
@@ -458,9 +501,12 @@ template <int Q>
 static cudaError_t launch_gemm_tc_q(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
                                     int k, int nb, bool precise, int ks, cudaStream_t st) {
   // TMA weight staging needs 16-byte row pitches (all K-quant configs with k % 2048 == 0 qualify)
-  const bool ta = (Q != Q8_0) && host_row_bytes_dev<Q>(k) % 16 == 0;
-  if (ta) return launch_gemm_tc_qt<Q, true>(w, xh, xl, out, m, k, nb, precise, ks, st);
-  return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, ks, st);
+  if constexpr (Q == Q8_0 || Q == TQ2_0) {  // blocks off 16-byte boundaries: producers read global memory
+    return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, ks, st);
+  } else {
+    if (host_row_bytes_dev<Q>(k) % 16 == 0) return launch_gemm_tc_qt<Q, true>(w, xh, xl, out, m, k, nb, precise, ks, st);
+    return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, ks, st);
+  }
 }
 
 // out[i] = sum over splits z of part[z][i], in split order (deterministic).
@@ -507,6 +553,7 @@ cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, 
     case Q5_K: e = launch_gemm_tc_q<Q5_K>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
     case Q6_K: e = launch_gemm_tc_q<Q6_K>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
     case Q8_0: e = launch_gemm_tc_q<Q8_0>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
+    case TQ2_0: e = launch_gemm_tc_q<TQ2_0>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess || ks == 1) return e;

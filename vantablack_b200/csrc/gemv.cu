@@ -1,5 +1,5 @@
-// gemv.cu -- SIMT decode GEMV y[m] = W[m,k] . x[k] for GGUF Q5_K / Q8_0
-// weights, Q6_K rows that are not 16-byte multiples, and the Q8_0 x Q8_0
+// gemv.cu -- SIMT decode GEMV y[m] = W[m,k] . x[k] for GGUF Q5_K / Q8_0 /
+// TQ2_0 weights, Q6_K rows that are not 16-byte multiples, and the Q8_0 x Q8_0
 // path, with f32 activations (the reference's matmul_q*_* in
 // src/kernels/simd.zig:159-434, dispatched by forward.zig:552-627).  Q4_K and
 // TMA-compatible Q6_K run on the integer tensor cores (gemv_mma.cu,
@@ -33,6 +33,7 @@ template <int Q> struct GemvCfg;
 template <> struct GemvCfg<Q5_K> { static constexpr int CH = 8; };
 template <> struct GemvCfg<Q6_K> { static constexpr int CH = 8; };
 template <> struct GemvCfg<Q8_0> { static constexpr int CH = 32; };
+template <> struct GemvCfg<TQ2_0> { static constexpr int CH = 8; };
 
 template <int Q>
 struct Slot {
@@ -188,6 +189,39 @@ __device__ __forceinline__ float lane_dot_q6k(const uint8_t* blk, int j, const X
                sc2 * hsum(add2(acc[2][0], acc[2][1]))) + sc3 * hsum(add2(acc[3][0], acc[3][1])));
 }
 
+// TQ2_0 (simd.zig:436-498, the reference's layout): lane -> block b = lane>>2,
+// group j = lane&3 (weights 64j..64j+63).  Weight 64j + l takes the 2-bit field
+// at bits 2j of qs[16j + l % 16], so weights l, l+16, l+32, l+48 of the group
+// share one value: the lane folds its 64 activations into 16 sums.
+__device__ __forceinline__ void load_x_tq2(const float* x, int col0, XSlice& xs) {
+  float4 a[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = ldx4(x + col0 + 4 * i);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // fold l, l+16, l+32, l+48 (l = 4i..4i+3)
+    const float4 p = a[i], q = a[4 + i], r = a[8 + i], s = a[12 + i];
+    xs.v[2 * i] = pk((p.x + q.x) + (r.x + s.x), (p.y + q.y) + (r.y + s.y));
+    xs.v[2 * i + 1] = pk((p.z + q.z) + (r.z + s.z), (p.w + q.w) + (r.w + s.w));
+  }
+  xs.s0 = xs.s1 = 0.f;
+}
+
+__device__ __forceinline__ float lane_dot_tq2(const uint8_t* blk, int j, const XSlice& xs) {
+  uint32_t q[4], dw[1];
+  lds_words_a2<4>(blk + 16 * j, q);
+  lds_words_a2<1>(blk + 64, dw);
+  const float d = h2f((uint16_t)(dw[0] & 0xffffu));
+  const f2 mg = pk(-8388609.f, -8388609.f);  // 2^23 + 1: raw field -> raw - 1
+  f2 a0 = pk(0.f, 0.f), a1 = a0;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint32_t r = (q[t] >> (2 * j)) & 0x03030303u;
+    a0 = fma2(add2(pk(byte_magic<0>(r), byte_magic<1>(r)), mg), xs.v[2 * t], a0);
+    a1 = fma2(add2(pk(byte_magic<2>(r), byte_magic<3>(r)), mg), xs.v[2 * t + 1], a1);
+  }
+  return d * hsum(add2(a0, a1));
+}
+
 // Q8_0 (simd.zig:159-190): lane -> one 32-weight block.
 __device__ __forceinline__ void load_x_q80(const float* x, int col0, XSlice& xs) {
 #pragma unroll
@@ -316,6 +350,7 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
           xqs.d = __ldg(dx + b0 + bl);
         } else if constexpr (Q == Q8_0) load_x_q80(x, (b0 + bl) * 32, xs);
         else if constexpr (Q == Q6_K) load_x_q6k(x, (b0 + bl) * 256, j, xs);
+        else if constexpr (Q == TQ2_0) load_x_tq2(x, (b0 + bl) * 256 + 64 * j, xs);
         else load_x_kq(x, (b0 + bl) * 256 + 64 * j, xs);
       }
       x_chunk = c;
@@ -336,6 +371,7 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
         float v;
         if constexpr (Q == Q5_K) v = lane_dot_q5k(blk, j, xs);
         else if constexpr (Q == Q6_K) v = lane_dot_q6k(blk, j, xs);
+        else if constexpr (Q == TQ2_0) v = lane_dot_tq2(blk, j, xs);
         else if constexpr (XQ) v = lane_dot_q80_i8(blk, xqs);
         else v = lane_dot_q80(blk, xs);
         acc[r] += v;
@@ -389,6 +425,7 @@ cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, i
       if (q6k_mma_ok(w, k)) return launch_gemv_q6k_mma(w, x, y, m, k, st, pdl, accumulate);
       return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
     case Q8_0: return launch_gemv_t<Q8_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
+    case TQ2_0: return launch_gemv_t<TQ2_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -115,16 +115,20 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Raise this rank's flag to the next epoch in every peer's block (one thread;
+// called after griddepcontrol.wait, i.e. once this rank's partial is complete).
+__device__ __forceinline__ void tp_raise_flag(const PeerPtrs& peers, int world, int me, long long flag_off) {
+  unsigned* mine = reinterpret_cast<unsigned*>(peers.p[me] + flag_off);
+  const unsigned e = mine[TP_MAX] + 1;  // epoch: one per all-reduce, identical on every rank
+  mine[TP_MAX] = e;
+  __threadfence_system();
+  for (int r = 0; r < world; ++r)
+    if (r != me) st_release_sys(reinterpret_cast<unsigned*>(peers.p[r] + flag_off) + me, e);
+}
+
 __global__ void tp_signal_kernel(PeerPtrs peers, int world, int me, long long flag_off) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the partial of this rank is complete
-  if (threadIdx.x == 0) {
-    unsigned* mine = reinterpret_cast<unsigned*>(peers.p[me] + flag_off);
-    const unsigned e = mine[TP_MAX] + 1;  // epoch: one per all-reduce, identical on every rank
-    mine[TP_MAX] = e;
-    __threadfence_system();
-    for (int r = 0; r < world; ++r)
-      if (r != me) st_release_sys(reinterpret_cast<unsigned*>(peers.p[r] + flag_off) + me, e);
-  }
+  if (threadIdx.x == 0) tp_raise_flag(peers, world, me, flag_off);
   asm volatile("griddepcontrol.launch_dependents;");
 }
 
@@ -133,9 +137,10 @@ __global__ void tp_signal_kernel(PeerPtrs peers, int world, int me, long long fl
 // head_dim % 8 == 0, so the float4 loop below covers every element.
 __global__ void __launch_bounds__(1024) rmsnorm_tp_kernel(float* __restrict__ x, PeerPtrs peers, int world, int me, long long slot_off,
                                   long long flag_off, const float* __restrict__ w, float* __restrict__ out, int n,
-                                  float eps) {
+                                  float eps, int signal) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
+    if (signal) tp_raise_flag(peers, world, me, flag_off);  // single-CTA launch: publish, then wait
     const unsigned* flags = reinterpret_cast<const unsigned*>(peers.p[me] + flag_off);
     const unsigned e = flags[TP_MAX];
     for (int r = 0; r < world; ++r) {
@@ -783,6 +788,7 @@ struct VtbCudaState {
   int nsplit;
   float* logits_local;      // [rows][V] LM-head slice under tensor parallelism
   bool pending = false;     // tmp holds an all-reduced partial still to be added to x
+  bool sig_pending = false; // peer memory: this rank's partial is complete but its flag not yet raised
   bool decode_rows = false; // staged rows are distinct sequences (decode), not one prompt (prefill)
   int max_pos = 0;          // largest staged position (sizes prefill attention grids)
   bool one_seq = false;     // every staged row belongs to one sequence
@@ -1182,6 +1188,7 @@ static int stage_rows(VtbCudaState* s, int rows, const int32_t* tok, const int32
   }
   s->rows = rows;
   s->pending = false;
+  s->sig_pending = false;
   s->max_pos = 0;
   for (int r = 0; r < rows; ++r) s->max_pos = std::max(s->max_pos, (int)pos[r]);
   s->one_seq = true;
@@ -1221,9 +1228,18 @@ static cudaError_t enqueue_norm(VtbCudaState* s, const float* w, int r0, int n) 
   const VtbCudaLlamaConfig& c = s->m->c;
   if (s->pending && s->p2p) {  // the all-reduce itself happens here, over peer memory
     s->pending = false;
+    // One row (batch-1 decode, the last prefill row): the single CTA raises this
+    // rank's flag itself.  Several rows: a one-thread kernel raises it first.
+    const int sig = s->sig_pending && n == 1;
+    if (s->sig_pending && !sig) {
+      cudaError_t e = pdl_launch(tp_signal_kernel, dim3(1), dim3(32), 0, s->st, s->peers, s->m->tp->world,
+                                 s->m->tp->rank, s->flag_off);
+      if (e) return e;
+    }
+    s->sig_pending = false;
     const long long slot_off = (long long)(s->par ^ 1) * s->max_rows * c.dim + (long long)r0 * c.dim;
     return pdl_launch(rmsnorm_tp_kernel, dim3(n), dim3(1024), 0, s->st, s->x + (size_t)r0 * c.dim, s->peers,
-                      s->m->tp->world, s->m->tp->rank, slot_off, s->flag_off, w, s->xb, c.dim, c.rms_eps);
+                      s->m->tp->world, s->m->tp->rank, slot_off, s->flag_off, w, s->xb, c.dim, c.rms_eps, sig);
   }
   const float* res = s->pending ? s->tmp + (size_t)r0 * c.dim : nullptr;
   s->pending = false;
@@ -1237,12 +1253,11 @@ static float* partial_out(VtbCudaState* s) {
 }
 
 static cudaError_t allreduce_tmp(VtbCudaState* s, size_t n) {
-  if (s->p2p) {  // publish this rank's partial; the next RMSNorm sums the ranks' slots
-    cudaError_t e = pdl_launch(tp_signal_kernel, dim3(1), dim3(32), 0, s->st, s->peers, s->m->tp->world,
-                               s->m->tp->rank, s->flag_off);
+  if (s->p2p) {  // the partial is published (flag raised) and summed by the next RMSNorm
     s->par ^= 1;
     s->pending = true;
-    return e;
+    s->sig_pending = true;
+    return cudaSuccess;
   }
   const ncclResult_t r = ncclAllReduce(s->tmp, s->tmp, n, ncclFloat32, ncclSum, s->m->tp->comm, s->st);
   if (r != ncclSuccess) {

@@ -34,6 +34,10 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* blk, int e) {
     unsigned q = (s & 1) ? (qs[l] >> 4) : (qs[l] & 15u);
     if constexpr (Q == Q5_K) q += (blk[16 + l] >> s) & 1u ? 16u : 0u;
     return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
+  } else if constexpr (Q == TQ2_0) {  // dequantBlockTQ2_0, simd.zig:457-472
+    const int g = e >> 6, l = e & 63;
+    const unsigned raw = (blk[16 * g + (l & 15)] >> (2 * g)) & 3u;
+    return __fmul_rn(h2f(ld16(blk + 64)), (float)((int)raw - 1));
   } else {  // Q6_K
     const float d = h2f(ld16(blk + 208));
     const int half = e >> 7, r = e & 127, n = r >> 5, l = r & 31;
@@ -116,6 +120,7 @@ cudaError_t launch_dequant(int q, const void* w, float* out, long long n, cudaSt
     case Q4_K: dequant_kernel<Q4_K><<<g, 256, 0, st>>>(p, out, n); break;
     case Q5_K: dequant_kernel<Q5_K><<<g, 256, 0, st>>>(p, out, n); break;
     case Q6_K: dequant_kernel<Q6_K><<<g, 256, 0, st>>>(p, out, n); break;
+    case TQ2_0: dequant_kernel<TQ2_0><<<g, 256, 0, st>>>(p, out, n); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -130,6 +135,7 @@ cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* ou
     case Q4_K: embed_kernel<Q4_K><<<grid, 256, 0, st>>>(p, ids, out, dim, n_tok); break;
     case Q5_K: embed_kernel<Q5_K><<<grid, 256, 0, st>>>(p, ids, out, dim, n_tok); break;
     case Q6_K: embed_kernel<Q6_K><<<grid, 256, 0, st>>>(p, ids, out, dim, n_tok); break;
+    case TQ2_0: embed_kernel<TQ2_0><<<grid, 256, 0, st>>>(p, ids, out, dim, n_tok); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

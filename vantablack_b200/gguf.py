@@ -99,7 +99,7 @@ class GgufFile:
 # u64 offset relative to the data section); zero padding to the alignment;
 # tensor data, each tensor starting on an aligned offset.
 _META_FMT = {"u32": (4, "<I"), "i32": (5, "<i"), "f32": (6, "<f"), "u64": (10, "<Q"), "f64": (12, "<d")}
-_BLOCK = {0: (1, 4), 8: (32, 34), 12: (256, 144), 13: (256, 176), 14: (256, 210)}  # type: (elems, bytes)
+_BLOCK = {0: (1, 4), 8: (32, 34), 12: (256, 144), 13: (256, 176), 14: (256, 210), 32: (256, 66)}  # type: (elems, bytes)
 
 
 def _gstr(s: str) -> bytes:

@@ -11,6 +11,9 @@ Distributions (per block format):
 * Q6_K (210 B / 256): 128 B low nibbles and 64 B high 2-bit fields uniform
   u8; 16 i8 sub-block scales uniform in [-32, 31]; f16 d = f16(|N(0,1)| * 2^-9).
 * Q8_0 (34 B / 32): f16 d = f16(|N(0,1)| * 2^-8); 32 i8 uniform in [-127, 127].
+* TQ2_0 (66 B / 256, id 32 as in the reference's parser): 64 bytes of 2-bit
+  fields, each field uniform in {0, 1, 2} (ternary -1/0/+1); f16 d =
+  f16(|N(0,1)| * 2^-6).
 * activations f32 ~ N(0, 1); norm weights 1 + 0.02 * N(0, 1).
 
 Block layouts follow the ggml formats restated in the reference at
@@ -20,11 +23,11 @@ from __future__ import annotations
 
 import numpy as np
 
-F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
+F32, Q8_0, Q4_K, Q5_K, Q6_K, TQ2_0 = 0, 8, 12, 13, 14, 32
 
-BLOCK_BYTES = {Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
-BLOCK_ELEMS = {Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
-NAMES = {Q8_0: "q8_0", Q4_K: "q4_k", Q5_K: "q5_k", Q6_K: "q6_k", F32: "f32"}
+BLOCK_BYTES = {Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210, TQ2_0: 66}
+BLOCK_ELEMS = {Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256, TQ2_0: 256}
+NAMES = {Q8_0: "q8_0", Q4_K: "q4_k", Q5_K: "q5_k", Q6_K: "q6_k", TQ2_0: "tq2_0", F32: "f32"}
 
 
 def row_bytes(quant: int, k: int) -> int:
@@ -56,6 +59,10 @@ def quant_tensor(rng: np.random.Generator, quant: int, m: int, k: int) -> np.nda
     elif quant == Q8_0:
         blocks[:, 0:2] = _f16_bytes(rng, nb, 2.0 ** -8)
         blocks[:, 2:34] = rng.integers(-127, 128, size=(nb, 32), dtype=np.int8).view(np.uint8)
+    elif quant == TQ2_0:
+        f = rng.integers(0, 3, size=(nb, 64, 4), dtype=np.uint8)
+        blocks[:, 0:64] = f[..., 0] | (f[..., 1] << 2) | (f[..., 2] << 4) | (f[..., 3] << 6)
+        blocks[:, 64:66] = _f16_bytes(rng, nb, 2.0 ** -6)
     else:
         raise ValueError(f"unsupported quant {quant}")
     return blocks.reshape(-1)
