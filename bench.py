@@ -729,6 +729,12 @@ def run_profile_case(case: str) -> None:
         acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
         for _ in range(2):
             ops.gemm(S.Q6_K, w, acts, m, k, precise=True)
+    elif case == "gemm_b32_q4k":  # batch decode shape: Q4_K gate|up 28672 x 4096, B = 32, precise mode, two launches
+        m, k, b = 28672, 4096, 32
+        w = torch.from_numpy(S.quant_tensor(rng, Q4_K, m, k)).cuda()
+        acts = torch.from_numpy(S.activations(rng, b, k)).cuda()
+        for _ in range(2):
+            ops.gemm(Q4_K, w, acts, m, k, precise=True)
     elif case == "decode8b_b32":  # Llama-3-8B, 32 sequences: 3 decode steps of one token each
         from vantablack_b200.model import LLAMA3_8B, Context, CudaModel, CudaState, HostWeights
         ctx = Context(0)
@@ -751,7 +757,7 @@ def run_profile_case(case: str) -> None:
     print("ok", case)
 
 
-PROFILE_CASES = ["gemv", "gemv_chain", "gemv_q6k", "gemm", "gemm_precise", "gemm_b32", "decode", "decode8b",
+PROFILE_CASES = ["gemv", "gemv_chain", "gemv_q6k", "gemm", "gemm_precise", "gemm_b32", "gemm_b32_q4k", "decode", "decode8b",
                  "decode8b_b32"]
 
 
