@@ -240,6 +240,14 @@ VtbCudaModel *vtb_cuda_model_create(VtbCudaCtx *ctx, const VtbCudaLlamaConfig *c
                                     int32_t q_output);
 void vtb_cuda_model_destroy(VtbCudaModel *m);
 size_t vtb_cuda_model_weight_bytes(VtbCudaModel *m);
+/* Dynamic activation quantization for Q8_0 weights: with on = 1, every Q8_0
+ * projection of states created afterwards quantizes its activation row per
+ * 32-block to Q8_0 (d = max|x|/127, round half away from zero) and runs the
+ * Q8_0 x Q8_0 path -- exact int32 block dots (dot_i8, simd.zig:31-62) scaled
+ * by d_w * d_x -- instead of the f32-activation matmul_q8_0 of matmulRuntime
+ * (forward.zig:552-627).  Prefill rows of such projections run one row at a
+ * time.  Other quant types are unaffected.  Default off. */
+int vtb_cuda_model_set_q8_activations(VtbCudaModel *m, int on);
 
 /* Per-session device state (forward.zig State :33-113 + KvCache kv_cache.zig:20-73):
  * n_seqs independent sequences decoded together (batch decode), and up to

@@ -68,6 +68,7 @@ def _load():
         "vtbo_argmax": (_sz, [_f32p, _sz]),
         "vtbo_model_create": (C.c_void_p, [C.c_void_p, C.c_void_p, _u8p, C.c_int, _f32p, _u8p, C.c_int]),
         "vtbo_model_destroy": (None, [C.c_void_p]),
+        "vtbo_model_set_q8_activations": (None, [C.c_void_p, C.c_int]),
         "vtbo_model_reset": (None, [C.c_void_p]),
         "vtbo_model_pos": (C.c_int64, [C.c_void_p]),
         "vtbo_step": (C.c_int, [C.c_void_p, C.c_uint32, _f32p]),
@@ -248,9 +249,10 @@ class _Layer(C.Structure):
 class Model:
     """The reference's CPU forward (forward.zig step + prefill.zig prefillCpu)
     over host weights held by a ``vantablack_b200.model.HostWeights``:
-    ``cfg`` plus per-layer dicts of (quant, ndarray)."""
+    ``cfg`` plus per-layer dicts of (quant, ndarray).  ``q8_activations``:
+    Q8_0 projections take Q8_0-quantized activations (the Q8_0 x Q8_0 path)."""
 
-    def __init__(self, weights):
+    def __init__(self, weights, q8_activations: bool = False):
         cfg = weights.cfg
         self.cfg = cfg
         self._keep = weights
@@ -269,6 +271,8 @@ class Model:
         qo, out = weights.output
         self._h = lib.vtbo_model_create(C.byref(c), C.cast(layers, C.c_void_p), _p(emb, _u8p), qe,
                                         _p(weights.output_norm, _f32p), _p(out, _u8p), qo)
+        if q8_activations:
+            lib.vtbo_model_set_q8_activations(self._h, 1)
 
     def __del__(self):
         h = getattr(self, "_h", None)

@@ -17,6 +17,7 @@
 #include <stdatomic.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #define LANES 8 /* simd.zig:10 lane_width */
 
@@ -339,7 +340,8 @@ static void matmul_q8_0_q8_0_rows(float *out, const uint8_t *w, const int8_t *xq
 }
 
 /* ---------------- thread pool: pool.zig:44-114 ----------------
- * Persistent workers spin on an epoch counter (then yield), the caller runs
+ * Persistent workers spin on an epoch counter (then yield, then sleep in 50 us
+ * steps once idle for milliseconds), the caller runs
  * worker 0, and a matmul stripes rows as chunk = ceil(m / n_workers)
  * (forward.zig:534-550, prefill.zig:348-378). */
 typedef void (*job_fn)(int wid, int nw, void *ctx);
@@ -359,9 +361,17 @@ static void *worker_loop(void *arg) {
     unsigned long seen = g_pool.start_epoch;
     for (;;) {
         unsigned long e;
-        int spins = 0;
+        int spins = 0, yields = 0;
         while ((e = atomic_load_explicit(&g_pool.epoch, memory_order_acquire)) == seen) {
-            if (++spins > 4096) { sched_yield(); spins = 0; }
+            if (++spins > 4096) {
+                spins = 0;
+                if (++yields < 2048) {
+                    sched_yield();
+                } else {  /* idle for milliseconds: sleep, so an idle pool leaves the cores to other work */
+                    struct timespec ts = {0, 50000};
+                    nanosleep(&ts, NULL);
+                }
+            }
         }
         seen = e;
         if (atomic_load(&g_pool.shutdown)) return NULL;
@@ -598,7 +608,25 @@ struct vtbo_model {
     int64_t pos;
     /* forward.zig State, :33-113 */
     float *x, *xb, *xb2, *q, *kc, *vc, *scores, *attn_out, *gate, *up, *ffn_out;
+    int q8_act; /* Q8_0 projections take Q8_0-quantized activations (int32 block dots) */
 };
+
+/* matmulRuntime for one row (mm) or B rows (mmb, out[B][rows]).  With the
+ * model's q8_act option a Q8_0 projection runs the Q8_0 x Q8_0 path instead
+ * (activations quantized per 32-block, dot_i8 block dots, simd.zig:31-62). */
+static int mm(const vtbo_model *m, int q, float *out, const uint8_t *w, const float *x, size_t rows, size_t k) {
+    if (m->q8_act && q == VTBO_Q8_0) return vtbo_matmul_q8_0_q8_0(out, w, x, rows, k);
+    return vtbo_matmul(q, out, w, x, rows, k);
+}
+static int mmb(const vtbo_model *m, int q, float *out, const uint8_t *w, const float *acts, size_t rows, size_t k,
+               size_t B) {
+    if (!(m->q8_act && q == VTBO_Q8_0)) return vtbo_matmul_batched(q, out, w, acts, rows, k, B);
+    for (size_t b = 0; b < B; b++)
+        if (vtbo_matmul_q8_0_q8_0(out + b * rows, w, acts + b * k, rows, k)) return -1;
+    return 0;
+}
+
+void vtbo_model_set_q8_activations(vtbo_model *m, int on) { m->q8_act = on != 0; }
 
 vtbo_model *vtbo_model_create(const vtbo_config *c, const vtbo_layer *layers,
                               const uint8_t *token_embd, int q_token_embd,
@@ -697,22 +725,22 @@ static int layer_step(vtbo_model *m, size_t l) {
     size_t d = (size_t)c->dim, kvd = kv_dim(c), f = (size_t)c->ffn_dim, hd = (size_t)c->head_dim;
     memcpy(m->xb, m->x, d * 4);
     vtbo_rms_norm(m->xb, L->attn_norm, d, c->rms_eps);
-    if (vtbo_matmul(L->q_attn_q, m->q, L->attn_q, m->xb, d, d)) return -1;
-    if (vtbo_matmul(L->q_attn_k, m->kc, L->attn_k, m->xb, kvd, d)) return -1;
-    if (vtbo_matmul(L->q_attn_v, m->vc, L->attn_v, m->xb, kvd, d)) return -1;
+    if (mm(m, L->q_attn_q, m->q, L->attn_q, m->xb, d, d)) return -1;
+    if (mm(m, L->q_attn_k, m->kc, L->attn_k, m->xb, kvd, d)) return -1;
+    if (mm(m, L->q_attn_v, m->vc, L->attn_v, m->xb, kvd, d)) return -1;
     for (int64_t h = 0; h < c->n_heads; h++) vtbo_rope(m->q + h * (int64_t)hd, hd, (size_t)m->pos, c->rope_base);
     for (int64_t h = 0; h < c->n_kv_heads; h++) vtbo_rope(m->kc + h * (int64_t)hd, hd, (size_t)m->pos, c->rope_base);
     memcpy(layer_k(m, l) + (size_t)m->pos * kvd, m->kc, kvd * 4);
     memcpy(layer_v(m, l) + (size_t)m->pos * kvd, m->vc, kvd * 4);
     attention_one(m, l, m->q, m->attn_out, m->scores, m->pos);
-    if (vtbo_matmul(L->q_attn_o, m->xb2, L->attn_o, m->attn_out, d, d)) return -1;
+    if (mm(m, L->q_attn_o, m->xb2, L->attn_o, m->attn_out, d, d)) return -1;
     vtbo_add_into(m->x, m->xb2, d);
     memcpy(m->xb, m->x, d * 4);
     vtbo_rms_norm(m->xb, L->ffn_norm, d, c->rms_eps);
-    if (vtbo_matmul(L->q_ffn_gate, m->gate, L->ffn_gate, m->xb, f, d)) return -1;
-    if (vtbo_matmul(L->q_ffn_up, m->up, L->ffn_up, m->xb, f, d)) return -1;
+    if (mm(m, L->q_ffn_gate, m->gate, L->ffn_gate, m->xb, f, d)) return -1;
+    if (mm(m, L->q_ffn_up, m->up, L->ffn_up, m->xb, f, d)) return -1;
     vtbo_swiglu(m->gate, m->up, f);
-    if (vtbo_matmul(L->q_ffn_down, m->ffn_out, L->ffn_down, m->gate, d, f)) return -1;
+    if (mm(m, L->q_ffn_down, m->ffn_out, L->ffn_down, m->gate, d, f)) return -1;
     vtbo_add_into(m->x, m->ffn_out, d);
     return 0;
 }
@@ -728,7 +756,7 @@ int vtbo_step(vtbo_model *m, uint32_t token, float *logits) {
         if (layer_step(m, l)) return -1;
     m->pos += 1;
     vtbo_rms_norm(m->x, m->output_norm, (size_t)c->dim, c->rms_eps);
-    return vtbo_matmul(m->q_out, logits, m->output_w, m->x, (size_t)c->vocab_size, (size_t)c->dim);
+    return mm(m, m->q_out, logits, m->output_w, m->x, (size_t)c->vocab_size, (size_t)c->dim);
 }
 
 /* prefillCpu / prefillLayer, prefill.zig:111-232 */
@@ -754,9 +782,9 @@ int vtbo_prefill(vtbo_model *m, const uint32_t *tokens, size_t B, float *logits)
             memcpy(xb + b * d, x + b * d, d * 4);
             vtbo_rms_norm(xb + b * d, L->attn_norm, d, c->rms_eps);
         }
-        if (vtbo_matmul_batched(L->q_attn_q, q, L->attn_q, xb, d, d, B) ||
-            vtbo_matmul_batched(L->q_attn_k, kc, L->attn_k, xb, kvd, d, B) ||
-            vtbo_matmul_batched(L->q_attn_v, vc, L->attn_v, xb, kvd, d, B)) { rc = -1; goto done; }
+        if (mmb(m, L->q_attn_q, q, L->attn_q, xb, d, d, B) ||
+            mmb(m, L->q_attn_k, kc, L->attn_k, xb, kvd, d, B) ||
+            mmb(m, L->q_attn_v, vc, L->attn_v, xb, kvd, d, B)) { rc = -1; goto done; }
         for (size_t b = 0; b < B; b++) {
             size_t pb = (size_t)m->pos + b;
             for (int64_t h = 0; h < c->n_heads; h++) vtbo_rope(q + b * qd + (size_t)h * hd, hd, pb, c->rope_base);
@@ -766,23 +794,23 @@ int vtbo_prefill(vtbo_model *m, const uint32_t *tokens, size_t B, float *logits)
         }
         for (size_t b = 0; b < B; b++)
             attention_one(m, l, q + b * qd, ao + b * d, sc, m->pos + (int64_t)b);
-        if (vtbo_matmul_batched(L->q_attn_o, xb2, L->attn_o, ao, d, d, B)) { rc = -1; goto done; }
+        if (mmb(m, L->q_attn_o, xb2, L->attn_o, ao, d, d, B)) { rc = -1; goto done; }
         for (size_t b = 0; b < B; b++) vtbo_add_into(x + b * d, xb2 + b * d, d);
         for (size_t b = 0; b < B; b++) {
             memcpy(xb + b * d, x + b * d, d * 4);
             vtbo_rms_norm(xb + b * d, L->ffn_norm, d, c->rms_eps);
         }
-        if (vtbo_matmul_batched(L->q_ffn_gate, g, L->ffn_gate, xb, f, d, B) ||
-            vtbo_matmul_batched(L->q_ffn_up, u, L->ffn_up, xb, f, d, B)) { rc = -1; goto done; }
+        if (mmb(m, L->q_ffn_gate, g, L->ffn_gate, xb, f, d, B) ||
+            mmb(m, L->q_ffn_up, u, L->ffn_up, xb, f, d, B)) { rc = -1; goto done; }
         for (size_t b = 0; b < B; b++) vtbo_swiglu(g + b * f, u + b * f, f);
-        if (vtbo_matmul_batched(L->q_ffn_down, fo, L->ffn_down, g, d, f, B)) { rc = -1; goto done; }
+        if (mmb(m, L->q_ffn_down, fo, L->ffn_down, g, d, f, B)) { rc = -1; goto done; }
         for (size_t b = 0; b < B; b++) vtbo_add_into(x + b * d, fo + b * d, d);
     }
     m->pos += (int64_t)B;
     {
         float *last = x + (B - 1) * d;
         vtbo_rms_norm(last, m->output_norm, d, c->rms_eps);
-        rc = vtbo_matmul_batched(m->q_out, logits, m->output_w, last, (size_t)c->vocab_size, d, 1);
+        rc = mmb(m, m->q_out, logits, m->output_w, last, (size_t)c->vocab_size, d, 1);
     }
 done:
     free(x); free(xb); free(xb2); free(q); free(kc); free(vc); free(ao); free(g); free(u); free(fo); free(sc);

@@ -105,6 +105,8 @@ vtbo_model *vtbo_model_create(const vtbo_config *c, const vtbo_layer *layers,
                               const float *output_norm,
                               const uint8_t *output_w, int q_output);
 void vtbo_model_destroy(vtbo_model *m);
+/* Q8_0 projections take Q8_0-quantized activations (the Q8_0 x Q8_0 path). */
+void vtbo_model_set_q8_activations(vtbo_model *m, int on);
 void vtbo_model_reset(vtbo_model *m);
 int64_t vtbo_model_pos(const vtbo_model *m);
 /* One token through stepWithBackend + CpuBackend; logits written to `logits`. */

@@ -126,3 +126,24 @@ def test_q8_0_q5_k_and_tq2_0_models(small):
         ids_p, lgp = CudaState(CudaModel(ctx, hw), 1, max_rows=16).generate_greedy(list(range(5, 21)), 4)
         ids_pr, lpr = O.Model(hw).generate_greedy(list(range(5, 21)), 4, use_prefill=True)
         assert ids_p == ids_pr and rel(lgp, lpr) <= LTOL, S.NAMES[q]
+
+
+def test_q8_0_model_with_q8_0_activations(small):
+    """Dynamic activation quantization (the Q8_0 x Q8_0 path on every Q8_0
+    projection, vtb_cuda_model_set_q8_activations): greedy ids and logits equal
+    the oracle run with the same option, in decode and in prefill."""
+    from vantablack_b200.model import CudaModel, CudaState
+    w, ctx, _ = small
+    qs = {n: S.Q8_0 for n in ("attn_q", "attn_k", "attn_v", "attn_o", "ffn_gate", "ffn_up", "ffn_down")}
+    hw = HostWeights(SMALL, seed=19, quants=dict(qs, token_embd=S.Q8_0, output=S.Q8_0))
+    ids_ref, lr = O.Model(hw, q8_activations=True).generate_greedy([5, 6, 7], 8, use_prefill=False)
+    m = CudaModel(ctx, hw, q8_activations=True)
+    ids, lg = CudaState(m, 1).generate_greedy([5, 6, 7], 8, use_prefill=False)
+    assert ids == ids_ref and rel(lg, lr) <= LTOL
+    prompt = list(range(5, 21))
+    ids_p, lgp = CudaState(m, 1, max_rows=16).generate_greedy(prompt, 4)
+    ids_pr, lpr = O.Model(hw, q8_activations=True).generate_greedy(prompt, 4, use_prefill=True)
+    assert ids_p == ids_pr and rel(lgp, lpr) <= LTOL
+    # the option changes the arithmetic: the f32-activation oracle differs
+    _, lf = O.Model(hw).generate_greedy([5, 6, 7], 8, use_prefill=False)
+    assert rel(lf, lr) > 0

@@ -59,6 +59,7 @@ SIGNATURES = {
     "vtb_cuda_model_create": (_vp, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _i32]),
     "vtb_cuda_model_destroy": (None, [_vp]),
     "vtb_cuda_model_weight_bytes": (_sz, [_vp]),
+    "vtb_cuda_model_set_q8_activations": (_int, [_vp, _int]),
     "vtb_cuda_state_create": (_vp, [_vp, _i32, _i32]),
     "vtb_cuda_state_destroy": (None, [_vp]),
     "vtb_cuda_state_reset": (_int, [_vp]),

@@ -15,7 +15,7 @@ cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, i
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                 int accumulate, const float* norm_w, float eps, float* swi);
 cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* dx, float* y, int m, int k,
-                                  cudaStream_t st, bool pdl);
+                                  cudaStream_t st, bool pdl, int accumulate = 0);
 cudaError_t launch_dequant(int q, const void* w, float* out, long long n, cudaStream_t st);
 cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* out, int dim, int n_tok,
                          cudaStream_t st);

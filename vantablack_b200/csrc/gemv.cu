@@ -431,8 +431,8 @@ cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, i
 }
 
 cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* dx, float* y, int m, int k,
-                                  cudaStream_t st, bool pdl) {
-  return launch_gemv_t<Q8_0, 4, 4, 4, true>(w, xq, dx, y, m, k, st, pdl);
+                                  cudaStream_t st, bool pdl, int accumulate) {
+  return launch_gemv_t<Q8_0, 4, 4, 4, true>(w, xq, dx, y, m, k, st, pdl, accumulate);
 }
 
 }  // namespace vtb

@@ -48,6 +48,10 @@ __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ t, l
   asm volatile("griddepcontrol.launch_dependents;");
 }
 
+cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* dx, float* y, int m, int k,
+                                  cudaStream_t st, bool pdl, int accumulate);
+cudaError_t launch_quantize_q8_0(const float* x, int8_t* qs, float* d, int nblocks, cudaStream_t st);
+
 static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
                             int accumulate) {
   if (q == Q4_K) return launch_gemv_q4k_mma(w, x, y, m, k, st, true, accumulate, nullptr, 0.f, nullptr);
@@ -768,6 +772,9 @@ struct VtbCudaModel {
   VtbCudaTp* tp = nullptr;
   VtbCudaTpShard sh;
   int H, KV, F, V;  // local q heads, kv heads, ffn rows, vocab rows
+  // Q8_0 projections take Q8_0-quantized activations (vtb_cuda_model_set_q8_activations);
+  // copied into each state at its creation.
+  bool q8_act = false;
 };
 
 struct VtbCudaState {
@@ -776,7 +783,8 @@ struct VtbCudaState {
   cudaStream_t st;
   int n_seqs, max_rows;
   float *x, *xb, *qkv, *att, *gu, *h, *logits, *part, *tmp;
-  void* ws;  // GEMM activation workspace (bf16 hi + lo)
+  void* ws;  // GEMM activation workspace (bf16 hi + lo); the Q8_0 activation quants of the Q8_0 x Q8_0 path
+  bool q8_act = false;  // the model's option when the state was created
   float* gsplit = nullptr;  // split-K partial tiles of small-batch GEMMs
   size_t gsplit_elems = 0;
   int32_t *tok, *seq, *pos, *amax;
@@ -1060,6 +1068,12 @@ void vtb_cuda_model_destroy(VtbCudaModel* m) {
 
 size_t vtb_cuda_model_weight_bytes(VtbCudaModel* m) { return m ? m->blob_bytes : 0; }
 
+int vtb_cuda_model_set_q8_activations(VtbCudaModel* m, int on) {
+  if (!m) return merr(VTB_CUDA_ERR_INVALID_ARG, "null model");
+  m->q8_act = on != 0;
+  return VTB_CUDA_OK;
+}
+
 VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max_rows) {
   if (!m || n_seqs <= 0 || max_rows < n_seqs || max_rows > 65535) {
     merr(VTB_CUDA_ERR_INVALID_ARG, "bad state dimensions");
@@ -1071,6 +1085,7 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   if (!s) return nullptr;
   s->m = m;
   s->device = m->device;
+  s->q8_act = m->q8_act;
   // The state owns its stream, so it never depends on the context outliving it.
   if (cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
     mcuda(cudaGetLastError());
@@ -1268,6 +1283,20 @@ static cudaError_t allreduce_tmp(VtbCudaState* s, size_t n) {
   return cudaSuccess;
 }
 
+// One row of a projection: y (+)= W . x.  Under the Q8_0 x Q8_0 option a Q8_0
+// weight takes x quantized per 32-block into the state's workspace (the
+// quantizer, then int32 block dots; dot_i8, simd.zig:31-62).
+static cudaError_t gemv_row(VtbCudaState* s, int q, const void* w, const float* x, float* y, int m, int k, int acc) {
+  if (s->q8_act && q == Q8_0) {
+    int8_t* xq = static_cast<int8_t*>(s->ws);
+    float* dx = reinterpret_cast<float*>(static_cast<char*>(s->ws) + (((size_t)k + 15) & ~size_t(15)));
+    cudaError_t e = launch_quantize_q8_0(x, xq, dx, k / 32, s->st);
+    if (e) return e;
+    return launch_gemv_q8_0_q8_0(w, xq, dx, y, m, k, s->st, true, acc);
+  }
+  return gemv_any(q, w, x, y, m, k, s->st, acc);
+}
+
 // One transformer block for the staged rows (cpuLayerStep, forward.zig:230-288).
 static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   VtbCudaModel* m = s->m;
@@ -1290,7 +1319,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   };
   auto proj = [&](int q, const uint8_t* w, const float* in, float* out, int mm, int k, int ld_out, int acc) -> cudaError_t {
     // out[r*ld_out + i] (+)= W . in[r]; GEMM rows need a dense out, so `acc` goes through tmp
-    if (gemm && k % 64 == 0 && (acc || ld_out == mm)) {
+    if (gemm && k % 64 == 0 && (acc || ld_out == mm) && !(s->q8_act && q == Q8_0)) {
       if (acc) {
         cudaError_t e2 = launch_gemm_tc(q, w, in, s->tmp, mm, k, R, true, s->ws, st, s->gsplit, s->gsplit_elems);
         if (e2) return e2;
@@ -1300,7 +1329,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
       return launch_gemm_tc(q, w, in, out, mm, k, R, true, s->ws, st, s->gsplit, s->gsplit_elems);
     }
     for (int r = 0; r < R; ++r) {
-      cudaError_t e2 = gemv_any(q, w, in + (size_t)r * k, out + (size_t)r * ld_out, mm, k, st, acc);
+      cudaError_t e2 = gemv_row(s, q, w, in + (size_t)r * k, out + (size_t)r * ld_out, mm, k, acc);
       if (e2) return e2;
     }
     return cudaSuccess;
@@ -1410,11 +1439,12 @@ static cudaError_t enqueue_final(VtbCudaState* s, bool last_only) {
   const int r0 = last_only ? s->rows - 1 : 0, n = last_only ? 1 : s->rows;
   if ((e = enqueue_norm(s, m->out_norm, r0, n))) return e;
   float* lg = tp ? s->logits_local : s->logits;
-  if (n >= GEMM_MIN_ROWS && c.dim % 64 == 0) {  // batch decode: one GEMM reads the LM head once for all rows
+  if (n >= GEMM_MIN_ROWS && c.dim % 64 == 0 && !(s->q8_act && m->q_out == Q8_0)) {
+    // batch decode: one GEMM reads the LM head once for all rows
     if ((e = launch_gemm_tc(m->q_out, m->out_w, s->xb, lg, m->V, c.dim, n, true, s->ws, st, s->gsplit, s->gsplit_elems))) return e;
   } else {
     for (int r = 0; r < n; ++r)
-      if ((e = gemv_any(m->q_out, m->out_w, s->xb + (size_t)r * c.dim, lg + (size_t)r * m->V, m->V, c.dim, st, 0)))
+      if ((e = gemv_row(s, m->q_out, m->out_w, s->xb + (size_t)r * c.dim, lg + (size_t)r * m->V, m->V, c.dim, 0)))
         return e;
   }
   if (tp) {  // all-gather the vocabulary slices, one row at a time (rank slices are contiguous vocab ranges)

@@ -258,7 +258,8 @@ def tp_slice(quant: int, t: np.ndarray, rows: int, k: int, row0: int, nrows: int
 class CudaModel:
     """Weights resident in HBM (vtb_cuda_model_create / _tp)."""
 
-    def __init__(self, ctx: Context, w: HostWeights, tp: "TensorParallel | None" = None):
+    def __init__(self, ctx: Context, w: HostWeights, tp: "TensorParallel | None" = None,
+                 q8_activations: bool = False):
         self.ctx, self.cfg, self.lib, self.tp = ctx, w.cfg, ctx.lib, tp
         c = w.cfg
         cc = _CConfig(c.dim, c.n_layers, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn_dim, c.vocab_size, c.max_seq,
@@ -278,6 +279,8 @@ class CudaModel:
                                                    _ptr(emb), qe, _ptr(w.output_norm), _ptr(out), qo)
         if not self.h:
             raise _lib.VtbError(-1, "vtb_cuda_model_create")
+        if q8_activations:  # Q8_0 projections on the Q8_0 x Q8_0 path (states created from now on)
+            _lib.check(self.lib.vtb_cuda_model_set_q8_activations(self.h, 1), "set_q8_activations")
 
     @classmethod
     def from_gguf(cls, ctx: Context, gguf, max_seq: int = 0, tp: "TensorParallel | None" = None) -> "CudaModel":
