@@ -22,7 +22,7 @@ cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* ou
 cudaError_t launch_quantize_q8_0(const float* x, int8_t* qs, float* d, int nblocks, cudaStream_t st);
 cudaError_t launch_q8_0_block_dots(const void* w, const int8_t* xq, int32_t* dots, int m, int nb, cudaStream_t st);
 cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
-                           void* ws, cudaStream_t st, float* part, size_t part_elems);
+                           void* ws, cudaStream_t st, float* part, size_t part_elems, long long pitch);
 }  // namespace vtb
 
 using namespace vtb;

@@ -258,7 +258,7 @@ template <int Q, int BN, int PASSES, int S, bool TA>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapBh,
                const __grid_constant__ CUtensorMap mapBl, const uint8_t* __restrict__ W, float* __restrict__ out,
-               int M, int K, int NB) {
+               int M, int K, int NB, long long pitch) {
   using C = TcCfg<Q, BN, PASSES, S, TA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -278,7 +278,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
   const int sb0 = ks > 1 ? z * nsb / ks : 0, sb1 = ks > 1 ? (z + 1) * nsb / ks : nsb;
   const int kb0 = ks > 1 ? 4 * sb0 : 0, kb1 = ks > 1 ? 4 * sb1 : K / TC_BK;
   out += (long long)z * NB * M;
-  const long long rb = host_row_bytes_dev<Q>(K);
+  const long long rb = pitch;  // bytes between weight rows (the dense row size, or a padded pitch)
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -430,14 +430,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
 
 template <int Q, int BN, int PASSES, int S, bool TA>
 static cudaError_t launch_gemm_tc_t(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
-                                    int k, int nb, int ks, cudaStream_t st) {
+                                    int k, int nb, int ks, cudaStream_t st, long long pitch) {
   using C = TcCfg<Q, BN, PASSES, S, TA>;
   auto kern = gemm_tc_kernel<Q, BN, PASSES, S, TA>;
   cudaError_t ea = ensure_smem_attr<gemm_tc_kernel<Q, BN, PASSES, S, TA>>(current_device(), C::SMEM);
   if (ea != cudaSuccess) return ea;
   CUtensorMap mA, mBh, mBl;
   memset(&mA, 0, sizeof mA);
-  const uint64_t rbytes = (uint64_t)host_row_bytes_dev<Q>(k);
+  const uint64_t rbytes = (uint64_t)pitch;
   if (TA &&
       !make_tmap(&mA, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, rbytes, (uint64_t)m, rbytes, TmaA<Q>::BOX, TC_BM,
                  CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -462,7 +462,7 @@ static cudaError_t launch_gemm_tc_t(const void* w, const __nv_bfloat16* xh, cons
   a[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = a;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, mA, mBh, mBl, (const uint8_t*)w, out, m, k, nb);
+  return cudaLaunchKernelEx(&cfg, kern, mA, mBh, mBl, (const uint8_t*)w, out, m, k, nb, pitch);
 }
 
 // Largest stage count (<= SMAX) whose shared memory fits the 227 KiB per-CTA limit.
@@ -475,37 +475,37 @@ constexpr int fit_stages() {
 
 template <int Q, int BN, int PASSES, bool TA>
 static cudaError_t launch_fit(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m, int k,
-                              int nb, int ks, cudaStream_t st) {
+                              int nb, int ks, cudaStream_t st, long long pitch) {
   constexpr int S = fit_stages<Q, BN, PASSES, TA, 5>();
   static_assert(TcCfg<Q, BN, PASSES, S, TA>::SMEM <= 227 * 1024, "GEMM tile does not fit in shared memory");
-  return launch_gemm_tc_t<Q, BN, PASSES, S, TA>(w, xh, xl, out, m, k, nb, ks, st);
+  return launch_gemm_tc_t<Q, BN, PASSES, S, TA>(w, xh, xl, out, m, k, nb, ks, st, pitch);
 }
 
 template <int Q, bool TA>
 static cudaError_t launch_gemm_tc_qt(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
-                                     int k, int nb, bool precise, int ks, cudaStream_t st) {
+                                     int k, int nb, bool precise, int ks, cudaStream_t st, long long pitch) {
   if (precise) {  // hi + lo tiles: twice the shared memory per stage
-    if (nb <= 64) return launch_fit<Q, 64, 3, TA>(w, xh, xl, out, m, k, nb, ks, st);
-    if (nb <= 128) return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, ks, st);
+    if (nb <= 64) return launch_fit<Q, 64, 3, TA>(w, xh, xl, out, m, k, nb, ks, st, pitch);
+    if (nb <= 128) return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, ks, st, pitch);
     if constexpr (TcCfg<Q, 256, 3, 2, TA>::SMEM <= 227 * 1024)
-      return launch_fit<Q, 256, 3, TA>(w, xh, xl, out, m, k, nb, ks, st);
+      return launch_fit<Q, 256, 3, TA>(w, xh, xl, out, m, k, nb, ks, st, pitch);
     else
-      return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, ks, st);
+      return launch_fit<Q, 128, 3, TA>(w, xh, xl, out, m, k, nb, ks, st, pitch);
   }
-  if (nb <= 64) return launch_fit<Q, 64, 1, TA>(w, xh, xl, out, m, k, nb, ks, st);
-  if (nb <= 128) return launch_fit<Q, 128, 1, TA>(w, xh, xl, out, m, k, nb, ks, st);
-  return launch_fit<Q, 256, 1, TA>(w, xh, xl, out, m, k, nb, ks, st);
+  if (nb <= 64) return launch_fit<Q, 64, 1, TA>(w, xh, xl, out, m, k, nb, ks, st, pitch);
+  if (nb <= 128) return launch_fit<Q, 128, 1, TA>(w, xh, xl, out, m, k, nb, ks, st, pitch);
+  return launch_fit<Q, 256, 1, TA>(w, xh, xl, out, m, k, nb, ks, st, pitch);
 }
 
 template <int Q>
 static cudaError_t launch_gemm_tc_q(const void* w, const __nv_bfloat16* xh, const __nv_bfloat16* xl, float* out, int m,
-                                    int k, int nb, bool precise, int ks, cudaStream_t st) {
+                                    int k, int nb, bool precise, int ks, cudaStream_t st, long long pitch) {
   // TMA weight staging needs 16-byte row pitches (all K-quant configs with k % 2048 == 0 qualify)
   if constexpr (Q == Q8_0 || Q == TQ2_0) {  // blocks off 16-byte boundaries: producers read global memory
-    return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, ks, st);
+    return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, ks, st, pitch);
   } else {
-    if (host_row_bytes_dev<Q>(k) % 16 == 0) return launch_gemm_tc_qt<Q, true>(w, xh, xl, out, m, k, nb, precise, ks, st);
-    return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, ks, st);
+    if (pitch % 16 == 0) return launch_gemm_tc_qt<Q, true>(w, xh, xl, out, m, k, nb, precise, ks, st, pitch);
+    return launch_gemm_tc_qt<Q, false>(w, xh, xl, out, m, k, nb, precise, ks, st, pitch);
   }
 }
 
@@ -524,8 +524,10 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, float* __re
 // `part` (optional, `part_elems` floats): when the (M/128) x (B/BN) tile grid
 // leaves most SMs idle (small batches), K is split across up to 8 CTAs per
 // tile, each writing a partial tile there; splitk_reduce_kernel sums them.
+// `pitch`: bytes between consecutive weight rows (0 = the dense row size).
 cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
-                           void* ws, cudaStream_t st, float* part = nullptr, size_t part_elems = 0) {
+                           void* ws, cudaStream_t st, float* part = nullptr, size_t part_elems = 0, long long pitch = 0) {
+  if (pitch == 0) pitch = host_row_bytes(q, k);
   __nv_bfloat16* xh = static_cast<__nv_bfloat16*>(ws);
   __nv_bfloat16* xl = precise ? xh + (size_t)nb * k : nullptr;
   const long long n = (long long)nb * k;
@@ -549,11 +551,11 @@ cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, 
   }
   float* dst = ks > 1 ? part : out;
   switch (q) {
-    case Q4_K: e = launch_gemm_tc_q<Q4_K>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
-    case Q5_K: e = launch_gemm_tc_q<Q5_K>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
-    case Q6_K: e = launch_gemm_tc_q<Q6_K>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
-    case Q8_0: e = launch_gemm_tc_q<Q8_0>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
-    case TQ2_0: e = launch_gemm_tc_q<TQ2_0>(w, xh, xl, dst, m, k, nb, precise, ks, st); break;
+    case Q4_K: e = launch_gemm_tc_q<Q4_K>(w, xh, xl, dst, m, k, nb, precise, ks, st, pitch); break;
+    case Q5_K: e = launch_gemm_tc_q<Q5_K>(w, xh, xl, dst, m, k, nb, precise, ks, st, pitch); break;
+    case Q6_K: e = launch_gemm_tc_q<Q6_K>(w, xh, xl, dst, m, k, nb, precise, ks, st, pitch); break;
+    case Q8_0: e = launch_gemm_tc_q<Q8_0>(w, xh, xl, dst, m, k, nb, precise, ks, st, pitch); break;
+    case TQ2_0: e = launch_gemm_tc_q<TQ2_0>(w, xh, xl, dst, m, k, nb, precise, ks, st, pitch); break;
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess || ks == 1) return e;

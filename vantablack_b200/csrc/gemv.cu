@@ -273,7 +273,7 @@ __device__ __forceinline__ float lane_dot_q80_i8(const uint8_t* blk, const XQSli
 template <int Q, int R, int S, int WARPS, bool XQ>
 __global__ void __launch_bounds__(WARPS * 32)
 gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const float* __restrict__ dx,
-            float* __restrict__ y, int M, int K, int accumulate) {
+            float* __restrict__ y, int M, int K, int accumulate, long long pitch) {
   const float* x = static_cast<const float*>(xv);
   constexpr int CH = GemvCfg<Q>::CH, BB = Fmt<Q>::bytes, EL = Fmt<Q>::elems;
   constexpr int SLOT = Slot<Q>::BYTES, STAGE = R * SLOT;
@@ -283,7 +283,7 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + WARPS * S * STAGE) + warp * S;
 
   const int nb = K / EL, nch = (nb + CH - 1) / CH;
-  const long long rb = (long long)nb * BB;
+  const long long rb = pitch;  // bytes between rows
   const int ngroups = (M + R - 1) / R;
   const int gw = blockIdx.x * WARPS + warp, NW = gridDim.x * WARPS;
   const int my_groups = gw < ngroups ? (ngroups - 1 - gw) / NW + 1 : 0;
@@ -393,7 +393,8 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
 // ---------------- host launcher ----------------
 template <int Q, int R, int S, int WARPS, bool XQ = false>
 static cudaError_t launch_gemv_t(const void* w, const void* x, const float* dx, float* y, int m, int k,
-                                 cudaStream_t st, bool pdl, int accumulate = 0) {
+                                 cudaStream_t st, bool pdl, int accumulate = 0, long long pitch = 0) {
+  if (pitch == 0) pitch = host_row_bytes(Q, k);
   auto kern = gemv_kernel<Q, R, S, WARPS, XQ>;
   constexpr int smem = WARPS * S * R * Slot<Q>::BYTES + WARPS * S * 8;
   const int dev = current_device();
@@ -414,20 +415,27 @@ static cudaError_t launch_gemv_t(const void* w, const void* x, const float* dx, 
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, dx, y, m, k, accumulate);
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, dx, y, m, k, accumulate, pitch);
+}
+
+// `pitch`: bytes between consecutive weight rows (0 = the dense row size).
+cudaError_t launch_gemv_pitched(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
+                                bool pdl, int accumulate, long long pitch) {
+  if (pitch == 0) pitch = host_row_bytes(q, k);
+  switch (q) {
+    case Q5_K: return launch_gemv_t<Q5_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
+    case Q6_K:  // integer tensor cores when rows sit on 16-byte pitches
+      if (q6k_mma_ok(w, k, pitch)) return launch_gemv_q6k_mma(w, x, y, m, k, st, pdl, accumulate, pitch);
+      return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
+    case Q8_0: return launch_gemv_t<Q8_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
+    case TQ2_0: return launch_gemv_t<TQ2_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                         int accumulate) {
-  switch (q) {
-    case Q5_K: return launch_gemv_t<Q5_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
-    case Q6_K:  // integer tensor cores when rows are whole 16-byte multiples
-      if (q6k_mma_ok(w, k)) return launch_gemv_q6k_mma(w, x, y, m, k, st, pdl, accumulate);
-      return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
-    case Q8_0: return launch_gemv_t<Q8_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
-    case TQ2_0: return launch_gemv_t<TQ2_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate);
-    default: return cudaErrorInvalidValue;
-  }
+  return launch_gemv_pitched(q, w, x, y, m, k, st, pdl, accumulate, 0);
 }
 
 cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* dx, float* y, int m, int k,

@@ -238,12 +238,12 @@ constexpr int q6k_mma_smem(int k) {
 
 template <int WARPS, int S>
 static cudaError_t launch_q6k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                    int accumulate) {
+                                    int accumulate, long long pitch) {
   auto kern = gemv_q6k_mma_kernel<WARPS, S>;
   const int smem = q6k_mma_smem<WARPS, S>(k);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   CUtensorMap wmap;
-  const uint64_t rbytes = (uint64_t)(k / 256) * 210;
+  const uint64_t rbytes = (uint64_t)pitch;  // row pitch, a 16-byte multiple (rows may carry zero padding)
   if (!make_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, rbytes / 4, (uint64_t)m, rbytes, Q6M_BOXB / 4, Q6M_ROWS,
                  CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
@@ -270,15 +270,18 @@ static cudaError_t launch_q6k_mma_t(const void* w, const float* x, float* y, int
   return cudaLaunchKernelEx(&cfg, kern, wmap, y, x, m, k, ksplit, accumulate);
 }
 
-// Usable when rows are whole 16-byte multiples (k % 2048 == 0) and w is 16-byte aligned.
-bool q6k_mma_ok(const void* w, int k) {
-  return k % 2048 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && q6k_mma_smem<8, 2>(k) <= 227 * 1024;
+// Usable when the row pitch is a 16-byte multiple (dense rows when k % 2048 == 0,
+// or rows the model uploaded with zero padding), rows hold whole super-block
+// pairs (k % 512 == 0) and w is 16-byte aligned.
+bool q6k_mma_ok(const void* w, int k, long long pitch) {
+  return k % 512 == 0 && pitch % 16 == 0 && pitch >= (long long)(k / 256) * 210 &&
+         (reinterpret_cast<uintptr_t>(w) & 15) == 0 && q6k_mma_smem<8, 2>(k) <= 227 * 1024;
 }
 
 cudaError_t launch_gemv_q6k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                int accumulate) {
-  if (q6k_mma_smem<12, 2>(k) <= 227 * 1024) return launch_q6k_mma_t<12, 2>(w, x, y, m, k, st, pdl, accumulate);
-  return launch_q6k_mma_t<8, 2>(w, x, y, m, k, st, pdl, accumulate);
+                                int accumulate, long long pitch) {
+  if (q6k_mma_smem<12, 2>(k) <= 227 * 1024) return launch_q6k_mma_t<12, 2>(w, x, y, m, k, st, pdl, accumulate, pitch);
+  return launch_q6k_mma_t<8, 2>(w, x, y, m, k, st, pdl, accumulate, pitch);
 }
 
 }  // namespace vtb

@@ -29,12 +29,14 @@ namespace vtb {
 
 cudaError_t launch_gemv(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                         int accumulate);
+cudaError_t launch_gemv_pitched(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
+                                bool pdl, int accumulate, long long pitch);
 cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                 int accumulate, const float* norm_w, float eps, float* swi);
 cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* out, int dim, int n_tok,
                          cudaStream_t st);
 cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
-                           void* ws, cudaStream_t st, float* part, size_t part_elems);
+                           void* ws, cudaStream_t st, float* part, size_t part_elems, long long pitch);
 
 // Prefill steps with at least this many rows run their projections as one
 // tensor-core GEMM (precise mode) instead of one GEMV per row.
@@ -52,10 +54,11 @@ cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* 
                                   cudaStream_t st, bool pdl, int accumulate);
 cudaError_t launch_quantize_q8_0(const float* x, int8_t* qs, float* d, int nblocks, cudaStream_t st);
 
+// `pitch`: bytes between weight rows (0 = dense; only Q6_K rows are ever padded).
 static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
-                            int accumulate) {
+                            int accumulate, long long pitch = 0) {
   if (q == Q4_K) return launch_gemv_q4k_mma(w, x, y, m, k, st, true, accumulate, nullptr, 0.f, nullptr);
-  return launch_gemv(q, w, x, y, m, k, st, true, accumulate);
+  return launch_gemv_pitched(q, w, x, y, m, k, st, true, accumulate, pitch);
 }
 
 // ---------------- kernels ----------------
@@ -749,6 +752,7 @@ struct DevLayer {
   bool gu_il;
   const uint8_t* gate; const uint8_t* up;
   const uint8_t* down;
+  long long down_pitch;  // bytes between ffn_down rows: Q6_K rows padded to 16 bytes for the tensor-core GEMV
   const float* attn_norm;
   const float* ffn_norm;
   int q_q, q_k, q_v, q_o, q_gate, q_up, q_down;
@@ -946,6 +950,13 @@ VtbCudaModel* vtb_cuda_model_create_tp(VtbCudaCtx* ctx, VtbCudaTp* tp, const Vtb
   auto rbytes = [](int q, int k) { return (size_t)host_row_bytes(q, k); };
   size_t off = 0;
   auto take = [&](size_t n) { size_t o = off; off = (off + n + 255) & ~size_t(255); return o; };
+  // ffn_down rows (k = this rank's F): Q6_K rows that are not 16-byte multiples are
+  // padded with zeros to a 16-byte pitch when they hold whole super-block pairs,
+  // which the tensor-core GEMV and the GEMM's TMA staging need.
+  auto down_pitch = [&](int q, int k) -> size_t {
+    const size_t rb = rbytes(q, k);
+    return (q == Q6_K && k % 512 == 0 && rb % 16) ? (rb + 15) & ~size_t(15) : rb;
+  };
   struct Off { size_t qkv, q, k, v, o, gu, gate, up, down, an, fn; bool fq, fg; };
   std::vector<Off> offs(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
@@ -957,7 +968,7 @@ VtbCudaModel* vtb_cuda_model_create_tp(VtbCudaCtx* ctx, VtbCudaTp* tp, const Vtb
     o.o = take(rbytes(lw[l].q_attn_o, qd) * d);
     if (o.fg) o.gu = take(rbytes(lw[l].q_ffn_gate, d) * 2 * F);
     else { o.gate = take(rbytes(lw[l].q_ffn_gate, d) * F); o.up = take(rbytes(lw[l].q_ffn_up, d) * F); }
-    o.down = take(rbytes(lw[l].q_ffn_down, F) * d);
+    o.down = take(down_pitch(lw[l].q_ffn_down, F) * d);
     o.an = take(4 * (size_t)d);
     o.fn = take(4 * (size_t)d);
   }
@@ -1031,7 +1042,15 @@ VtbCudaModel* vtb_cuda_model_create_tp(VtbCudaCtx* ctx, VtbCudaTp* tp, const Vtb
       up_shard(o.up, L.q_up, lw[l].ffn_up, d, sh.ffn_row0, F, 0, d);
     }
     L.down = B + o.down;
-    up_shard(o.down, L.q_down, lw[l].ffn_down, f, 0, d, sh.down_col0, sh.down_cols);
+    L.down_pitch = (long long)down_pitch(L.q_down, F);
+    if ((size_t)L.down_pitch == rbytes(L.q_down, F)) {
+      up_shard(o.down, L.q_down, lw[l].ffn_down, f, 0, d, sh.down_col0, sh.down_cols);
+    } else {  // padded rows: zero the padding, then copy each row's shard columns to its pitch
+      const size_t rb = rbytes(L.q_down, f), w = rbytes(L.q_down, F), c0 = rbytes(L.q_down, sh.down_col0);
+      ok = ok && cudaMemsetAsync(B + o.down, 0, (size_t)L.down_pitch * d, st) == cudaSuccess;
+      ok = ok && cudaMemcpy2DAsync(B + o.down, (size_t)L.down_pitch, static_cast<const uint8_t*>(lw[l].ffn_down) + c0,
+                                   rb, w, d, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    }
     L.attn_norm = reinterpret_cast<const float*>(B + o.an);
     L.ffn_norm = reinterpret_cast<const float*>(B + o.fn);
     up(o.an, lw[l].attn_norm, 4 * (size_t)d);
@@ -1286,7 +1305,8 @@ static cudaError_t allreduce_tmp(VtbCudaState* s, size_t n) {
 // One row of a projection: y (+)= W . x.  Under the Q8_0 x Q8_0 option a Q8_0
 // weight takes x quantized per 32-block into the state's workspace (the
 // quantizer, then int32 block dots; dot_i8, simd.zig:31-62).
-static cudaError_t gemv_row(VtbCudaState* s, int q, const void* w, const float* x, float* y, int m, int k, int acc) {
+static cudaError_t gemv_row(VtbCudaState* s, int q, const void* w, const float* x, float* y, int m, int k, int acc,
+                            long long pitch = 0) {
   if (s->q8_act && q == Q8_0) {
     int8_t* xq = static_cast<int8_t*>(s->ws);
     float* dx = reinterpret_cast<float*>(static_cast<char*>(s->ws) + (((size_t)k + 15) & ~size_t(15)));
@@ -1294,7 +1314,7 @@ static cudaError_t gemv_row(VtbCudaState* s, int q, const void* w, const float* 
     if (e) return e;
     return launch_gemv_q8_0_q8_0(w, xq, dx, y, m, k, s->st, true, acc);
   }
-  return gemv_any(q, w, x, y, m, k, s->st, acc);
+  return gemv_any(q, w, x, y, m, k, s->st, acc, pitch);
 }
 
 // One transformer block for the staged rows (cpuLayerStep, forward.zig:230-288).
@@ -1317,28 +1337,29 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
                               nullptr);
     return true;
   };
-  auto proj = [&](int q, const uint8_t* w, const float* in, float* out, int mm, int k, int ld_out, int acc) -> cudaError_t {
+  auto proj = [&](int q, const uint8_t* w, const float* in, float* out, int mm, int k, int ld_out, int acc,
+                  long long pitch = 0) -> cudaError_t {
     // out[r*ld_out + i] (+)= W . in[r]; GEMM rows need a dense out, so `acc` goes through tmp
     if (gemm && k % 64 == 0 && (acc || ld_out == mm) && !(s->q8_act && q == Q8_0)) {
       if (acc) {
-        cudaError_t e2 = launch_gemm_tc(q, w, in, s->tmp, mm, k, R, true, s->ws, st, s->gsplit, s->gsplit_elems);
+        cudaError_t e2 = launch_gemm_tc(q, w, in, s->tmp, mm, k, R, true, s->ws, st, s->gsplit, s->gsplit_elems, pitch);
         if (e2) return e2;
         return pdl_launch(add_kernel, dim3(min(1184, (R * mm + 255) / 256)), dim3(256), 0, st, out,
                           (const float*)s->tmp, (long long)R * mm);
       }
-      return launch_gemm_tc(q, w, in, out, mm, k, R, true, s->ws, st, s->gsplit, s->gsplit_elems);
+      return launch_gemm_tc(q, w, in, out, mm, k, R, true, s->ws, st, s->gsplit, s->gsplit_elems, pitch);
     }
     for (int r = 0; r < R; ++r) {
-      cudaError_t e2 = gemv_row(s, q, w, in + (size_t)r * k, out + (size_t)r * ld_out, mm, k, acc);
+      cudaError_t e2 = gemv_row(s, q, w, in + (size_t)r * k, out + (size_t)r * ld_out, mm, k, acc, pitch);
       if (e2) return e2;
     }
     return cudaSuccess;
   };
   // x += W . in for the row-parallel projections (O, down): single GPU adds
   // straight into x; tensor parallel writes the partial to tmp and all-reduces.
-  auto residual = [&](int q, const uint8_t* w, const float* in, int k) -> cudaError_t {
-    if (!tp) return proj(q, w, in, s->x, d, k, d, 1);
-    cudaError_t e2 = proj(q, w, in, partial_out(s), d, k, d, 0);
+  auto residual = [&](int q, const uint8_t* w, const float* in, int k, long long pitch) -> cudaError_t {
+    if (!tp) return proj(q, w, in, s->x, d, k, d, 1, pitch);
+    cudaError_t e2 = proj(q, w, in, partial_out(s), d, k, d, 0, pitch);
     if (e2) return e2;
     return allreduce_tmp(s, (size_t)R * d);
   };
@@ -1400,7 +1421,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
                         s->att, ri, H, hd, s->nsplit)))
       return e;
   }
-  if ((e = residual(L.q_o, L.o, s->att, qd))) return e;  // x += W_o . att (addInto fused)
+  if ((e = residual(L.q_o, L.o, s->att, qd, 0))) return e;  // x += W_o . att (addInto fused)
   if (!gemm && L.gu && L.gu_il && L.q_gate == Q4_K) {
     // SwiGLU in the GEMV's epilogue (h directly); the FFN RMSNorm in its prologue,
     // or, with a tensor-parallel partial pending, in the all-reduce kernel before it
@@ -1410,7 +1431,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
       e = launch_gemv_q4k_mma(L.gu, (pend ? s->xb : s->x) + (size_t)r * d, nullptr, 2 * f, d, st, true, 0,
                               pend ? nullptr : L.ffn_norm, c.rms_eps, s->h + (size_t)r * f);
     if (e) return e;
-    return residual(L.q_down, L.down, s->h, f);
+    return residual(L.q_down, L.down, s->h, f, L.down_pitch);
   }
   if (fused_norm_gemv(L.ffn_norm, L.q_gate, L.gu, s->gu, 2 * f)) {
     if (e) return e;
@@ -1425,7 +1446,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   if ((e = pdl_launch(swiglu_kernel, dim3(min(1184, (R * f + 255) / 256)), dim3(256), 0, st, (const float*)s->gu, s->h,
                       f, R, L.gu && L.gu_il ? 1 : 0)))
     return e;
-  return residual(L.q_down, L.down, s->h, f);
+  return residual(L.q_down, L.down, s->h, f, L.down_pitch);
 }
 
 // Final RMSNorm + LM head (backend_cpu.zig finalStep :88-106) and argmax.
