@@ -71,6 +71,18 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int chunk) {  // byte offse
 
 // ---- bit-exact dequantization of 64 consecutive weights [k0, k0+64) of one row ----
 __device__ __forceinline__ uint32_t ldg_u32(const uint8_t* p) { return __ldg(reinterpret_cast<const uint32_t*>(p)); }
+// Explicit shared-memory loads: the staging pointers pass through integer
+// alignment arithmetic, after which the compiler would emit generic loads.
+__device__ __forceinline__ uint32_t lds_u32(const uint8_t* p) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
+  return v;
+}
+__device__ __forceinline__ uint4 lds_u128(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_u32(p)));
+  return v;
+}
 // 4-byte words from a 2-byte-aligned global address
 template <int NW, bool SMEM = false>
 __device__ __forceinline__ void ldg_words_a2(const uint8_t* p, uint32_t* out) {
@@ -79,17 +91,17 @@ __device__ __forceinline__ void ldg_words_a2(const uint8_t* p, uint32_t* out) {
   const unsigned sh = (unsigned)(a & 3) * 8u;
   uint32_t w[NW + 1];
 #pragma unroll
-  for (int i = 0; i <= NW; ++i) w[i] = SMEM ? *reinterpret_cast<const uint32_t*>(b + 4 * i) : ldg_u32(b + 4 * i);
+  for (int i = 0; i <= NW; ++i) w[i] = SMEM ? lds_u32(b + 4 * i) : ldg_u32(b + 4 * i);
 #pragma unroll
   for (int i = 0; i < NW; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }
 __device__ __forceinline__ unsigned byte_of(const uint32_t* w, int i) { return (w[i >> 2] >> (8 * (i & 3))) & 0xffu; }
 
 // SMEM: `blk` points into shared memory (TMA-staged super-block), read with
-// generic loads; otherwise it is global memory, read through the read-only path.
+// ld.shared; otherwise it is global memory, read through the read-only path.
 template <bool SMEM>
 __device__ __forceinline__ uint4 ld16(const uint8_t* p) {
-  if constexpr (SMEM) return *reinterpret_cast<const uint4*>(p);
+  if constexpr (SMEM) return lds_u128(p);
   else return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
