@@ -14,10 +14,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_tinyllama_greedy_identical(tmp_path):
+@pytest.mark.parametrize("source", ["host", "gguf"])
+def test_tp2_tinyllama_greedy_identical(tmp_path, source):
     out = tmp_path / "tp.json"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(HERE, "tp_worker.py"), str(out), "64"]
+           "--master-addr=127.0.0.1", f"--master-port={29533 + (source == 'gguf')}", os.path.join(HERE, "tp_worker.py"),
+           str(out), "64"] + ([str(tmp_path / "tiny.gguf")] if source == "gguf" else [])
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-3000:]

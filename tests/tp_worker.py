@@ -2,7 +2,9 @@
 tests/test_tp_gpu.py through torch.distributed.run, one process per GPU.
 
 Every rank builds the same seeded TinyLlama-architecture weights, uploads its
-shard (vtb_cuda_model_create_tp), runs a batched prefill of a 128-token prompt
+shard (vtb_cuda_model_create_tp; or, given a GGUF path as argv[3], rank 0
+writes the weights to that file and every rank uploads its shard from it with
+vtb_cuda_model_create_gguf_tp), runs a batched prefill of a 128-token prompt
 and greedy decode; rank 0 compares the token ids with the CPU oracle and
 writes the verdict to the JSON path given as argv[1]."""
 import json
@@ -17,6 +19,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def main():
     out_path, n_gen = sys.argv[1], int(sys.argv[2])
+    gguf_path = sys.argv[3] if len(sys.argv) > 3 else None  # load the shards from one GGUF file
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     dist.init_process_group("gloo")
 
@@ -30,7 +33,17 @@ def main():
     prompt = np.random.default_rng(44).integers(3, TINYLLAMA.vocab_size, 128)
     ctx = Context(local)
     tp = TensorParallel(local, rank, world, exchange)
-    st = CudaState(CudaModel(ctx, w, tp), 1, max_rows=128)
+    if gguf_path:  # rank 0 writes the file, every rank uploads its shard from it
+        from vantablack_b200.gguf import GgufFile
+        from vantablack_b200.model import write_synthetic_gguf
+        if rank == 0:
+            write_synthetic_gguf(gguf_path, TINYLLAMA, seed=4)
+        dist.barrier()
+        with GgufFile(gguf_path) as g:
+            model = CudaModel.from_gguf(ctx, g, tp=tp)
+    else:
+        model = CudaModel(ctx, w, tp)
+    st = CudaState(model, 1, max_rows=128)
     ids, logits = st.generate_greedy(prompt, n_gen, use_prefill=True)
     from vantablack_b200 import _lib
     _lib.check(_lib.load().vtb_cuda_check_device_error(), "device error word")  # no peer wait timed out
