@@ -183,6 +183,30 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
       :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+// Four int8 limbs of four activations r (|r| < 2^22) in base 254, as the
+// integer tensor-core GEMVs feed them: lw[c] packs limb c of elements 0..3
+// (byte i = element i), with L_0 = rint(r) and L_c = rint((r_{c-1} -
+// L_{c-1}) * 254).  t = r + 1.5*2^23 rounds to the nearest integer (ties to
+// even, as rintf) and leaves L's two's-complement byte in t's low byte;
+// -254 L = fma(t, -254, 254 * 1.5*2^23) is exact, and fma(r, 254, -254 L)
+// rounds (r - L) * 254 once, exactly as the subtract-then-multiply does.
+__device__ __forceinline__ void limbs254(float xv[4], uint32_t lw[4]) {
+  constexpr float kMagic = 12582912.0f, kMagic254 = 12582912.0f * 254.0f;
+#pragma unroll
+  for (int li = 0; li < 4; ++li) {
+    float tq[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tq[c] = xv[c] + kMagic;
+    const uint32_t lo = __byte_perm(__float_as_uint(tq[0]), __float_as_uint(tq[1]), 0x0040);
+    const uint32_t hi = __byte_perm(__float_as_uint(tq[2]), __float_as_uint(tq[3]), 0x0040);
+    lw[li] = __byte_perm(lo, hi, 0x5410);
+    if (li < 3) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) xv[c] = fmaf(xv[c], 254.f, fmaf(tq[c], -254.f, kMagic254));
+    }
+  }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

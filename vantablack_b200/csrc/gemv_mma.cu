@@ -29,7 +29,10 @@
 // super-block HBM -> shared as one 2-D TMA box (no multicast) into an S-stage
 // mbarrier ring; the copies for the first S tiles are issued before
 // griddepcontrol.wait, so with programmatic dependent launch they overlap the
-// kernel that produces x.
+// kernel that produces x.  A landed tile is read out at once (A fragments and
+// decoded block scales into registers), which frees its stage for the next
+// copy; the activation loads are issued before the first read-out so their
+// L2 latency overlaps it.
 #include <cstring>
 
 #include "common.cuh"
@@ -55,80 +58,90 @@ struct XShared {
   float2* xs;
 };
 
+// Converts group gi (4 sub-blocks, 128 elements; this lane holds elements
+// 4*lane .. 4*lane+3 in `a`) into int8 limbs and {2^e, sum x} per sub-block.
+__device__ __forceinline__ void convert_group(float4 a, int gi, int lane, XShared xsh) {
+  const int sub = lane >> 3, part = lane & 7;
+  float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
+  float sum = (a.x + a.y) + (a.z + a.w);
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  const int E = (int)((__float_as_uint(m) >> 23) & 0xffu);  // biased exponent of max|x|
+  // max|x| * 2^-e in [32, 64), so L0 = rint(x') fits int8 with room; zero /
+  // subnormal blocks keep e = 0 (their limbs round to 0)
+  const int e = (E == 0) ? 0 : (E - 127 - 5);
+  const float sx = __uint_as_float((uint32_t)(127 + e) << 23);
+  const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+  float xv[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};  // exact (power of two)
+  uint32_t lw[4];
+  limbs254(xv, lw);
+  const int s = gi * 4 + sub;
+  // element l = 4*part + c sits at t = part & 3, half = part >> 2, byte c
+  int8_t* dst = xsh.xq + s * 128 + (part & 3) * 8 + (part >> 2) * 4;
+#pragma unroll
+  for (int li = 0; li < 4; ++li) *reinterpret_cast<uint32_t*>(dst + 32 * li) = lw[li];
+  if (part == 0) xsh.xs[s] = make_float2(sx, sum);
+}
+
+// x (times the RMSNorm weight `nw` and `inv` when nw is given: the layer's
+// rmsNorm, math.zig:11-32, fused into the GEMV that consumes it) for groups
+// gi = base + u * nwarps.
+__device__ __forceinline__ float4 load_group(const float* __restrict__ x, int gi, int lane, const float* __restrict__ nw,
+                                             float inv) {
+  float4 v = __ldg(reinterpret_cast<const float4*>(x + gi * 128) + lane);
+  if (nw) {
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(nw + gi * 128) + lane);
+    v = make_float4((v.x * wv.x) * inv, (v.y * wv.y) * inv, (v.z * wv.z) * inv, (v.w * wv.w) * inv);
+  }
+  return v;
+}
+
 // Each warp converts 4 sub-blocks per float4 load (8 lanes per sub-block) and
 // keeps up to 8 loads in flight, so the prologue costs about one L2 round trip.
-// With `nw` (an RMSNorm weight), x is replaced by (x * nw) * inv where
-// inv = 1 / sqrt(mean(x^2) + eps): the layer's rmsNorm (math.zig:11-32)
-// fused into the GEMV that consumes it.  `inv` is computed by the caller.
 __device__ __forceinline__ void build_x_shared(const float* __restrict__ x, int K, XShared xsh, int warp, int lane,
                                                int nwarps, const float* __restrict__ nw, float inv) {
   const int n4 = K / 128;  // groups of 4 sub-blocks
-  const int sub = lane >> 3, part = lane & 7;
   for (int base = warp; base < n4; base += nwarps * 8) {
     float4 v[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int gi = base + u * nwarps;
-      if (gi < n4) {
-        v[u] = __ldg(reinterpret_cast<const float4*>(x + gi * 128) + lane);
-        if (nw) {
-          const float4 wv = __ldg(reinterpret_cast<const float4*>(nw + gi * 128) + lane);
-          v[u] = make_float4((v[u].x * wv.x) * inv, (v[u].y * wv.y) * inv, (v[u].z * wv.z) * inv, (v[u].w * wv.w) * inv);
-        }
-      }
+      if (gi < n4) v[u] = load_group(x, gi, lane, nw, inv);
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int gi = base + u * nwarps;
       if (gi >= n4) break;
-      const float4 a = v[u];
-      float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
-      float sum = (a.x + a.y) + (a.z + a.w);
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      }
-      const int E = (int)((__float_as_uint(m) >> 23) & 0xffu);  // biased exponent of max|x|
-      // max|x| * 2^-e in [32, 64), so L0 = rint(x') fits int8 with room; zero /
-      // subnormal blocks keep e = 0 (their limbs round to 0)
-      const int e = (E == 0) ? 0 : (E - 127 - 5);
-      const float sx = __uint_as_float((uint32_t)(127 + e) << 23);
-      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
-      const float xv[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};  // exact (power of two)
-      uint32_t lw[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float r = xv[c];
-#pragma unroll
-        for (int li = 0; li < 4; ++li) {  // r - L is exact in f32; each step scales by 254
-          const float L = rintf(r);
-          lw[li] |= ((uint32_t)(int)L & 0xffu) << (8 * c);
-          r = (r - L) * 254.f;
-        }
-      }
-      const int s = gi * 4 + sub;
-      // element l = 4*part + c sits at t = part & 3, half = part >> 2, byte c
-      int8_t* dst = xsh.xq + s * 128 + (part & 3) * 8 + (part >> 2) * 4;
-#pragma unroll
-      for (int li = 0; li < 4; ++li) *reinterpret_cast<uint32_t*>(dst + 32 * li) = lw[li];
-      if (part == 0) xsh.xs[s] = make_float2(sx, sum);
+      convert_group(v[u], gi, lane, xsh);
     }
   }
 }
 
-// TM: the tile arrives as one 2-D TMA box (32 rows x one super-block, rows
-// dense at 144 B = 4 (mod 32) words, conflict-free); otherwise as one 1-D
-// bulk copy per row into rows padded to 12 (mod 32) words.  Per-row copies of
-// a few hundred bytes cap the stream near 5 TB/s on their issue rate alone;
-// one box per tile moves the same bytes with 32x fewer copy operations.
+// The tile arrives as one 2-D TMA box (32 or 16 rows x one super-block, rows
+// dense at 144 B = 4 (mod 32) words, so the fragment loads are conflict-free).
+// Per-row copies of a few hundred bytes capped the stream near 5 TB/s on their
+// issue rate alone; one box per tile moves the same bytes with 32x fewer copy
+// operations.
 template <int CHB, bool TM, int ROWS_ = 32>
 struct MmaQ4K {
   static constexpr int ROWS = ROWS_;  // 32 (two m16 MMA tiles per warp tile) or 16 (one)
   static constexpr int BB = 144;
-  static constexpr int SLOT = TM ? CHB * BB : CHB * BB + 16;
+  static constexpr int SLOT = BB;
   static constexpr int STAGE = ROWS * SLOT;
-  static_assert(!TM || CHB == 1, "2-D TMA tiles hold one super-block per row");
+  static_assert(TM && CHB == 1, "tiles are 2-D TMA boxes of one super-block per row");
+};
+
+// A tile's weight-side operands, read out of shared memory before the
+// activations are needed: the MMA A fragments (raw nibble words) and, per
+// (sub-block group, row), the block scales d*sc (times 1/16 for the high-
+// nibble sub-blocks, which the MMA sees as 16q) and dmin*mn.
+template <int MT>
+struct TilePrep {
+  uint32_t a[2][2][MT][4];  // [group][pair in group][m-tile][a0..a3]
+  float d1[2][2 * MT], m1[2][2 * MT];
 };
 
 template <int WARPS, int S, int CHB, bool TM, int ROWS>
@@ -148,17 +161,17 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
   xsh.xq = reinterpret_cast<int8_t*>(red + WARPS * 32);
   xsh.xs = reinterpret_cast<float2*>(xsh.xq + 4 * K);
 
-  // Work: 32-row units.  The CTA's warps form WARPS/ksplit slots; a slot's
-  // ksplit warps share one unit and split its K range by chunks of CHB
-  // super-blocks (chunk c goes to part c % ksplit).  Small M uses a large
-  // ksplit so every SM streams; large M uses ksplit = 1.
-  const int slots = WARPS / ksplit, slot = warp / ksplit, kpart = warp % ksplit;
-  const int nb = K / 256, nch = (nb + CHB - 1) / CHB;
-  const long long rb = (long long)nb * C::BB;
+  // Work: ROWS-row units.  The CTA's warps form WARPS/ksplit slots; a slot's
+  // ksplit warps share one unit and split its K range by super-blocks
+  // (super-block c goes to part c % ksplit).  Small M uses a large ksplit so
+  // every SM streams; large M uses ksplit = 1.  ksplit is a power of two.
+  const int kshift = __ffs(ksplit) - 1;
+  const int slots = WARPS >> kshift, slot = warp >> kshift, kpart = warp & (ksplit - 1);
+  const int nch = K / 256;
   const int nunits = (M + C::ROWS - 1) / C::ROWS;
-  const int ngroups = (nunits + slots - 1) / slots;  // a group = `slots` consecutive units
+  const int ngroups = (nunits + slots - 1) >> (__ffs(slots) - 1);  // a group = `slots` consecutive units
   const int my_groups = blockIdx.x < ngroups ? (ngroups - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int my_chunks = kpart < nch ? (nch - 1 - kpart) / ksplit + 1 : 0;
+  const int my_chunks = kpart < nch ? ((nch - 1 - kpart) >> kshift) + 1 : 0;
   const int ntiles = my_groups * my_chunks;
 
   if (lane == 0) {
@@ -167,34 +180,73 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
   }
   __syncwarp();
 
-  // Tile tt = (group tt / my_chunks, chunk kpart + ksplit * (tt % my_chunks)).
-  // Each lane copies one row; lane 0 arms the barrier first.
-  auto issue = [&](int tt) {
-    const int u = (blockIdx.x + (tt / my_chunks) * gridDim.x) * slots + slot;
-    const int c = kpart + ksplit * (tt % my_chunks), st = tt % S;
-    const int b0 = c * CHB, nblk = min(CHB, nb - b0);
-    const int r0 = u * C::ROWS, nr = max(0, min(C::ROWS, M - r0));
-    if constexpr (TM) {  // rows past M arrive zero-filled and count toward the box bytes
-      if (lane == 0) {
-        mbar_expect_tx(&bars[st], (unsigned)C::STAGE);
-        tma_load_2d(ring + st * C::STAGE, &wmap, b0 * (C::BB / 4), r0, &bars[st]);
-      }
-    } else {
-      const unsigned bytes = (unsigned)(nblk * C::BB);
-      if (lane == 0) mbar_expect_tx(&bars[st], bytes * (unsigned)nr);
-      __syncwarp();
-      if (lane < nr)
-        bulk_g2s(ring + st * C::STAGE + lane * C::SLOT, W + (long long)(r0 + lane) * rb + (long long)b0 * C::BB,
-                 bytes, &bars[st]);
+  // Tiles go out in order (group, chunk); rows past M arrive zero-filled and
+  // count toward the box bytes.
+  int iss_g = 0, iss_c = 0, iss_n = 0;
+  auto issue_next = [&]() {
+    if (iss_n >= ntiles) return;
+    const int u = (blockIdx.x + iss_g * gridDim.x) * slots + slot;
+    const int c = kpart + (iss_c << kshift), st = iss_n % S;
+    if (lane == 0) {
+      mbar_expect_tx(&bars[st], (unsigned)C::STAGE);
+      tma_load_2d(ring + st * C::STAGE, &wmap, c * (C::BB / 4), u * C::ROWS, &bars[st]);
     }
+    ++iss_n;
+    if (++iss_c == my_chunks) { iss_c = 0; ++iss_g; }
   };
-  for (int tt = 0; tt < min(S, ntiles); ++tt) issue(tt);
+#pragma unroll
+  for (int i = 0; i < S; ++i) issue_next();
 
   // Let the next kernel in the stream launch now (its own wait still orders it
   // after this grid completes): its CTAs start their weight prefetch on free SMs.
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // Read tile tt's weight-side operands into registers, then hand its stage
+  // back to the copy engine.
+  TilePrep<MT> P;
+  auto prep = [&](int tt) -> bool {
+    const int st = tt % S;
+    if (!mbar_wait_bounded(&bars[st], (unsigned)((tt / S) & 1))) return false;
+    const uint8_t* base = ring + st * C::STAGE + g * C::SLOT;  // row g + 8i at base + 8i*SLOT
+#pragma unroll
+    for (int grp = 0; grp < 2; ++grp)
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const uint8_t* r = base + 16 * mt * C::SLOT + 16 + 32 * (2 * grp + jj) + 4 * t;
+          P.a[grp][jj][mt][0] = *reinterpret_cast<const uint32_t*>(r);
+          P.a[grp][jj][mt][1] = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT);
+          P.a[grp][jj][mt][2] = *reinterpret_cast<const uint32_t*>(r + 16);
+          P.a[grp][jj][mt][3] = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + 16);
+        }
+    const float qscale = (t & 1) ? 0.0625f : 1.0f;  // odd sub-blocks are high nibbles, carried as 16*q
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const uint4 hh = *reinterpret_cast<const uint4*>(base + 8 * i * C::SLOT);
+      const float dd = h2f((uint16_t)(hh.x & 0xffffu)) * qscale, dm = h2f((uint16_t)(hh.x >> 16));
+      const unsigned yb = (hh.y >> (8 * t)) & 0xffu, zb = (hh.z >> (8 * t)) & 0xffu, wb = (hh.w >> (8 * t)) & 0xffu;
+      // q4kScaleMin (simd.zig:211-219): sub-block t (< 4) and 4 + t
+      P.d1[0][i] = dd * (float)(yb & 63u);
+      P.m1[0][i] = dm * (float)(zb & 63u);
+      P.d1[1][i] = dd * (float)((wb & 15u) | ((yb >> 6) << 4));
+      P.m1[1][i] = dm * (float)((wb >> 4) | ((zb >> 6) << 4));
+    }
+    __syncwarp();
+    issue_next();  // this stage's bytes are in registers: refill it
+    return true;
+  };
+
   float inv = 1.f;
+  const int n4 = K / 128;
+  const bool early_x = norm_w == nullptr && n4 <= 2 * WARPS;
+  float4 xv0 = make_float4(0.f, 0.f, 0.f, 0.f), xv1 = xv0;
+  if (early_x) {  // the activation loads fly while the first tile is read out
+    if (warp < n4) xv0 = load_group(x, warp, lane, nullptr, 1.f);
+    if (warp + WARPS < n4) xv1 = load_group(x, warp + WARPS, lane, nullptr, 1.f);
+  }
+  bool ok = ntiles == 0 || prep(0);
   if (norm_w) {  // sum of squares of the whole row (every CTA; x is L2-resident)
     float ss = 0.f;
     for (int i = threadIdx.x; i < K / 4; i += WARPS * 32) {
@@ -204,100 +256,69 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
-    float t = 0.f;
-    for (int w = 0; w < WARPS; ++w) t += red[w];
-    inv = 1.0f / sqrtf(t / (float)K + eps);
+    float tsum = 0.f;
+    for (int w = 0; w < WARPS; ++w) tsum += red[w];
+    inv = 1.0f / sqrtf(tsum / (float)K + eps);
     __syncthreads();
   }
-  build_x_shared(x, K, xsh, warp, lane, WARPS, norm_w, inv);
+  if (early_x) {
+    if (warp < n4) convert_group(xv0, warp, lane, xsh);
+    if (warp + WARPS < n4) convert_group(xv1, warp + WARPS, lane, xsh);
+  } else {
+    build_x_shared(x, K, xsh, warp, lane, WARPS, norm_w, inv);
+  }
   __syncthreads();
 
   const int gs = g >> 1;                  // sub-block (within a group of 4) whose B columns this lane holds
   const int boff = (g & 1) * 32 + t * 8;  // limb g&1, quad t
-  const float qscale = (t & 1) ? 0.0625f : 1.0f;  // odd sub-blocks are high nibbles, carried as 16*q
-  bool ok = true;
 
   for (int ui = 0; ui < my_groups; ++ui) {
     const int u = (blockIdx.x + ui * gridDim.x) * slots + slot;
     const int r0 = u * C::ROWS, nr = max(0, min(C::ROWS, M - r0));
     float acc[NI] = {};  // rows g + 8i; this lane's sub-blocks t and 4+t
     for (int ci = 0; ci < my_chunks && ok; ++ci) {
-      const int tt = ui * my_chunks + ci, st = tt % S;
-      const int c = kpart + ksplit * ci, b0 = c * CHB, nblk = min(CHB, nb - b0);
-      if (!mbar_wait_bounded(&bars[st], (unsigned)((tt / S) & 1))) { ok = false; break; }
-      const uint8_t* base = ring + st * C::STAGE + g * C::SLOT;  // row g + 8i at base + 8i*SLOT
-      for (int bi = 0; bi < nblk; ++bi) {
-        const int sb = b0 + bi;
-        const uint8_t* blk = base + bi * C::BB;
-        uint4 hd[NI];
-        float dd[NI], dm[NI], nd[NI], nm[NI];
+      const int tt = ui * my_chunks + ci;
+      const int sb = kpart + (ci << kshift);
+#pragma unroll
+      for (int grp = 0; grp < 2; ++grp) {
+        const int8_t* xb = xsh.xq + (sb * 8 + 4 * grp + gs) * 128 + boff;
+        const uint2 bx = *reinterpret_cast<const uint2*>(xb);        // limb (g&1)
+        const uint2 bz = *reinterpret_cast<const uint2*>(xb + 64);   // limb 2 + (g&1)
+        int D[MT][4] = {};  // [m-tile][frag], limbs 0/1
+        int E[MT][4] = {};  // limbs 2/3
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {  // nibble pair 2 grp + jj: sub-blocks 2p (low), 2p+1 (high)
+          const bool mlo = gs == 2 * jj, mhi = gs == 2 * jj + 1;
+          const uint32_t bl0 = mlo ? bx.x : 0u, bl1 = mlo ? bx.y : 0u;
+          const uint32_t bh0 = mhi ? bx.x : 0u, bh1 = mhi ? bx.y : 0u;
+          const uint32_t zl0 = mlo ? bz.x : 0u, zl1 = mlo ? bz.y : 0u;
+          const uint32_t zh0 = mhi ? bz.x : 0u, zh1 = mhi ? bz.y : 0u;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const uint32_t* a = P.a[grp][jj][mt];
+            const uint32_t l0 = a[0] & 0x0F0F0F0Fu, l1 = a[1] & 0x0F0F0F0Fu, l2 = a[2] & 0x0F0F0F0Fu, l3 = a[3] & 0x0F0F0F0Fu;
+            const uint32_t h0 = a[0] & 0xF0F0F0F0u, h1 = a[1] & 0xF0F0F0F0u, h2 = a[2] & 0xF0F0F0F0u, h3 = a[3] & 0xF0F0F0F0u;
+            imma16832(D[mt], l0, l1, l2, l3, bl0, bl1);
+            imma16832(D[mt], h0, h1, h2, h3, bh0, bh1);
+            imma16832(E[mt], l0, l1, l2, l3, zl0, zl1);
+            imma16832(E[mt], h0, h1, h2, h3, zh0, zh1);
+          }
+        }
+        // D[mt][0..1]: row 16mt+g, limbs (L0, L1) of sub-block s = 4 grp + t; D[mt][2..3]: row 16mt+g+8.
+        const float2 xs = xsh.xs[sb * 8 + 4 * grp + t];
+        const float f = xs.x * (1.0f / 254.0f);
 #pragma unroll
         for (int i = 0; i < NI; ++i) {
-          hd[i] = *reinterpret_cast<const uint4*>(blk + 8 * i * C::SLOT);
-          dd[i] = h2f((uint16_t)(hd[i].x & 0xffffu));
-          dm[i] = h2f((uint16_t)(hd[i].x >> 16));
-          nd[i] = -dd[i] * 8388608.f;  // exact: power-of-two scaling of an f16 value
-          nm[i] = -dm[i] * 8388608.f;
-        }
-#pragma unroll
-        for (int grp = 0; grp < 2; ++grp) {
-          const int8_t* xb = xsh.xq + (sb * 8 + 4 * grp + gs) * 128 + boff;
-          const uint2 bx = *reinterpret_cast<const uint2*>(xb);        // limb (g&1)
-          const uint2 bz = *reinterpret_cast<const uint2*>(xb + 64);   // limb 2 + (g&1)
-          int D[MT][4] = {};  // [m-tile][frag], limbs 0/1
-          int E[MT][4] = {};  // limbs 2/3
-#pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const int p = 2 * grp + jj;  // nibble pair p: sub-blocks 2p (low), 2p+1 (high)
-            const bool mlo = gs == 2 * jj, mhi = gs == 2 * jj + 1;
-            const uint32_t bl0 = mlo ? bx.x : 0u, bl1 = mlo ? bx.y : 0u;
-            const uint32_t bh0 = mhi ? bx.x : 0u, bh1 = mhi ? bx.y : 0u;
-            const uint32_t zl0 = mlo ? bz.x : 0u, zl1 = mlo ? bz.y : 0u;
-            const uint32_t zh0 = mhi ? bz.x : 0u, zh1 = mhi ? bz.y : 0u;
-            const int q0 = 16 + 32 * p + 4 * t;
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-              const uint8_t* r = blk + 16 * mt * C::SLOT;
-              const uint32_t a0 = *reinterpret_cast<const uint32_t*>(r + q0);
-              const uint32_t a1 = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + q0);
-              const uint32_t a2 = *reinterpret_cast<const uint32_t*>(r + q0 + 16);
-              const uint32_t a3 = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + q0 + 16);
-              const uint32_t l0 = a0 & 0x0F0F0F0Fu, l1 = a1 & 0x0F0F0F0Fu, l2 = a2 & 0x0F0F0F0Fu, l3 = a3 & 0x0F0F0F0Fu;
-              const uint32_t h0 = a0 & 0xF0F0F0F0u, h1 = a1 & 0xF0F0F0F0u, h2 = a2 & 0xF0F0F0F0u, h3 = a3 & 0xF0F0F0F0u;
-              imma16832(D[mt], l0, l1, l2, l3, bl0, bl1);
-              imma16832(D[mt], h0, h1, h2, h3, bh0, bh1);
-              imma16832(E[mt], l0, l1, l2, l3, zl0, zl1);
-              imma16832(E[mt], h0, h1, h2, h3, zh0, zh1);
-            }
-          }
-          // D[mt][0..1]: row 16mt+g, limbs (L0, L1) of sub-block s = 4 grp + t; D[mt][2..3]: row 16mt+g+8.
-          const float2 xs = xsh.xs[sb * 8 + 4 * grp + t];
-          const float fx = xs.x * qscale;
-#pragma unroll
-          for (int i = 0; i < NI; ++i) {
-            const int mt = i >> 1, e = (i & 1) * 2;
-            // limbs combined exactly in int32 (|D0*254 + D1| < 2^27), then converted once
-            const float hi = (float)(D[mt][e] * 254 + D[mt][e + 1]);
-            const float lo = (float)(E[mt][e] * 254 + E[mt][e + 1]);
-            const float sq = (hi + lo * (1.0f / 64516.0f)) * (fx * (1.0f / 254.0f));  // sum_k q_k x_k
-            const uint4 hh = hd[i];
-            const unsigned yb = (hh.y >> (8 * t)) & 0xffu, zb = (hh.z >> (8 * t)) & 0xffu;
-            unsigned sc, mn;
-            if (grp == 0) {  // q4kScaleMin, s < 4
-              sc = yb & 63u; mn = zb & 63u;
-            } else {         // s >= 4
-              const unsigned wb = (hh.w >> (8 * t)) & 0xffu;
-              sc = (wb & 15u) | ((yb >> 6) << 4); mn = (wb >> 4) | ((zb >> 6) << 4);
-            }
-            // 6-bit sc/mn -> float exactly via the 2^23 magic (keeps the int->float unit free):
-          // d * sc = fma(d, 2^23 + sc, -d * 2^23)
-          const float fsc = __uint_as_float(0x4B000000u | sc), fmn = __uint_as_float(0x4B000000u | mn);
-          acc[i] += fmaf(dd[i], fsc, nd[i]) * sq - fmaf(dm[i], fmn, nm[i]) * xs.y;
-          }
+          const int mt = i >> 1, e = (i & 1) * 2;
+          // limbs combined exactly in int32 (|D0*254 + D1| < 2^27), then converted once
+          const float hi = (float)(D[mt][e] * 254 + D[mt][e + 1]);
+          const float lo = (float)(E[mt][e] * 254 + E[mt][e + 1]);
+          const float sq = fmaf(lo, 1.0f / 64516.0f, hi) * f;  // sum_k q_k x_k (16 q for high nibbles)
+          acc[i] = fmaf(P.d1[grp][i], sq, acc[i]);
+          acc[i] = fmaf(-P.m1[grp][i], xs.y, acc[i]);
         }
       }
-      __syncwarp();
-      if (tt + S < ntiles) issue(tt + S);
+      if (tt + 1 < ntiles && !prep(tt + 1)) ok = false;
     }
     // CTA reduction of the K-split partial sums for this unit's rows.
 #pragma unroll
@@ -310,7 +331,8 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
     __syncthreads();
     if (kpart == 0) {  // warp-uniform
       float v = 0.f;
-      for (int w = 0; w < min(ksplit, nch); ++w) v += red[(warp + w) * 32 + lane];
+      const int nk = min(ksplit, nch);
+      for (int w = 0; w < nk; ++w) v += red[(warp + w) * 32 + lane];
       if (swi) {
         // rows interleave as [gate 8 | up 8] blocks: lane i < 8 of each 16-row block holds
         // gate row i, lane i + 8 its up row; SwiGLU (math.zig:154-161) goes straight to h.

@@ -70,18 +70,9 @@ __device__ __forceinline__ void build_x_q6k(const float* __restrict__ x, int K, 
       const int e = (E == 0) ? 0 : (E - 127 - 5);  // max|x| * 2^-e in [32, 64)
       const float sx = __uint_as_float((uint32_t)(127 + e) << 23);
       const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
-      const float xv[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};
-      uint32_t lw[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float r = xv[c];
-#pragma unroll
-        for (int li = 0; li < 4; ++li) {
-          const float L = rintf(r);
-          lw[li] |= ((uint32_t)(int)L & 0xffu) << (8 * c);
-          r = (r - L) * 254.f;
-        }
-      }
+      float xv[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};
+      uint32_t lw[4];
+      limbs254(xv, lw);
       const int sb = f >> 2, t = f & 3, sbl = sb & 3;
 #pragma unroll
       for (int c = 0; c < 2; ++c)
