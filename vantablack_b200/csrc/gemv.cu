@@ -418,6 +418,10 @@ static cudaError_t launch_gemv_t(const void* w, const void* x, const float* dx, 
   return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w, x, dx, y, m, k, accumulate, pitch);
 }
 
+cudaError_t launch_gemv_q8_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                               int accumulate);
+static bool q8_mma_ok(const void* w, int k);
+
 // `pitch`: bytes between consecutive weight rows (0 = the dense row size).
 cudaError_t launch_gemv_pitched(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
                                 bool pdl, int accumulate, long long pitch) {
@@ -427,7 +431,9 @@ cudaError_t launch_gemv_pitched(int q, const void* w, const float* x, float* y, 
     case Q6_K:  // integer tensor cores when rows sit on 16-byte pitches
       if (q6k_mma_ok(w, k, pitch)) return launch_gemv_q6k_mma(w, x, y, m, k, st, pdl, accumulate, pitch);
       return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
-    case Q8_0: return launch_gemv_t<Q8_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
+    case Q8_0:  // integer tensor cores when rows sit on 16-byte pitches
+      if (pitch == host_row_bytes(Q8_0, k) && q8_mma_ok(w, k)) return launch_gemv_q8_mma(w, x, y, m, k, st, pdl, accumulate);
+      return launch_gemv_t<Q8_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
     case TQ2_0: return launch_gemv_t<TQ2_0, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
     default: return cudaErrorInvalidValue;
   }

@@ -48,6 +48,14 @@ __device__ __forceinline__ void imma16832(int* d, uint32_t a0, uint32_t a1, uint
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void imma_s8(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Shared layout of the activation vector, written once per CTA:
 //   xq[s] : 128 bytes per sub-block s = [limb c][lane-quad t][8 bytes]; the 8
 //           bytes are the B-fragment registers b0 (k = 4t..4t+3) and b1
@@ -233,6 +241,9 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
       P.d1[1][i] = dd * (float)((wb & 15u) | ((yb >> 6) << 4));
       P.m1[1][i] = dm * (float)((wb >> 4) | ((zb >> 6) << 4));
     }
+    // The refill is an async-proxy write into the bytes just read: order
+    // every lane's reads before it.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     issue_next();  // this stage's bytes are in registers: refill it
     return true;

@@ -4,6 +4,7 @@
 #include "gemv_q6k_mma.cu"
 #include "gemv.cu"
 #include "gemv_mma.cu"
+#include "gemv_q8_mma.cu"
 #include "quant_aux.cu"
 #include "gemm_tc.cu"
 #include "api.cu"
