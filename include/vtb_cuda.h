@@ -150,9 +150,9 @@ int vtb_cuda_gemm(int quant, const void *w, const float *acts, float *out, int64
  * resolves the array's address on the current device; make that first call
  * before any stream capture.  The address is kept for the life of the
  * process: after cudaDeviceReset (or in another primary context) it is stale,
- * so do not call this entry point again in that process.  The quantizer
- * rewrites every scratch byte the GEMV reads, so nothing carries over from
- * the previous call.  All calls share the one array: calls that can
+ * so do not call this entry point again in that process.  Every call rewrites
+ * the quantized activations before anything reads them, so nothing carries
+ * over from the previous call.  All calls share the one array: calls that can
  * overlap on the GPU (other streams, other host threads) race and must be
  * serialized by the caller.  Allocates nothing. */
 #define VTB_CUDA_NOALLOC_MAX_K 65536

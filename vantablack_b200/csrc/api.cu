@@ -20,6 +20,9 @@ cudaError_t launch_dequant(int q, const void* w, float* out, long long n, cudaSt
 cudaError_t launch_embed(int q, const void* table, const int32_t* ids, float* out, int dim, int n_tok,
                          cudaStream_t st);
 cudaError_t launch_quantize_q8_0(const float* x, int8_t* qs, float* d, int nblocks, cudaStream_t st);
+cudaError_t launch_gemv_q8_0_q8_0_x(const void* w, const float* x, int8_t* xq, float* dx, float* y, int m, int k,
+                                    cudaStream_t st, bool pdl, int accumulate);
+
 cudaError_t launch_q8_0_block_dots(const void* w, const int8_t* xq, int32_t* dots, int m, int nb, cudaStream_t st);
 cudaError_t launch_gemm_tc(int q, const void* w, const float* acts, float* out, int m, int k, int nb, bool precise,
                            void* ws, cudaStream_t st, float* part, size_t part_elems, long long pitch);
@@ -161,9 +164,7 @@ int vtb_cuda_gemv_q8_0_q8_0(const void* w, const float* x, float* y, int64_t m, 
   if (!x || !y || !xq_scratch || !dx_scratch) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null pointer");
   if (!aligned16(xq_scratch)) return set_err(VTB_CUDA_ERR_INVALID_ARG, "xq_scratch is not 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
-  cudaError_t e = launch_quantize_q8_0(x, xq_scratch, dx_scratch, (int)(k / 32), st);
-  if (e != cudaSuccess) return cuda_status(e);
-  return cuda_status(launch_gemv_q8_0_q8_0(w, xq_scratch, dx_scratch, y, (int)m, (int)k, st, pdl != 0));
+  return cuda_status(launch_gemv_q8_0_q8_0_x(w, x, xq_scratch, dx_scratch, y, (int)m, (int)k, st, pdl != 0, 0));
 }
 
 size_t vtb_cuda_gemm_workspace_bytes(int64_t k, int64_t n_tokens, int precise) {

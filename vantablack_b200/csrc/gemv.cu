@@ -449,4 +449,20 @@ cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* 
   return launch_gemv_t<Q8_0, 4, 4, 4, true>(w, xq, dx, y, m, k, st, pdl, accumulate);
 }
 
+cudaError_t launch_quantize_q8_0(const float* x, int8_t* qs, float* d, int nblocks, cudaStream_t st);
+cudaError_t launch_gemv_q8q8_mma(const void* w, const float* x, int8_t* xq, float* dx, float* y, int m, int k,
+                                 cudaStream_t st, bool pdl, int accumulate);
+
+// Q8_0 x Q8_0 from f32 x: x is quantized per 32-block into xq / dx (k int8 and
+// k/32 scales) and the GEMV takes the int8 dots.  On 16-byte row pitches one
+// tensor-core kernel does both (every CTA quantizes x itself; CTA 0 stores
+// xq / dx); otherwise the quantizer runs first and the SIMT GEMV reads xq / dx.
+cudaError_t launch_gemv_q8_0_q8_0_x(const void* w, const float* x, int8_t* xq, float* dx, float* y, int m, int k,
+                                    cudaStream_t st, bool pdl, int accumulate) {
+  if (q8_mma_ok(w, k)) return launch_gemv_q8q8_mma(w, x, xq, dx, y, m, k, st, pdl, accumulate);
+  cudaError_t e = launch_quantize_q8_0(x, xq, dx, k / 32, st);
+  if (e != cudaSuccess) return e;
+  return launch_gemv_t<Q8_0, 4, 4, 4, true>(w, xq, dx, y, m, k, st, pdl, accumulate);
+}
+
 }  // namespace vtb

@@ -16,16 +16,48 @@
 // loads with one byte permute.  Rows must sit on a 16-byte pitch, i.e.
 // k % 256 == 0.  A landed tile is read out into registers at once (A words
 // and the block scales), which frees its stage for the next copy.
+//
+// XQ = true is the Q8_0 x Q8_0 form (dot_i8, simd.zig:40-62): every CTA
+// quantizes x per 32-block with the rule of vtb_cuda_quantize_q8_0 (CTA 0
+// also stores the result in the caller's scratch), B holds one int8 column
+// per block of the chunk, one MMA per (16 rows, block) gives the exact int32
+// block dots, and y += (d_w * d_x) * dot.
 namespace vtb {
 
 constexpr int Q8M_ROWS = 16;
 constexpr int Q8M_RB = 272;  // 8 blocks x 34 B
 constexpr int Q8M_STAGE = Q8M_ROWS * Q8M_RB;
 
-template <int WARPS, int S>
+// Quantizes group gi of x (4 blocks of 32; this lane holds elements
+// 4*lane .. 4*lane+3) to Q8_0 with the rule of vtb_cuda_quantize_q8_0
+// (d = amax / 127, q = round(x * (1 / d)), IEEE division and rounding), into
+// the B-fragment layout: block b at b*32 bytes, lane quad t's 8 bytes =
+// k 4t..4t+3 | 16+4t..16+4t+3.  CTA 0 also writes qs and d to xq_out / dx_out.
+__device__ __forceinline__ void quantize_group_q8(float4 a, int gi, int lane, int8_t* xq, float* dxs,
+                                                  int8_t* __restrict__ xq_out, float* __restrict__ dx_out) {
+  const int part = lane & 7, b = gi * 4 + (lane >> 3);
+  float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float dd = __fdiv_rn(m, 127.0f);
+  const float id = dd != 0.f ? __fdiv_rn(1.0f, dd) : 0.f;
+  const uint32_t q0 = (uint32_t)(int)roundf(__fmul_rn(a.x, id)) & 0xffu;
+  const uint32_t q1 = (uint32_t)(int)roundf(__fmul_rn(a.y, id)) & 0xffu;
+  const uint32_t q2 = (uint32_t)(int)roundf(__fmul_rn(a.z, id)) & 0xffu;
+  const uint32_t q3 = (uint32_t)(int)roundf(__fmul_rn(a.w, id)) & 0xffu;
+  const uint32_t wq = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+  *reinterpret_cast<uint32_t*>(xq + b * 32 + (part & 3) * 8 + (part >> 2) * 4) = wq;
+  if (part == 0) dxs[b] = dd;
+  if (blockIdx.x == 0 && xq_out) {
+    *reinterpret_cast<uint32_t*>(xq_out + b * 32 + 4 * part) = wq;
+    if (part == 0) dx_out[b] = dd;
+  }
+}
+
+template <int WARPS, int S, bool XQ>
 __global__ void __launch_bounds__(WARPS * 32, 1)
-gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x, float* __restrict__ y, int M,
-                   int K, int ksplit, int accumulate) {
+gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x, int8_t* __restrict__ xqg,
+                   float* __restrict__ dxg, float* __restrict__ y, int M, int K, int ksplit, int accumulate) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -36,6 +68,7 @@ gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __rest
   XShared xsh;
   xsh.xq = reinterpret_cast<int8_t*>(red + WARPS * 32);
   xsh.xs = reinterpret_cast<float2*>(xsh.xq + 4 * K);
+  float* dxs = reinterpret_cast<float*>(xsh.xq + K);  // XQ: d_x per block after the k quants
 
   // Work split as in the Q4_K GEMV: 16-row units, ksplit (a power of two)
   // warps of a slot share a unit and split its K range by 256-weight chunks.
@@ -100,7 +133,7 @@ gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __rest
     }
 #pragma unroll
     for (int grp = 0; grp < 2; ++grp) {
-      const int b = 4 * grp + t;
+      const int b = XQ ? 2 * t + grp : 4 * grp + t;  // XQ: blocks 2t, 2t+1 (accumulator columns)
       dsc[grp][0] = h2f(*reinterpret_cast<const uint16_t*>(r0 + 34 * b));
       dsc[grp][1] = h2f(*reinterpret_cast<const uint16_t*>(r1 + 34 * b));
     }
@@ -112,6 +145,7 @@ gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __rest
     return true;
   };
 
+  bool ok;
   const int n4 = K / 128;
   const bool early_x = n4 <= 2 * WARPS;
   float4 xv0 = make_float4(0.f, 0.f, 0.f, 0.f), xv1 = xv0;
@@ -119,12 +153,22 @@ gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __rest
     if (warp < n4) xv0 = load_group(x, warp, lane, nullptr, 1.f);
     if (warp + WARPS < n4) xv1 = load_group(x, warp + WARPS, lane, nullptr, 1.f);
   }
-  bool ok = ntiles == 0 || prep(0);
-  if (early_x) {
-    if (warp < n4) convert_group(xv0, warp, lane, xsh);
-    if (warp + WARPS < n4) convert_group(xv1, warp + WARPS, lane, xsh);
+  ok = ntiles == 0 || prep(0);
+  if constexpr (XQ) {
+    if (early_x) {
+      if (warp < n4) quantize_group_q8(xv0, warp, lane, xsh.xq, dxs, xqg, dxg);
+      if (warp + WARPS < n4) quantize_group_q8(xv1, warp + WARPS, lane, xsh.xq, dxs, xqg, dxg);
+    } else {
+      for (int gi = warp; gi < n4; gi += WARPS)
+        quantize_group_q8(load_group(x, gi, lane, nullptr, 1.f), gi, lane, xsh.xq, dxs, xqg, dxg);
+    }
   } else {
-    build_x_shared(x, K, xsh, warp, lane, WARPS, nullptr, 1.f);
+    if (early_x) {
+      if (warp < n4) convert_group(xv0, warp, lane, xsh);
+      if (warp + WARPS < n4) convert_group(xv1, warp + WARPS, lane, xsh);
+    } else {
+      build_x_shared(x, K, xsh, warp, lane, WARPS, nullptr, 1.f);
+    }
   }
   __syncthreads();
 
@@ -138,6 +182,22 @@ gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __rest
     for (int ci = 0; ci < my_chunks && ok; ++ci) {
       const int tt = ui * my_chunks + ci;
       const int cb = (kpart + (ci << kshift)) * 8;  // first block of the chunk
+      if constexpr (XQ) {
+        // column g = block cb + g; this lane's accumulators are blocks cb + 2t, cb + 2t + 1
+        const uint2 bc = *reinterpret_cast<const uint2*>(xsh.xq + (cb + g) * 32 + 8 * t);
+        int D[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+          const bool on = g == b;
+          imma_s8(D, A[b][0], A[b][1], A[b][2], A[b][3], on ? bc.x : 0u, on ? bc.y : 0u);
+        }
+        const float dx0 = dxs[cb + 2 * t], dx1 = dxs[cb + 2 * t + 1];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          acc[i] = fmaf(dsc[0][i] * dx0, (float)D[2 * i], acc[i]);
+          acc[i] = fmaf(dsc[1][i] * dx1, (float)D[2 * i + 1], acc[i]);
+        }
+      } else {
 #pragma unroll
       for (int grp = 0; grp < 2; ++grp) {
         const int8_t* xb = xsh.xq + (cb + 4 * grp + gs) * 128 + boff;
@@ -160,6 +220,7 @@ gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __rest
           const float lo = (float)(E[2 * i] * 254 + E[2 * i + 1]);
           acc[i] = fmaf(dsc[grp][i], fmaf(lo, 1.0f / 64516.0f, hi) * f, acc[i]);
         }
+      }
       }
       if (tt + 1 < ntiles && !prep(tt + 1)) ok = false;
     }
@@ -191,10 +252,10 @@ static bool q8_mma_ok(const void* w, int k) {
   return (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && k % 256 == 0 && q8_mma_smem<16, 1>(k) <= 227 * 1024;
 }
 
-template <int WARPS, int S>
-static cudaError_t launch_q8_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                   int accumulate) {
-  constexpr auto kern = gemv_q8_mma_kernel<WARPS, S>;
+template <int WARPS, int S, bool XQ>
+static cudaError_t launch_q8_mma_t(const void* w, const float* x, int8_t* xq, float* dx, float* y, int m,
+                                   int k, cudaStream_t st, bool pdl, int accumulate) {
+  constexpr auto kern = gemv_q8_mma_kernel<WARPS, S, XQ>;
   const int smem = q8_mma_smem<WARPS, S>(k);
   const uint64_t rbytes = (uint64_t)(k / 32) * 34;
   CUtensorMap wmap;
@@ -218,15 +279,24 @@ static cudaError_t launch_q8_mma_t(const void* w, const float* x, float* y, int 
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, wmap, x, y, m, k, ksplit, accumulate);
+  return cudaLaunchKernelEx(&cfg, kern, wmap, x, xq, dx, y, m, k, ksplit, accumulate);
 }
 
 // Two stages per warp for matrices above 2^24 weights when they fit, else one.
 cudaError_t launch_gemv_q8_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                int accumulate) {
   if ((long long)m * k > (1LL << 24) && q8_mma_smem<16, 2>(k) <= 227 * 1024)
-    return launch_q8_mma_t<16, 2>(w, x, y, m, k, st, pdl, accumulate);
-  return launch_q8_mma_t<16, 1>(w, x, y, m, k, st, pdl, accumulate);
+    return launch_q8_mma_t<16, 2, false>(w, x, nullptr, nullptr, y, m, k, st, pdl, accumulate);
+  return launch_q8_mma_t<16, 1, false>(w, x, nullptr, nullptr, y, m, k, st, pdl, accumulate);
+}
+
+// Q8_0 x Q8_0 in one launch: x (f32) is quantized inside the GEMV; the
+// quantized x (k int8) and its scales (k/32) are also written to xq / dx.
+cudaError_t launch_gemv_q8q8_mma(const void* w, const float* x, int8_t* xq, float* dx, float* y, int m, int k,
+                                 cudaStream_t st, bool pdl, int accumulate) {
+  if ((long long)m * k > (1LL << 24) && q8_mma_smem<16, 2>(k) <= 227 * 1024)
+    return launch_q8_mma_t<16, 2, true>(w, x, xq, dx, y, m, k, st, pdl, accumulate);
+  return launch_q8_mma_t<16, 1, true>(w, x, xq, dx, y, m, k, st, pdl, accumulate);
 }
 
 }  // namespace vtb

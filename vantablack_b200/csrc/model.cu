@@ -53,6 +53,9 @@ __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ t, l
 cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* dx, float* y, int m, int k,
                                   cudaStream_t st, bool pdl, int accumulate);
 cudaError_t launch_quantize_q8_0(const float* x, int8_t* qs, float* d, int nblocks, cudaStream_t st);
+cudaError_t launch_gemv_q8_0_q8_0_x(const void* w, const float* x, int8_t* xq, float* dx, float* y, int m, int k,
+                                    cudaStream_t st, bool pdl, int accumulate);
+
 
 // `pitch`: bytes between weight rows (0 = dense; only Q6_K rows are ever padded).
 static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
@@ -1310,9 +1313,7 @@ static cudaError_t gemv_row(VtbCudaState* s, int q, const void* w, const float* 
   if (s->q8_act && q == Q8_0) {
     int8_t* xq = static_cast<int8_t*>(s->ws);
     float* dx = reinterpret_cast<float*>(static_cast<char*>(s->ws) + (((size_t)k + 15) & ~size_t(15)));
-    cudaError_t e = launch_quantize_q8_0(x, xq, dx, k / 32, s->st);
-    if (e) return e;
-    return launch_gemv_q8_0_q8_0(w, xq, dx, y, m, k, s->st, true, acc);
+    return launch_gemv_q8_0_q8_0_x(w, x, xq, dx, y, m, k, s->st, true, acc);
   }
   return gemv_any(q, w, x, y, m, k, s->st, acc, pitch);
 }

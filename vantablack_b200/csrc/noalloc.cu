@@ -57,10 +57,9 @@ extern "C" int vtb_cuda_gemv_q8_0_q8_0_noalloc(const void* w, const float* x, fl
   }
   int8_t* xq = reinterpret_cast<int8_t*>(base);
   float* dx = reinterpret_cast<float*>(base + VTB_CUDA_NOALLOC_MAX_K);
-  // The quantizer writes every scratch byte the GEMV then reads (k quants and
-  // k/32 scales), so nothing has to be cleared between calls.
+  // Every call rewrites the k quants and k/32 scales before anything reads
+  // them (the tensor-core path quantizes inside the GEMV and stores them; the
+  // SIMT path runs the quantizer first), so nothing has to be cleared.
   cudaStream_t st = (cudaStream_t)stream;
-  e = launch_quantize_q8_0(x, xq, dx, (int)(k / 32), st);
-  if (e != cudaSuccess) return cuda_status(e);
-  return cuda_status(launch_gemv_q8_0_q8_0(w, xq, dx, y, (int)m, (int)k, st, pdl != 0));
+  return cuda_status(launch_gemv_q8_0_q8_0_x(w, x, xq, dx, y, (int)m, (int)k, st, pdl != 0, 0));
 }
