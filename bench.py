@@ -10,7 +10,7 @@ decode chain.  `e2e` is the same metric through the C-ABI context API with
 host buffers (x copied H2D from pinned memory, every y read back D2H).
 
 The same line carries, under `workloads`:
-  * gemv_sweep   -- Q6_K, Q8_0 and Q8_0xQ8_0 GEMVs at the Llama-3-8B decode
+  * gemv_sweep   -- Q6_K, Q8_0, Q8_0xQ8_0 and Q5_K GEMVs at the Llama-3-8B decode
                     shapes (GB/s, roofline fraction, oracle parity on sampled
                     rows, the oracle's GB/s on the host cores);
   * prefill_gemm -- the batched prefill GEMM (prefill.zig:325-378) for Q4_K
@@ -52,7 +52,7 @@ sys.path.insert(0, ROOT)
 
 M, K = 5632, 2048
 N_COPIES = 64
-Q8_0, Q4_K, Q6_K = 8, 12, 14
+Q8_0, Q4_K, Q5_K, Q6_K = 8, 12, 13, 14
 W_BYTES = M * (K // 256) * 144
 ALG_BYTES = W_BYTES + 4 * K + 4 * M  # per GEMV: W + x + y = 6,518,784 B
 METRIC = "Q4_K GEMV HBM GB/s (TinyLlama ffn_up 5632x2048, batch 1)"
@@ -235,8 +235,8 @@ def time_graph(build, replays: int, stream):
 
 
 def gemv_sweep(dev, hbm: float, cpu_threads: int) -> dict:
-    """Q6_K / Q8_0 / Q8_0xQ8_0 GEMVs at the Llama-3-8B decode shapes
-    (simd.zig:159-190, 406-434; dot_i8 :40-62 for the int8 variant), each a PDL
+    """Q6_K / Q8_0 / Q8_0xQ8_0 / Q5_K GEMVs at the Llama-3-8B decode shapes
+    (simd.zig:159-190, 406-434, 290-347; dot_i8 :40-62 for the int8 variant), each a PDL
     chain over distinct weight copies totalling > 4x L2.  The weights are one
     seeded buffer per format (the largest shape's; smaller shapes use a prefix,
     which is whole blocks), copied on the device."""
@@ -248,7 +248,7 @@ def gemv_sweep(dev, hbm: float, cpu_threads: int) -> dict:
     stream = torch.cuda.Stream(device=dev)
     O.set_threads(cpu_threads)
     out = {}
-    for quant, name in ((Q6_K, "q6_k"), (Q8_0, "q8_0"), (-1, "q8_0xq8_0")):
+    for quant, name in ((Q6_K, "q6_k"), (Q8_0, "q8_0"), (-1, "q8_0xq8_0"), (Q5_K, "q5_k")):
         q = Q8_0 if quant < 0 else quant
         if quant != -1:
             host = S.quant_tensor(rng, q, 128256, 4096)

@@ -421,13 +421,18 @@ static cudaError_t launch_gemv_t(const void* w, const void* x, const float* dx, 
 cudaError_t launch_gemv_q8_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                int accumulate);
 static bool q8_mma_ok(const void* w, int k);
+cudaError_t launch_gemv_q5k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                                int accumulate);
 
 // `pitch`: bytes between consecutive weight rows (0 = the dense row size).
 cudaError_t launch_gemv_pitched(int q, const void* w, const float* x, float* y, int m, int k, cudaStream_t st,
                                 bool pdl, int accumulate, long long pitch) {
   if (pitch == 0) pitch = host_row_bytes(q, k);
   switch (q) {
-    case Q5_K: return launch_gemv_t<Q5_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
+    case Q5_K:  // integer tensor cores on dense, 16-byte aligned rows
+      if (pitch == host_row_bytes(Q5_K, k) && (reinterpret_cast<uintptr_t>(w) & 15u) == 0)
+        return launch_gemv_q5k_mma(w, x, y, m, k, st, pdl, accumulate);
+      return launch_gemv_t<Q5_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);
     case Q6_K:  // integer tensor cores when rows sit on 16-byte pitches
       if (q6k_mma_ok(w, k, pitch)) return launch_gemv_q6k_mma(w, x, y, m, k, st, pdl, accumulate, pitch);
       return launch_gemv_t<Q6_K, 4, 4, 4>(w, x, nullptr, y, m, k, st, pdl, accumulate, pitch);

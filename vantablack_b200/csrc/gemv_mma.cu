@@ -133,14 +133,25 @@ __device__ __forceinline__ void build_x_shared(const float* __restrict__ x, int 
 // Per-row copies of a few hundred bytes capped the stream near 5 TB/s on their
 // issue rate alone; one box per tile moves the same bytes with 32x fewer copy
 // operations.
-template <int CHB, bool TM, int ROWS_ = 32>
+//
+// Q5_K (176 B: d, dmin, 12 scale bytes, qh[32], qs[128]) runs the same kernel:
+// its sub-block values q + 16 * (bit s of qh[l]) (simd.zig:290-319) are
+// assembled per A word from the nibbles and the qh bits, and fit u8 as they are.
+template <int Q, int ROWS_ = 32>
 struct MmaQ4K {
   static constexpr int ROWS = ROWS_;  // 32 (two m16 MMA tiles per warp tile) or 16 (one)
-  static constexpr int BB = 144;
+  static constexpr int BB = Q == Q5_K ? 176 : 144;
+  static constexpr int QS = Q == Q5_K ? 48 : 16;  // offset of qs[] in the block
   static constexpr int SLOT = BB;
   static constexpr int STAGE = ROWS * SLOT;
-  static_assert(TM && CHB == 1, "tiles are 2-D TMA boxes of one super-block per row");
+  static_assert(Q == Q4_K || Q == Q5_K, "Q4_K / Q5_K super-blocks");
 };
+
+// Bit s of each byte of v moved to bit 4 (the qh bit of Q5_K, worth 16).
+// (sh is a constant once the loops over sub-blocks are unrolled.)
+__device__ __forceinline__ uint32_t qh_bit4(uint32_t v, int sh) {
+  return (sh <= 4 ? (v << (4 - sh)) : (v >> (sh - 4))) & 0x10101010u;
+}
 
 // A tile's weight-side operands, read out of shared memory before the
 // activations are needed: the MMA A fragments (raw nibble words) and, per
@@ -149,14 +160,15 @@ struct MmaQ4K {
 template <int MT>
 struct TilePrep {
   uint32_t a[2][2][MT][4];  // [group][pair in group][m-tile][a0..a3]
+  uint32_t h[MT][4];        // Q5_K: qh words at the same rows / k positions
   float d1[2][2 * MT], m1[2][2 * MT];
 };
 
-template <int WARPS, int S, int CHB, bool TM, int ROWS>
+template <int WARPS, int S, int Q, int ROWS>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
                     int ksplit, int accumulate, const float* __restrict__ norm_w, float eps, float* __restrict__ swi) {
-  using C = MmaQ4K<CHB, TM, ROWS>;
+  using C = MmaQ4K<Q, ROWS>;
   constexpr int MT = ROWS / 16, NI = 2 * MT;  // m16 tiles; rows g + 8i this lane holds
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -223,13 +235,24 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
       for (int jj = 0; jj < 2; ++jj)
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-          const uint8_t* r = base + 16 * mt * C::SLOT + 16 + 32 * (2 * grp + jj) + 4 * t;
+          const uint8_t* r = base + 16 * mt * C::SLOT + C::QS + 32 * (2 * grp + jj) + 4 * t;
           P.a[grp][jj][mt][0] = *reinterpret_cast<const uint32_t*>(r);
           P.a[grp][jj][mt][1] = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT);
           P.a[grp][jj][mt][2] = *reinterpret_cast<const uint32_t*>(r + 16);
           P.a[grp][jj][mt][3] = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + 16);
         }
-    const float qscale = (t & 1) ? 0.0625f : 1.0f;  // odd sub-blocks are high nibbles, carried as 16*q
+    if constexpr (Q == Q5_K) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint8_t* r = base + 16 * mt * C::SLOT + 16 + 4 * t;  // qh[4t], qh[16 + 4t]
+        P.h[mt][0] = *reinterpret_cast<const uint32_t*>(r);
+        P.h[mt][1] = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT);
+        P.h[mt][2] = *reinterpret_cast<const uint32_t*>(r + 16);
+        P.h[mt][3] = *reinterpret_cast<const uint32_t*>(r + 8 * C::SLOT + 16);
+      }
+    }
+    // Q4_K: odd sub-blocks are high nibbles, carried in place as 16*q
+    const float qscale = (Q == Q4_K && (t & 1)) ? 0.0625f : 1.0f;
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
       const uint4 hh = *reinterpret_cast<const uint4*>(base + 8 * i * C::SLOT);
@@ -307,8 +330,18 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             const uint32_t* a = P.a[grp][jj][mt];
-            const uint32_t l0 = a[0] & 0x0F0F0F0Fu, l1 = a[1] & 0x0F0F0F0Fu, l2 = a[2] & 0x0F0F0F0Fu, l3 = a[3] & 0x0F0F0F0Fu;
-            const uint32_t h0 = a[0] & 0xF0F0F0F0u, h1 = a[1] & 0xF0F0F0F0u, h2 = a[2] & 0xF0F0F0F0u, h3 = a[3] & 0xF0F0F0F0u;
+            uint32_t l0, l1, l2, l3, h0, h1, h2, h3;
+            if constexpr (Q == Q5_K) {  // q + 16 * bit (2p | 2p+1) of qh[l]
+              const uint32_t* hq = P.h[mt];
+              const int SL = 2 * (2 * grp + jj), SHI = SL + 1;
+              l0 = (a[0] & 0x0F0F0F0Fu) | qh_bit4(hq[0], SL); l1 = (a[1] & 0x0F0F0F0Fu) | qh_bit4(hq[1], SL);
+              l2 = (a[2] & 0x0F0F0F0Fu) | qh_bit4(hq[2], SL); l3 = (a[3] & 0x0F0F0F0Fu) | qh_bit4(hq[3], SL);
+              h0 = ((a[0] >> 4) & 0x0F0F0F0Fu) | qh_bit4(hq[0], SHI); h1 = ((a[1] >> 4) & 0x0F0F0F0Fu) | qh_bit4(hq[1], SHI);
+              h2 = ((a[2] >> 4) & 0x0F0F0F0Fu) | qh_bit4(hq[2], SHI); h3 = ((a[3] >> 4) & 0x0F0F0F0Fu) | qh_bit4(hq[3], SHI);
+            } else {
+              l0 = a[0] & 0x0F0F0F0Fu; l1 = a[1] & 0x0F0F0F0Fu; l2 = a[2] & 0x0F0F0F0Fu; l3 = a[3] & 0x0F0F0F0Fu;
+              h0 = a[0] & 0xF0F0F0F0u; h1 = a[1] & 0xF0F0F0F0u; h2 = a[2] & 0xF0F0F0F0u; h3 = a[3] & 0xF0F0F0F0u;
+            }
             imma16832(D[mt], l0, l1, l2, l3, bl0, bl1);
             imma16832(D[mt], h0, h1, h2, h3, bh0, bh1);
             imma16832(E[mt], l0, l1, l2, l3, zl0, zl1);
@@ -361,25 +394,23 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
   }
 }
 
-template <int WARPS, int S, int CHB, bool TM, int ROWS = 32>
+template <int WARPS, int S, int Q, int ROWS = 32>
 constexpr int q4k_mma_smem(int k) {
-  return WARPS * S * MmaQ4K<CHB, TM, ROWS>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
+  return WARPS * S * MmaQ4K<Q, ROWS>::STAGE + WARPS * S * 8 + WARPS * 128 + k * 4 + (k / 32) * 8;
 }
 
-template <int WARPS, int S, int CHB, bool TM, int ROWS>
+template <int WARPS, int S, int Q, int ROWS>
 static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
                                     int accumulate, const float* norm_w, float eps, float* swi) {
-  using C = MmaQ4K<CHB, TM, ROWS>;
-  constexpr auto kern = gemv_q4k_mma_kernel<WARPS, S, CHB, TM, ROWS>;
-  const int smem = q4k_mma_smem<WARPS, S, CHB, TM, ROWS>(k);
+  using C = MmaQ4K<Q, ROWS>;
+  constexpr auto kern = gemv_q4k_mma_kernel<WARPS, S, Q, ROWS>;
+  const int smem = q4k_mma_smem<WARPS, S, Q, ROWS>(k);
   CUtensorMap wmap;
-  memset(&wmap, 0, sizeof wmap);
-  if (TM) {  // [m rows][k/256 * 36 u32]: one box = ROWS rows x 144 B
-    const uint64_t rbytes = (uint64_t)(k / 256) * 144;
-    if (!make_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, rbytes / 4, (uint64_t)m, rbytes, 36, ROWS,
-                   CU_TENSOR_MAP_SWIZZLE_NONE))
-      return cudaErrorInvalidValue;
-  }
+  // [m rows][k/256 * BB/4 u32]: one box = ROWS rows x one super-block
+  const uint64_t rbytes = (uint64_t)(k / 256) * C::BB;
+  if (!make_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, rbytes / 4, (uint64_t)m, rbytes, C::BB / 4, ROWS,
+                 CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   const int dev = current_device();
   cudaError_t ea = ensure_smem_attr<kern>(dev, 227 * 1024);
@@ -387,7 +418,7 @@ static cudaError_t launch_q4k_mma_t(const void* w, const float* x, float* y, int
   // occupancy depends on k through the shared x buffer
   const int sms = sm_count(dev), per_sm = ctas_per_sm<kern>(dev, WARPS * 32, smem);
   const int units = (m + C::ROWS - 1) / C::ROWS;
-  const int nch = (k / 256 + CHB - 1) / CHB;
+  const int nch = k / 256;
   const int cap = sms * per_sm;
   int ksplit = pick_ksplit(units, nch, WARPS, cap);
   const int groups = (units + WARPS / ksplit - 1) / (WARPS / ksplit);
@@ -416,24 +447,37 @@ static double q4k_tile_cost(int m, int k, int rows, int warps, int cap) {
   return (double)(rounds * ((nch + ks - 1) / ks)) * (rows == 16 ? 0.6 : 1.0);
 }
 
-// swi non-null: W's rows are [gate 8 | up 8] blocks (m % 16 == 0) and the
-// output is SwiGLU's h[m/2] in swi instead of y.
-cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
-                                int accumulate, const float* norm_w = nullptr, float eps = 0.f, float* swi = nullptr) {
+template <int Q>
+static cudaError_t launch_kq_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                                 int accumulate, const float* norm_w, float eps, float* swi) {
   // One 2-D TMA box per tile.  Matrices above 2^24 weights stream with two
   // stages per warp; smaller ones (dominated by the dependent-launch chain)
   // with one.  Very long rows (x staged in shared memory at 4.25 B per column)
   // fall back to 8 warps.  The row-tile height (32 or 16) is the one whose
   // launch balances better over the SMs.
-  if (q4k_mma_smem<16, 2, 1, true>(k) > 227 * 1024)
-    return launch_q4k_mma_t<8, 2, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
+  if (q4k_mma_smem<16, 2, Q>(k) > 227 * 1024)
+    return launch_q4k_mma_t<8, 2, Q, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
   const int sms = sm_count(current_device());
   const bool r16 = q4k_tile_cost(m, k, 16, 16, sms) < q4k_tile_cost(m, k, 32, 16, sms);
   if ((long long)m * k > (1LL << 24))
-    return r16 ? launch_q4k_mma_t<16, 2, 1, true, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi)
-               : launch_q4k_mma_t<16, 2, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
-  return r16 ? launch_q4k_mma_t<16, 1, 1, true, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi)
-             : launch_q4k_mma_t<16, 1, 1, true, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
+    return r16 ? launch_q4k_mma_t<16, 2, Q, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi)
+               : launch_q4k_mma_t<16, 2, Q, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
+  return r16 ? launch_q4k_mma_t<16, 1, Q, 16>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi)
+             : launch_q4k_mma_t<16, 1, Q, 32>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
+}
+
+// swi non-null: W's rows are [gate 8 | up 8] blocks (m % 16 == 0) and the
+// output is SwiGLU's h[m/2] in swi instead of y.
+cudaError_t launch_gemv_q4k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                                int accumulate, const float* norm_w = nullptr, float eps = 0.f, float* swi = nullptr) {
+  return launch_kq_mma<Q4_K>(w, x, y, m, k, st, pdl, accumulate, norm_w, eps, swi);
+}
+
+// Q5_K on the same kernel; rows must be 16-byte aligned (176 B super-blocks
+// keep every row pitch a multiple of 16).
+cudaError_t launch_gemv_q5k_mma(const void* w, const float* x, float* y, int m, int k, cudaStream_t st, bool pdl,
+                                int accumulate) {
+  return launch_kq_mma<Q5_K>(w, x, y, m, k, st, pdl, accumulate, nullptr, 0.f, nullptr);
 }
 
 }  // namespace vtb
