@@ -207,6 +207,40 @@ int vtb_cuda_matmul_q6_k(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf
 int vtb_cuda_matmul_tq2_0(VtbCudaCtx *ctx, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
                           VtbCudaBuf *acts_buf, size_t m, size_t k);
 
+/* Batched dispatch (vtb_metal_segment_*, bridge.h:72-183).  Operations
+ * enqueued into a segment are recorded on the host; commit launches them as
+ * one CUDA graph on the context stream without waiting (vtb_cuda_wait_idle
+ * drains, as vtb_metal_wait_idle does).  The context keeps the graphs of the
+ * last 8 distinct operation lists, so re-committing the same list (same
+ * buffers, offsets and shapes, as a decode loop does every token) is one
+ * graph launch.  One segment per context is open at a time; begin returns it
+ * (NULL on a bad context).  Enqueue functions return nothing: the first bad
+ * argument is reported by commit (and the segment is dropped).  Matmul
+ * weights and activations must be 16-byte aligned.  Host buffers of the copy
+ * functions should be pinned; with pageable memory commit runs the list
+ * eagerly instead of as a graph.  The buffers a committed segment uses must
+ * stay alive until it has finished. */
+typedef struct VtbCudaSeg VtbCudaSeg;
+VtbCudaSeg *vtb_cuda_segment_begin(VtbCudaCtx *ctx);
+int vtb_cuda_segment_commit(VtbCudaSeg *seg);
+void vtb_cuda_segment_matmul_q8_0(VtbCudaSeg *seg, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                                  VtbCudaBuf *acts_buf, size_t m, size_t k);
+void vtb_cuda_segment_matmul_q4_k(VtbCudaSeg *seg, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                                  VtbCudaBuf *acts_buf, size_t m, size_t k);
+void vtb_cuda_segment_matmul_q5_k(VtbCudaSeg *seg, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                                  VtbCudaBuf *acts_buf, size_t m, size_t k);
+void vtb_cuda_segment_matmul_q6_k(VtbCudaSeg *seg, VtbCudaBuf *out_buf, VtbCudaBuf *w_buf, size_t w_offset,
+                                  VtbCudaBuf *acts_buf, size_t m, size_t k);
+/* f32 copy dst[dst_off..] = src[src_off..], n_floats values, byte offsets 4-aligned
+ * (vtb_metal_segment_copy). */
+void vtb_cuda_segment_copy(VtbCudaSeg *seg, VtbCudaBuf *dst_buf, size_t dst_offset_bytes, VtbCudaBuf *src_buf,
+                           size_t src_offset_bytes, size_t n_floats);
+/* Host <-> device copies inside a segment (Metal buffers are host-visible;
+ * CUDA device buffers are not, so inputs go in and results come back here). */
+void vtb_cuda_segment_copy_h2d(VtbCudaSeg *seg, VtbCudaBuf *dst_buf, size_t dst_offset, const void *host_src,
+                               size_t bytes);
+void vtb_cuda_segment_copy_d2h(VtbCudaSeg *seg, void *host_dst, VtbCudaBuf *src_buf, size_t src_offset, size_t bytes);
+
 /* ------------------------------------------------------------------ */
 /* Llama forward loop (the backend vtable, src/runtime/backend.zig:67-97) */
 /* ------------------------------------------------------------------ */

@@ -200,3 +200,66 @@ def test_gemv_activation_ranges(q, kind):
         x[: k // 2] = 0.0
     y = ops().gemv(q, torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda(), m, k).cpu().numpy()
     assert rel_err(y, O.matmul(q, w, x, m, k)) <= TOL
+
+
+def test_segment_graph_matches_one_shot():
+    """Segments (vtb_metal_segment_* counterpart, bridge.h:72-183): a chain of
+    matmuls of every K-quant plus a device copy, with host input and read-back
+    inside the segment, equals the same one-shot calls bit for bit; committing
+    the same list again replays the cached graph with new host data; a bad
+    argument is reported by commit."""
+    import torch
+    from vantablack_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(21)
+    n = 2048
+    quants = [(S.Q4_K, "q4_k"), (S.Q6_K, "q6_k"), (S.Q5_K, "q5_k"), (S.Q8_0, "q8_0")]
+    ws = [S.quant_tensor(rng, q, n, n) for q, _ in quants]
+    ctx = lib.vtb_cuda_init(0)
+    wb = [lib.vtb_cuda_upload(ctx, w.ctypes.data, w.nbytes) for w in ws]
+    bufs = [lib.vtb_cuda_alloc(ctx, n * 4, None) for _ in range(5)]
+    hx = torch.empty(n, dtype=torch.float32).pin_memory()
+    hy = torch.empty(len(quants) + 2, n, dtype=torch.float32).pin_memory()
+
+    def one_shot(x):
+        _lib.check(lib.vtb_cuda_copy_h2d(ctx, bufs[0], 0, x.ctypes.data, n * 4), "h2d")
+        for i, (q, name) in enumerate(quants):
+            _lib.check(getattr(lib, f"vtb_cuda_matmul_{name}")(ctx, bufs[i + 1], wb[i], 0, bufs[i], n, n), "mm")
+        out = [np.empty(n, np.float32) for _ in range(len(quants))]
+        for i, y in enumerate(out):
+            _lib.check(lib.vtb_cuda_copy_d2h(ctx, y.ctypes.data, bufs[i + 1], 0, n * 4), "d2h")
+        return out
+
+    def segment(x):
+        hx.copy_(torch.from_numpy(x))
+        seg = lib.vtb_cuda_segment_begin(ctx)
+        assert seg
+        lib.vtb_cuda_segment_copy_h2d(seg, bufs[0], 0, hx.data_ptr(), n * 4)
+        # read back before a later copy of the same segment overwrites bufs[0]
+        lib.vtb_cuda_segment_copy_d2h(seg, hy[len(quants) + 1].data_ptr(), bufs[0], 0, n * 4)
+        for i, (q, name) in enumerate(quants):
+            getattr(lib, f"vtb_cuda_segment_matmul_{name}")(seg, bufs[i + 1], wb[i], 0, bufs[i], n, n)
+            lib.vtb_cuda_segment_copy_d2h(seg, hy[i].data_ptr(), bufs[i + 1], 0, n * 4)
+        lib.vtb_cuda_segment_copy(seg, bufs[0], 0, bufs[2], 0, n)  # overwrites the chain's input
+        lib.vtb_cuda_segment_copy_d2h(seg, hy[len(quants)].data_ptr(), bufs[0], 0, n * 4)
+        _lib.check(lib.vtb_cuda_segment_commit(seg), "commit")
+        _lib.check(lib.vtb_cuda_wait_idle(ctx), "wait")
+        return [hy[i].numpy().copy() for i in range(len(quants) + 2)]
+
+    for trial in range(3):  # the second and third commits replay the cached graph
+        x = S.activations(rng, n)
+        ref = one_shot(x)
+        got = segment(x)
+        for a, b in zip(ref, got):
+            assert np.array_equal(a, b)
+        assert np.array_equal(got[len(quants)], ref[1])
+        assert np.array_equal(got[len(quants) + 1], x)
+        assert rel_err(ref[0], O.matmul(S.Q4_K, ws[0], x, n, n)) <= TOL
+    seg = lib.vtb_cuda_segment_begin(ctx)
+    lib.vtb_cuda_segment_matmul_q4_k(seg, bufs[1], wb[0], 0, bufs[0], n + 1, n)  # beyond the weights
+    assert lib.vtb_cuda_segment_commit(seg) == -1
+    assert lib.vtb_cuda_segment_commit(seg) == -1  # nothing open any more
+    _lib.check(lib.vtb_cuda_check_device_error(), "device error word")
+    for b in wb + bufs:
+        lib.vtb_cuda_release(b)
+    lib.vtb_cuda_destroy(ctx)

@@ -56,6 +56,15 @@ SIGNATURES = {
     "vtb_cuda_matmul_q5_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
     "vtb_cuda_matmul_q6_k": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
     "vtb_cuda_matmul_tq2_0": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_segment_begin": (_vp, [_vp]),
+    "vtb_cuda_segment_commit": (_int, [_vp]),
+    "vtb_cuda_segment_matmul_q8_0": (None, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_segment_matmul_q4_k": (None, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_segment_matmul_q5_k": (None, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_segment_matmul_q6_k": (None, [_vp, _vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_segment_copy": (None, [_vp, _vp, _sz, _vp, _sz, _sz]),
+    "vtb_cuda_segment_copy_h2d": (None, [_vp, _vp, _sz, _vp, _sz]),
+    "vtb_cuda_segment_copy_d2h": (None, [_vp, _vp, _vp, _sz, _sz]),
     "vtb_cuda_model_create": (_vp, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _i32]),
     "vtb_cuda_model_destroy": (None, [_vp]),
     "vtb_cuda_model_weight_bytes": (_sz, [_vp]),

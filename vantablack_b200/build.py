@@ -46,10 +46,10 @@ def sources():
 
 
 def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(os.path.join(HERE, "libvtbbridgeloop.so")):
         return False
     t = os.path.getmtime(LIB)
-    deps = sources() + [os.path.join(ROOT, "include", "vtb_cuda.h")]
+    deps = sources() + [os.path.join(ROOT, "include", "vtb_cuda.h"), os.path.join(HERE, "native", "bridge_loop.c")]
     return all(os.path.getmtime(s) <= t for s in deps if os.path.exists(s))
 
 
@@ -65,7 +65,20 @@ def build(force: bool = False, verbose: bool = False) -> str:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
     os.replace(LIB + ".tmp", LIB)
+    build_bridge_loop()
     return LIB
+
+
+BRIDGE_LOOP = os.path.join(HERE, "libvtbbridgeloop.so")
+
+
+def build_bridge_loop() -> str:
+    """native/bridge_loop.c: a compiled caller of the C ABI (bench.py's
+    end-to-end measurement), linked against libvtbcuda.so."""
+    src = os.path.join(HERE, "native", "bridge_loop.c")
+    subprocess.run(["gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-o", BRIDGE_LOOP, src,
+                    "-L" + HERE, "-l:libvtbcuda.so", "-Wl,-rpath,$ORIGIN"], check=True)
+    return BRIDGE_LOOP
 
 
 if __name__ == "__main__":

@@ -190,9 +190,14 @@ int vtb_cuda_gemm(int quant, const void* w, const float* acts, float* out, int64
 }  // extern "C"
 
 // ---------------- context / buffers ----------------
+struct VtbSegCache;  // segment.cu: the open segment and the graphs of recent ones
+namespace vtb {
+void seg_cache_destroy(VtbSegCache* s);
+}
 struct VtbCudaCtx {
   int device;
   cudaStream_t stream;
+  VtbSegCache* seg;
 };
 struct VtbCudaBuf {
   VtbCudaCtx* ctx;
@@ -230,7 +235,7 @@ VtbCudaCtx* vtb_cuda_init(int device_ordinal) {
     return nullptr;
   }
   if (cudaSetDevice(device_ordinal) != cudaSuccess) return nullptr;
-  VtbCudaCtx* c = new (std::nothrow) VtbCudaCtx{device_ordinal, nullptr};
+  VtbCudaCtx* c = new (std::nothrow) VtbCudaCtx{device_ordinal, nullptr, nullptr};
   if (!c) return nullptr;
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete c;
@@ -243,6 +248,7 @@ void vtb_cuda_destroy(VtbCudaCtx* c) {
   if (!c) return;
   cudaSetDevice(c->device);
   cudaStreamSynchronize(c->stream);
+  vtb::seg_cache_destroy(c->seg);
   cudaStreamDestroy(c->stream);
   delete c;
 }

@@ -8,6 +8,7 @@
 #include "quant_aux.cu"
 #include "gemm_tc.cu"
 #include "api.cu"
+#include "segment.cu"
 #include "tp.cu"
 #include "model.cu"
 #include "gguf.cu"
