@@ -44,10 +44,10 @@ constexpr int GEMM_MIN_ROWS = 8;
 
 // x += t (addInto, math.zig:178-187) for the GEMM path's residual adds.
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ t, long long n) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     x[i] += t[i];
-  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 cudaError_t launch_gemv_q8_0_q8_0(const void* w, const int8_t* xq, const float* dx, float* y, int m, int k,
@@ -72,6 +72,7 @@ static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int 
 // all-reduce).
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ res, const float* __restrict__ w,
                                float* __restrict__ out, int n, float eps) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = blockIdx.x;
   float* xr = x + (long long)r * n;
@@ -96,7 +97,6 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
   }
   __syncthreads();
   const float inv = 1.0f / sqrtf(part[0] / (float)n + eps);
-  asm volatile("griddepcontrol.launch_dependents;");
   float* o = out + (long long)r * n;
   for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = (xr[i] * w[i]) * inv;
 }
@@ -137,9 +137,9 @@ __device__ __forceinline__ void tp_raise_flag(const PeerPtrs& peers, int world, 
 }
 
 __global__ void tp_signal_kernel(PeerPtrs peers, int world, int me, long long flag_off) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the partial of this rank is complete
   if (threadIdx.x == 0) tp_raise_flag(peers, world, me, flag_off);
-  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // x[r] += sum over ranks of slot[r] (peer loads), then out = RMSNorm(x) as rmsnorm_kernel.
@@ -148,6 +148,7 @@ __global__ void tp_signal_kernel(PeerPtrs peers, int world, int me, long long fl
 __global__ void __launch_bounds__(1024) rmsnorm_tp_kernel(float* __restrict__ x, PeerPtrs peers, int world, int me, long long slot_off,
                                   long long flag_off, const float* __restrict__ w, float* __restrict__ out, int n,
                                   float eps, int signal) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
     if (signal) tp_raise_flag(peers, world, me, flag_off);  // single-CTA launch: publish, then wait
@@ -199,7 +200,6 @@ __global__ void __launch_bounds__(1024) rmsnorm_tp_kernel(float* __restrict__ x,
   }
   __syncthreads();
   const float inv = 1.0f / sqrtf(part[0] / (float)n + eps);
-  asm volatile("griddepcontrol.launch_dependents;");
   float* o = out + (long long)r * n;
   for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = (xr[i] * w[i]) * inv;
 }
@@ -212,7 +212,9 @@ struct RowInfo {
 };
 
 __global__ void rope_kv_kernel(float* __restrict__ qkv, float* __restrict__ kc, float* __restrict__ vc, RowInfo ri,
-                               int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd, float base) {
+                               int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd,
+                               const float* __restrict__ rope) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = blockIdx.x;
   const int qd = n_heads * hd, kvd = n_kv * hd, stride = qd + 2 * kvd;
@@ -220,15 +222,13 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, float* __restrict__ kc, 
   float* k = q + qd;
   const float* v = k + kvd;
   const int pos = ri.pos[r], seq = ri.seq[r];
-  const float pos_f = (float)pos;
   const long long slot = (((long long)seq * n_layers + layer) * max_seq + pos) * kvd;
   const int half = hd / 2;
+  const float2* cs = reinterpret_cast<const float2*>(rope + (long long)pos * hd);
   for (int p = threadIdx.x; p < (n_heads + n_kv) * half; p += blockDim.x) {
     const int h = p / half, i = 2 * (p % half);
-    const float e = (float)i / (float)hd;
-    const float inv_freq = 1.0f / powf(base, e);
-    const float theta = pos_f * inv_freq;
-    const float c = cosf(theta), s = sinf(theta);
+    const float2 t = cs[i / 2];
+    const float c = t.x, s = t.y;
     float* ptr = h < n_heads ? q + h * hd + i : k + (h - n_heads) * hd + i;
     const float x0 = ptr[0], x1 = ptr[1];
     const float a = x0 * c, b = x1 * s, pp = x0 * s, qq = x1 * c;
@@ -242,7 +242,6 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, float* __restrict__ kc, 
     }
   }
   for (int i = threadIdx.x; i < kvd; i += blockDim.x) vc[slot + i] = v[i];
-  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // Decode/causal attention (cpuAttention forward.zig:187-228, attentionCausal
@@ -262,7 +261,7 @@ static_assert(ATT_THREADS == 2 * ATT_CHUNK, "score pass: two threads per positio
 __host__ __device__ inline int attn_smem_floats(int G, int hd) {
   const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
   const int scf = G * ATT_CHUNK > slices * G * hd ? G * ATT_CHUNK : slices * G * hd;
-  return G * hd + scf + 2 * ATT_CHUNK * (hd + ATT_PAD);
+  return G * hd + scf + 2 * ATT_CHUNK * (hd + ATT_PAD) + hd;  // + the (cos, sin) pairs of the row's position
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -281,19 +280,25 @@ __global__ void __launch_bounds__(ATT_THREADS)
 attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
                     RowInfo ri, int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd,
                     float* __restrict__ part, int nsplit, float* __restrict__ kcw, float* __restrict__ vcw,
-                    float rope_base) {
+                    const float* __restrict__ rope) {
   // kcw / vcw non-null: decode step with RoPE + KV write fused in (rope_kv_kernel's
   // work): q is rotated in shared memory, and the split that holds the row's
   // position rotates its K and writes K and V to the cache and to its staged rows.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The cached K/V rows of earlier positions were written by earlier steps, so
+  // in that case the first split's copies are issued before griddepcontrol.wait
+  // and their DRAM latency overlaps the QKV projection still running.
+  asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ __align__(16) float sm[];
   const int kvh = blockIdx.x, r = blockIdx.y;
   int sp = blockIdx.z;
   const int G = GT ? GT : n_heads / n_kv;
   const int qd = n_heads * hd, kvd = n_kv * hd;
-  const int pos = ri.pos[r], seq = ri.seq[r];
+  const int pos = ri.pos[r], seq = ri.seq[r];  // host-staged before the step's first kernel
   const int len = pos + 1, nsp = (len + ATT_CHUNK - 1) / ATT_CHUNK;
-  if (sp >= nsp) return;  // attn_combine_kernel reads only live splits
+  if (sp >= nsp) {  // attn_combine_kernel reads only live splits
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    return;
+  }
   const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
   const int scf = G * ATT_CHUNK > slices * G * hd ? G * ATT_CHUNK : slices * G * hd;
   const int ks = hd + ATT_PAD, h4 = hd / 4;
@@ -302,31 +307,10 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   float* kst = sc + scf;    // [ATT_CHUNK][ks]
   float* vst = kst + ATT_CHUNK * ks;
   const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
-  const float inv_sqrt_hd = 1.0f / sqrtf((float)hd);
-  const float* q = qkv + (long long)r * (qd + 2 * kvd) + kvh * G * hd;
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[i];
-  __syncthreads();
-  if (kcw) {
-    const float pos_f = (float)pos;
-    const int half = hd / 2;
-    for (int p = threadIdx.x; p < G * half; p += blockDim.x) {  // rope (math.zig:88-104) on q in smem
-      const int h = p / half, i = 2 * (p % half);
-      const float inv_freq = 1.0f / powf(rope_base, (float)i / (float)hd);
-      const float theta = pos_f * inv_freq;
-      const float c = cosf(theta), sn = sinf(theta);
-      float* ptr = qs + h * hd + i;
-      const float x0 = ptr[0], x1 = ptr[1];
-      const float a = x0 * c, b = x1 * sn, pp = x0 * sn, qq = x1 * c;
-      ptr[0] = a - b;
-      ptr[1] = pp + qq;
-    }
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float hm[64], hl[64];
-  for (; sp < nsp; sp += gridDim.z) {
-    const int t0 = sp * ATT_CHUNK, t1 = min(len, t0 + ATT_CHUNK), n = t1 - t0;
-    float* pr = part + (((long long)r * n_heads + kvh * G) * nsplit + sp) * (hd + 2);  // head stride nsplit*(hd+2)
-    const int own = (kcw && sp == pos / ATT_CHUNK) ? pos - t0 : -1;  // staged row this CTA writes itself
+  // Stage split sp's K and V rows (all but the row this step writes itself).
+  auto stage = [&](int spl) {
+    const int t0 = spl * ATT_CHUNK, n = min(len, t0 + ATT_CHUNK) - t0;
+    const int own = (kcw && spl == pos / ATT_CHUNK) ? pos - t0 : -1;
     for (int i = threadIdx.x; i < n * h4; i += ATT_THREADS) {
       const int t = i / h4, c4 = 4 * (i % h4);
       if (t != own) cp_async16(kst + t * ks + c4, kc + (lbase + t0 + t) * kvd + kvh * hd + c4);
@@ -337,31 +321,63 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
       if (t != own) cp_async16(vst + t * ks + c4, vc + (lbase + t0 + t) * kvd + kvh * hd + c4);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    if (own >= 0) {  // this split owns position `pos`: rotate its K, write K and V to cache and stage
-      const float pos_f = (float)pos;
-      const int half = hd / 2;
-      const float* kr = qkv + (long long)r * (qd + 2 * kvd) + qd + kvh * hd;
-      const float* vr = kr + kvd;
-      const long long slot = (lbase + pos) * kvd + kvh * hd;
-      for (int p = threadIdx.x; p < half; p += blockDim.x) {
-        const int i = 2 * p;
-        const float inv_freq = 1.0f / powf(rope_base, (float)i / (float)hd);
-        const float theta = pos_f * inv_freq;
-        const float c = cosf(theta), sn = sinf(theta);
-        const float x0 = kr[i], x1 = kr[i + 1];
-        const float a = x0 * c, b = x1 * sn, pp = x0 * sn, qq = x1 * c;
-        const float k0 = a - b, k1 = pp + qq;
-        kcw[slot + i] = k0;
-        kcw[slot + i + 1] = k1;
-        kst[own * ks + i] = k0;
-        kst[own * ks + i + 1] = k1;
-      }
-      for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        const float v = vr[i];
-        vcw[slot + i] = v;
-        vst[own * ks + i] = v;
-      }
+  };
+  const bool early = kcw != nullptr;
+  float* csm = vst + ATT_CHUNK * ks;  // [hd]: (cos, sin) of each rotated pair at the row's position
+  if (early) {
+    stage(sp);
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) csm[i] = rope[(long long)pos * hd + i];
+    __syncthreads();
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const float inv_sqrt_hd = 1.0f / sqrtf((float)hd);
+  const float* q = qkv + (long long)r * (qd + 2 * kvd) + kvh * G * hd;
+  const int half = hd / 2;
+  // The row's own K / V (this step's QKV output): rotated K and V go to the
+  // cache and to the staged rows of the split that holds `pos`.
+  auto own_row = [&](int own) {
+    const float* kr = qkv + (long long)r * (qd + 2 * kvd) + qd + kvh * hd;
+    const float* vr = kr + kvd;
+    const long long slot = (lbase + pos) * kvd + kvh * hd;
+    for (int p = threadIdx.x; p < half; p += blockDim.x) {
+      const int i = 2 * p;
+      const float c = csm[i], sn = csm[i + 1];
+      const float2 xk = *reinterpret_cast<const float2*>(kr + i);
+      const float a = xk.x * c, b = xk.y * sn, pp = xk.x * sn, qq = xk.y * c;
+      const float k0 = a - b, k1 = pp + qq;
+      kcw[slot + i] = k0;
+      kcw[slot + i + 1] = k1;
+      kst[own * ks + i] = k0;
+      kst[own * ks + i + 1] = k1;
     }
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+      const float v = vr[i];
+      vcw[slot + i] = v;
+      vst[own * ks + i] = v;
+    }
+  };
+  if (kcw) {  // q with rope (math.zig:88-104) applied on the way into shared memory
+    for (int p = threadIdx.x; p < G * half; p += blockDim.x) {
+      const int h = p / half, i = 2 * (p % half);
+      const float2 xq = *reinterpret_cast<const float2*>(q + h * hd + i);
+      const float c = csm[i], sn = csm[i + 1];
+      const float a = xq.x * c, b = xq.y * sn, pp = xq.x * sn, qq = xq.y * c;
+      qs[h * hd + i] = a - b;
+      qs[h * hd + i + 1] = pp + qq;
+    }
+    if (sp == pos / ATT_CHUNK) own_row(pos - sp * ATT_CHUNK);  // its loads overlap the q loads
+  } else {
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[i];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float hm[64], hl[64];
+  for (bool first = true; sp < nsp; sp += gridDim.z, first = false) {
+    const int t0 = sp * ATT_CHUNK, t1 = min(len, t0 + ATT_CHUNK), n = t1 - t0;
+    float* pr = part + (((long long)r * n_heads + kvh * G) * nsplit + sp) * (hd + 2);  // head stride nsplit*(hd+2)
+    const int own = (kcw && sp == pos / ATT_CHUNK) ? pos - t0 : -1;  // staged row this CTA writes itself
+    if (!(first && early)) stage(sp);
+    if (own >= 0 && !first) own_row(own);  // (the first split's own row went in with q)
     asm volatile("cp.async.wait_group 1;" ::: "memory");  // K staged (V may still be in flight)
     __syncthreads();
     // scores: two threads per position, each over alternate float4 columns of the staged K row
@@ -471,7 +487,6 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     }
     __syncthreads();  // the next split reuses the staging and score buffers
   }
-  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 __device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
@@ -494,11 +509,12 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) 
 // computed once into shared memory; each dimension's sum then has independent loads.
 __global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ att, RowInfo ri, int n_heads,
                                     int hd, int nsplit) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ float wsm[];  // [nsplit]
   __shared__ float red[32];
   const int h = blockIdx.x, r = blockIdx.y;
-  const int na = min(nsplit, ri.pos[r] / ATT_CHUNK + 1);
+  const int na = min(nsplit, ri.pos[r] / ATT_CHUNK + 1);  // positions are staged before the step
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const float* p = part + ((long long)r * n_heads + h) * nsplit * (hd + 2);
   float M = -INFINITY;
   for (int s = threadIdx.x; s < na; s += blockDim.x) M = fmaxf(M, p[s * (hd + 2)]);
@@ -517,7 +533,6 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, float* __res
     for (int s = 0; s < na; ++s) a += p[s * (hd + 2) + 2 + d] * wsm[s];
     att[((long long)r * n_heads + h) * hd + d] = a * invL;
   }
-  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // Prefill attention: the rows are one prompt (one sequence, consecutive or
@@ -539,6 +554,7 @@ __global__ void __launch_bounds__(PA_THREADS)
 attn_prefill_kernel(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
                     RowInfo ri, int rows, int layer, int n_layers, int max_seq, int n_heads, int n_kv,
                     float* __restrict__ att) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   using P = PaSmem<HD>;
   extern __shared__ __align__(16) float sm[];
@@ -673,12 +689,12 @@ attn_prefill_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
       *reinterpret_cast<float4*>(out + 64 * h + 4 * pg) =
           make_float4(o[i][4 * h] * inv, o[i][4 * h + 1] * inv, o[i][4 * h + 2] * inv, o[i][4 * h + 3] * inv);
   }
-  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // swiglu (math.zig:154-161): h = (g / (1 + e^-g)) * u.  gu per row is
 // [gate | up], or with `il` the fused weights' [gate 8 | up 8] row blocks.
 __global__ void swiglu_kernel(const float* __restrict__ gu, float* __restrict__ h, int ffn, int rows, int il) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long n = (long long)rows * ffn;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -688,7 +704,6 @@ __global__ void swiglu_kernel(const float* __restrict__ gu, float* __restrict__ 
     const float den = 1.0f + expf(-g);
     h[i] = (g / den) * u;
   }
-  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // argmax (math.zig:190-201): first index of the maximum of each row.
@@ -796,6 +811,7 @@ struct VtbCudaState {
   size_t gsplit_elems = 0;
   int32_t *tok, *seq, *pos, *amax;
   float *kc, *vc;
+  float* rope;              // [max_seq][head_dim]: (cos, sin) of each rotated pair at each position
   int32_t* hbuf;            // pinned host staging: tok | seq | pos (3 * max_rows)
   int32_t* hamax;           // pinned host argmax
   std::vector<int64_t> seq_pos;  // host-authoritative positions (KvCache.pos, forward.zig:161,168)
@@ -1143,7 +1159,7 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   // split-K partials for small-batch GEMMs: splits x rows <= 512 of the widest projection
   const size_t gsplit = R >= (size_t)GEMM_MIN_ROWS ? 512 * std::max(std::max(qkvw, 2 * f), d) : 0;
   size_t fl = R * (d + d + qkvw + qd + 2 * f + f + (size_t)c.vocab_size + m->V + d + kmax) +
-              R * m->H * (size_t)s->nsplit * (hd + 2) + gsplit + 64;
+              R * m->H * (size_t)s->nsplit * (hd + 2) + gsplit + (size_t)c.max_seq * hd + 64;
   const size_t kvn = (size_t)n_seqs * c.n_layers * c.max_seq * kvd;
   float* base = nullptr;
   int32_t* ib = nullptr;
@@ -1167,8 +1183,21 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
   s->gsplit = gsplit ? carve(gsplit) : nullptr;
   s->gsplit_elems = gsplit;
   s->kc = carve(kvn); s->vc = carve(kvn);
+  s->rope = carve((size_t)c.max_seq * hd);
   s->tok = ib; s->seq = ib + R; s->pos = ib + 2 * R; s->amax = ib + 3 * R;
   cudaMemsetAsync(s->kc, 0, 2 * kvn * 4, s->st);
+  // RoPE angles with the reference's float steps (math.zig:88-104): inv_freq =
+  // 1 / pow(base, i / hd), theta = pos * inv_freq, cos / sin, computed once on
+  // the host with the C library's float functions.
+  std::vector<float> rope_h((size_t)c.max_seq * hd);
+  for (int pos = 0; pos < c.max_seq; ++pos)
+    for (size_t i = 0; i < hd; i += 2) {
+      const float inv_freq = 1.0f / powf(c.rope_base, (float)i / (float)hd);
+      const float theta = (float)pos * inv_freq;
+      rope_h[(size_t)pos * hd + i] = cosf(theta);
+      rope_h[(size_t)pos * hd + i + 1] = sinf(theta);
+    }
+  cudaMemcpyAsync(s->rope, rope_h.data(), rope_h.size() * 4, cudaMemcpyHostToDevice, s->st);
   s->seq_pos.assign(n_seqs, 0);
   if (m->tp && m->tp->world > 1 && m->tp->world <= TP_MAX && !tp_p2p_setup(s)) {
     vtb_cuda_state_destroy(s);
@@ -1244,6 +1273,10 @@ static cudaError_t enqueue_embed(VtbCudaState* s) {
   return launch_embed(s->m->q_embd, s->m->embd, s->tok, s->x, s->m->c.dim, s->rows, s->st);
 }
 
+// Every kernel of the forward loop releases its dependent at its first
+// instruction: the dependent's own griddepcontrol.wait still orders it after
+// this grid completes, so the early release only lets the next GEMV's CTAs
+// start their weight prefetch while this kernel runs.
 template <typename K, typename... A>
 static cudaError_t pdl_launch(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... args) {
   cudaLaunchConfig_t cfg = {};
@@ -1381,7 +1414,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
   // Prefill rows of one sequence read each other's K/V: separate kernel first.
   const bool fuse_rope = s->decode_rows;
   if (!fuse_rope && (e = pdl_launch(rope_kv_kernel, dim3(R), dim3(256), 0, st, s->qkv, s->kc, s->vc, ri, l, c.n_layers,
-                                    c.max_seq, H, KV, hd, c.rope_base)))
+                                    c.max_seq, H, KV, hd, (const float*)s->rope)))
     return e;
   float* kcw = fuse_rope ? s->kc : nullptr;
   float* vcw = fuse_rope ? s->vc : nullptr;
@@ -1408,14 +1441,14 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
     case g:                                                                                                      \
       e = pdl_launch(attn_partial_kernel<g>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,             \
                      (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,     \
-                     s->nsplit, kcw, vcw, c.rope_base);                                                          \
+                     s->nsplit, kcw, vcw, (const float*)s->rope);                                                          \
       break;
       VTB_ATT(1) VTB_ATT(2) VTB_ATT(4) VTB_ATT(8)
   #undef VTB_ATT
       default:
         e = pdl_launch(attn_partial_kernel<0>, agrid, dim3(ATT_THREADS), asmem, st, (const float*)s->qkv,
                        (const float*)s->kc, (const float*)s->vc, ri, l, c.n_layers, c.max_seq, H, KV, hd, s->part,
-                       s->nsplit, kcw, vcw, c.rope_base);
+                       s->nsplit, kcw, vcw, (const float*)s->rope);
     }
     if (e) return e;
     if ((e = pdl_launch(attn_combine_kernel, dim3(H, R), dim3(128), (size_t)s->nsplit * 4, st, (const float*)s->part,
