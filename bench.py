@@ -728,6 +728,14 @@ def run_profile_case(case: str) -> None:
             x = torch.from_numpy(S.activations(rng, k)).cuda()
             ops.gemv(S.Q6_K, w, x, m, k)
             torch.cuda.synchronize()
+    elif case == "gemv_q8":  # Q8_0 4096 x 14336 and 14336 x 4096 (f32 x), then Q8_0 x Q8_0 at 14336 x 4096
+        for m, k in ((4096, 14336), (14336, 4096)):
+            w = torch.from_numpy(S.quant_tensor(rng, Q8_0, m, k)).cuda()
+            x = torch.from_numpy(S.activations(rng, k)).cuda()
+            ops.gemv(Q8_0, w, x, m, k)
+            torch.cuda.synchronize()
+        ops.gemv_q8_0_q8_0(w, x, m, k)
+        torch.cuda.synchronize()
     elif case == "gemm":  # Q4_K 14336 x 4096, B = 2048, bf16 mode, two launches
         m, k, b = 14336, 4096, 2048
         w = torch.from_numpy(S.quant_tensor(rng, Q4_K, m, k)).cuda()
@@ -774,7 +782,7 @@ def run_profile_case(case: str) -> None:
     print("ok", case)
 
 
-PROFILE_CASES = ["gemv", "gemv_chain", "gemv_q6k", "gemm", "gemm_precise", "gemm_b32", "gemm_b32_q4k", "decode", "decode8b",
+PROFILE_CASES = ["gemv", "gemv_chain", "gemv_q6k", "gemv_q8", "gemm", "gemm_precise", "gemm_b32", "gemm_b32_q4k", "decode", "decode8b",
                  "decode8b_b32"]
 
 
