@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <vector>
 
 #include "../../include/vtb_cuda.h"
 #include "common.cuh"
@@ -347,3 +348,26 @@ int vtb_cuda_matmul_tq2_0(VtbCudaCtx* c, VtbCudaBuf* o, VtbCudaBuf* w, size_t of
 }
 
 }  // extern "C"
+
+#ifdef VTB_TIMELINE
+// Development builds only (-DVTB_TIMELINE): copies the launch timeline ring
+// (8 u64 per record: id | sm << 32, entry, wait returned, exit, 4 marks) into `out`,
+// oldest first, and returns the record count; reset != 0 clears it.
+extern "C" int vtb_cuda_timeline(unsigned long long* out, int max_records, int reset) {
+  unsigned n = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpyFromSymbol(&n, vtb::g_tl_n, sizeof n) != cudaSuccess)
+    return -1;
+  const unsigned have = n < vtb::kTlRing ? n : vtb::kTlRing;
+  std::vector<unsigned long long> ring(8 * (size_t)vtb::kTlRing);
+  if (cudaMemcpyFromSymbol(ring.data(), vtb::g_tl, ring.size() * 8) != cudaSuccess) return -1;
+  int k = 0;
+  for (unsigned j = n - have; j < n && k < max_records; ++j, ++k)
+    for (int c = 0; c < 8; ++c) out[8 * k + c] = ring[8 * (j % vtb::kTlRing) + c];
+  if (reset) {
+    const unsigned zero = 0;
+    cudaMemcpyToSymbol(vtb::g_tl_n, &zero, sizeof zero);
+  }
+  return k;
+}
+#endif
+

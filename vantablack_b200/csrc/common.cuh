@@ -118,6 +118,54 @@ __device__ unsigned g_dev_error = 0;  // one definition: the library is a single
 
 __device__ __forceinline__ void flag_error(unsigned code) { atomicOr(&g_dev_error, code); }
 
+// Optional launch timeline (a development build with -DVTB_TIMELINE): block
+// (0,0,0) of each instrumented kernel records its kernel id, SM, entry time,
+// the time its griddepcontrol.wait returned and its exit time (globaltimer
+// ns) into a ring read back by vtb_cuda_timeline.  Compiled out otherwise.
+#ifdef VTB_TIMELINE
+constexpr unsigned kTlRing = 16384;
+__device__ unsigned long long g_tl[8 * kTlRing];
+__device__ unsigned g_tl_n;
+__device__ __forceinline__ unsigned long long tl_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+struct TlRec {
+  unsigned long long t0 = 0, t1 = 0, mk[4] = {0, 0, 0, 0};
+  int id;
+  bool on;
+  __device__ explicit TlRec(int i) : id(i) {
+    on = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0;
+    if (on) t0 = tl_now();
+  }
+  __device__ void waited() {
+    if (on) t1 = tl_now();
+  }
+  __device__ void mark(int k) {
+    if (on) mk[k] = tl_now();
+  }
+  __device__ ~TlRec() {
+    if (!on) return;
+    unsigned sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    const unsigned i = atomicAdd(&g_tl_n, 1u) % kTlRing;
+    g_tl[8 * i] = (unsigned long long)id | ((unsigned long long)sm << 32);
+    g_tl[8 * i + 1] = t0;
+    g_tl[8 * i + 2] = t1 ? t1 : t0;
+    g_tl[8 * i + 3] = tl_now();
+    for (int k = 0; k < 4; ++k) g_tl[8 * i + 4 + k] = mk[k];
+  }
+};
+#define VTB_TL(id) TlRec vtb_tl_rec_(id)
+#define VTB_TL_WAITED() vtb_tl_rec_.waited()
+#define VTB_TL_MARK(k) vtb_tl_rec_.mark(k)
+#else
+#define VTB_TL_MARK(k)
+#define VTB_TL(id)
+#define VTB_TL_WAITED()
+#endif
+
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 
 // ---- packed f32x2 arithmetic (sm_100a) ----

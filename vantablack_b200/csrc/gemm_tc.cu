@@ -271,6 +271,7 @@ __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapBh,
                const __grid_constant__ CUtensorMap mapBl, const uint8_t* __restrict__ W, float* __restrict__ out,
                int M, int K, int NB, long long pitch) {
+  VTB_TL(5);
   using C = TcCfg<Q, BN, PASSES, S, TA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -332,6 +333,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
           }
         }
         if (i == 0) asm volatile("griddepcontrol.wait;" ::: "memory");  // activations come from the previous kernel
+  VTB_TL_WAITED();
         const int s = i % S;
         if (i >= S && !mbar_wait_bounded(&empty[s], (unsigned)(((i / S) - 1) & 1))) { ok = false; break; }
         uint8_t* st = smem + s * C::STAGE;
@@ -523,7 +525,9 @@ static cudaError_t launch_gemm_tc_q(const void* w, const __nv_bfloat16* xh, cons
 
 // out[i] = sum over splits z of part[z][i], in split order (deterministic).
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, float* __restrict__ out, long long n, int ks) {
+  VTB_TL(6);
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     float v = part[i];
     for (int z = 1; z < ks; ++z) v += part[(long long)z * n + i];

@@ -274,6 +274,7 @@ template <int Q, int R, int S, int WARPS, bool XQ>
 __global__ void __launch_bounds__(WARPS * 32)
 gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const float* __restrict__ dx,
             float* __restrict__ y, int M, int K, int accumulate, long long pitch) {
+  VTB_TL(4);
   const float* x = static_cast<const float*>(xv);
   constexpr int CH = GemvCfg<Q>::CH, BB = Fmt<Q>::bytes, EL = Fmt<Q>::elems;
   constexpr int SLOT = Slot<Q>::BYTES, STAGE = R * SLOT;
@@ -325,6 +326,7 @@ gemv_kernel(const uint8_t* __restrict__ W, const void* __restrict__ xv, const fl
 
   // x is produced by the previous kernel in the stream: wait for it only now.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   asm volatile("griddepcontrol.launch_dependents;");
 
   XSlice xs;

@@ -168,6 +168,7 @@ template <int WARPS, int S, int Q, int ROWS>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y, int M, int K,
                     int ksplit, int accumulate, const float* __restrict__ norm_w, float eps, float* __restrict__ swi) {
+  VTB_TL(1);
   using C = MmaQ4K<Q, ROWS>;
   constexpr int MT = ROWS / 16, NI = 2 * MT;  // m16 tiles; rows g + 8i this lane holds
   extern __shared__ __align__(128) uint8_t smem[];
@@ -219,8 +220,19 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
 
   // Let the next kernel in the stream launch now (its own wait still orders it
   // after this grid completes): its CTAs start their weight prefetch on free SMs.
+  // The x rows of at most 2 groups per warp stay in registers; the RMSNorm
+  // weight (when fused) is a weight, independent of the producer of x, so it
+  // is loaded before the wait.
+  const int n4 = K / 128;
+  const bool early_x = n4 <= 2 * WARPS;
+  float4 xv0 = make_float4(0.f, 0.f, 0.f, 0.f), xv1 = xv0, nv0 = xv0, nv1 = xv0;
+  if (norm_w && early_x) {
+    if (warp < n4) nv0 = __ldg(reinterpret_cast<const float4*>(norm_w + warp * 128) + lane);
+    if (warp + WARPS < n4) nv1 = __ldg(reinterpret_cast<const float4*>(norm_w + (warp + WARPS) * 128) + lane);
+  }
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
 
   // Read tile tt's weight-side operands into registers, then hand its stage
   // back to the copy engine.
@@ -273,19 +285,21 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
   };
 
   float inv = 1.f;
-  const int n4 = K / 128;
-  const bool early_x = norm_w == nullptr && n4 <= 2 * WARPS;
-  float4 xv0 = make_float4(0.f, 0.f, 0.f, 0.f), xv1 = xv0;
   if (early_x) {  // the activation loads fly while the first tile is read out
-    if (warp < n4) xv0 = load_group(x, warp, lane, nullptr, 1.f);
-    if (warp + WARPS < n4) xv1 = load_group(x, warp + WARPS, lane, nullptr, 1.f);
+    if (warp < n4) xv0 = __ldg(reinterpret_cast<const float4*>(x + warp * 128) + lane);
+    if (warp + WARPS < n4) xv1 = __ldg(reinterpret_cast<const float4*>(x + (warp + WARPS) * 128) + lane);
   }
   bool ok = ntiles == 0 || prep(0);
   if (norm_w) {  // sum of squares of the whole row (every CTA; x is L2-resident)
     float ss = 0.f;
-    for (int i = threadIdx.x; i < K / 4; i += WARPS * 32) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(x) + i);
-      ss += (a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w);
+    if (early_x) {  // the same float4s, in the same order, as the loop below
+      ss = (xv0.x * xv0.x + xv0.y * xv0.y) + (xv0.z * xv0.z + xv0.w * xv0.w);
+      ss += (xv1.x * xv1.x + xv1.y * xv1.y) + (xv1.z * xv1.z + xv1.w * xv1.w);
+    } else {
+      for (int i = threadIdx.x; i < K / 4; i += WARPS * 32) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(x) + i);
+        ss += (a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w);
+      }
     }
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
@@ -296,12 +310,17 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
     __syncthreads();
   }
   if (early_x) {
+    if (norm_w) {  // (x * w) * inv, as load_group scales
+      xv0 = make_float4((xv0.x * nv0.x) * inv, (xv0.y * nv0.y) * inv, (xv0.z * nv0.z) * inv, (xv0.w * nv0.w) * inv);
+      xv1 = make_float4((xv1.x * nv1.x) * inv, (xv1.y * nv1.y) * inv, (xv1.z * nv1.z) * inv, (xv1.w * nv1.w) * inv);
+    }
     if (warp < n4) convert_group(xv0, warp, lane, xsh);
     if (warp + WARPS < n4) convert_group(xv1, warp + WARPS, lane, xsh);
   } else {
     build_x_shared(x, K, xsh, warp, lane, WARPS, norm_w, inv);
   }
   __syncthreads();
+  VTB_TL_MARK(0);
 
   const int gs = g >> 1;                  // sub-block (within a group of 4) whose B columns this lane holds
   const int boff = (g & 1) * 32 + t * 8;  // limb g&1, quad t
@@ -364,6 +383,7 @@ gemv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __r
       }
       if (tt + 1 < ntiles && !prep(tt + 1)) ok = false;
     }
+    VTB_TL_MARK(1);
     // CTA reduction of the K-split partial sums for this unit's rows.
 #pragma unroll
     for (int i = 0; i < NI; ++i) {

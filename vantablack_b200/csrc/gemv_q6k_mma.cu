@@ -102,6 +102,7 @@ template <int WARPS, int S>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q6k_mma_kernel(const __grid_constant__ CUtensorMap wmap, float* __restrict__ y, const float* __restrict__ x,
                     int M, int K, int ksplit, int accumulate) {
+  VTB_TL(2);
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3, sbl = g >> 1;
@@ -140,6 +141,7 @@ gemv_q6k_mma_kernel(const __grid_constant__ CUtensorMap wmap, float* __restrict_
   // after this grid completes): its CTAs start their weight prefetch on free SMs.
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   build_x_q6k(x, K, xq, xs, warp, lane, WARPS);
   __syncthreads();
 

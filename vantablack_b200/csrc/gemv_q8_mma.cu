@@ -58,6 +58,7 @@ template <int WARPS, int S, bool XQ>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x, int8_t* __restrict__ xqg,
                    float* __restrict__ dxg, float* __restrict__ y, int M, int K, int ksplit, int accumulate) {
+  VTB_TL(3);
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -104,6 +105,7 @@ gemv_q8_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __rest
 
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
 
   // A words of the 8 blocks (rows g, g+8; k = 4t.. and 16+4t..) and the
   // scales d of this lane's blocks t and 4+t for both rows.

@@ -44,8 +44,10 @@ constexpr int GEMM_MIN_ROWS = 8;
 
 // x += t (addInto, math.zig:178-187) for the GEMM path's residual adds.
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ t, long long n) {
+  VTB_TL(7);
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     x[i] += t[i];
 }
@@ -72,8 +74,10 @@ static cudaError_t gemv_any(int q, const void* w, const float* x, float* y, int 
 // all-reduce).
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ res, const float* __restrict__ w,
                                float* __restrict__ out, int n, float eps) {
+  VTB_TL(8);
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   const int r = blockIdx.x;
   float* xr = x + (long long)r * n;
   const float* rr = res ? res + (long long)r * n : nullptr;
@@ -137,8 +141,10 @@ __device__ __forceinline__ void tp_raise_flag(const PeerPtrs& peers, int world, 
 }
 
 __global__ void tp_signal_kernel(PeerPtrs peers, int world, int me, long long flag_off) {
+  VTB_TL(9);
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the partial of this rank is complete
+  VTB_TL_WAITED();
   if (threadIdx.x == 0) tp_raise_flag(peers, world, me, flag_off);
 }
 
@@ -148,8 +154,10 @@ __global__ void tp_signal_kernel(PeerPtrs peers, int world, int me, long long fl
 __global__ void __launch_bounds__(1024) rmsnorm_tp_kernel(float* __restrict__ x, PeerPtrs peers, int world, int me, long long slot_off,
                                   long long flag_off, const float* __restrict__ w, float* __restrict__ out, int n,
                                   float eps, int signal) {
+  VTB_TL(10);
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   if (threadIdx.x == 0) {
     if (signal) tp_raise_flag(peers, world, me, flag_off);  // single-CTA launch: publish, then wait
     const unsigned* flags = reinterpret_cast<const unsigned*>(peers.p[me] + flag_off);
@@ -214,8 +222,10 @@ struct RowInfo {
 __global__ void rope_kv_kernel(float* __restrict__ qkv, float* __restrict__ kc, float* __restrict__ vc, RowInfo ri,
                                int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd,
                                const float* __restrict__ rope) {
+  VTB_TL(11);
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   const int r = blockIdx.x;
   const int qd = n_heads * hd, kvd = n_kv * hd, stride = qd + 2 * kvd;
   float* q = qkv + (long long)r * stride;
@@ -249,19 +259,22 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, float* __restrict__ kc, 
 // Split-K ("flash decode"): CTA (kv_head, row, split) handles positions
 // [split*CHUNK, ...) for the GQA group of q heads that share the kv head,
 // and writes a partial (max, sum, acc[hd]) per q head; attn_combine merges.
-constexpr int ATT_CHUNK = 64;
+constexpr int ATT_CHUNK = 64;  // prefill attention: positions per staged K/V chunk
+constexpr int DEC_CHUNK = 64;  // decode attention: positions per split
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_GMAX = 8;  // GQA group sizes up to 8 keep their accumulators in registers
 
 constexpr int ATT_PAD = 8;  // floats of padding per staged K/V row: the score pass reads conflict-free
-static_assert(ATT_THREADS == 2 * ATT_CHUNK, "score pass: two threads per position");
+constexpr int ATT_TPP = ATT_THREADS / DEC_CHUNK;  // score pass: threads per position
+static_assert(ATT_TPP * DEC_CHUNK == ATT_THREADS && (ATT_TPP & (ATT_TPP - 1)) == 0 && ATT_TPP <= 32,
+              "score pass: a power-of-two number of threads per position");
 
 // Shared-memory floats of one attention CTA: q [G][hd], scores [G][CHUNK] (reused
 // as the PV reduction [slices][G][hd]), staged K and V [CHUNK][hd + PAD].
 __host__ __device__ inline int attn_smem_floats(int G, int hd) {
   const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
-  const int scf = G * ATT_CHUNK > slices * G * hd ? G * ATT_CHUNK : slices * G * hd;
-  return G * hd + scf + 2 * ATT_CHUNK * (hd + ATT_PAD) + hd;  // + the (cos, sin) pairs of the row's position
+  const int scf = G * DEC_CHUNK > slices * G * hd ? G * DEC_CHUNK : slices * G * hd;
+  return G * hd + scf + 2 * DEC_CHUNK * (hd + ATT_PAD) + hd;  // + the (cos, sin) pairs of the row's position
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -270,7 +283,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 
 // One CTA per (kv head, row, split slot): partial softmax-attention of the G
 // query heads sharing the kv head (attention math of forward.zig's layer loop,
-// split flash-decoding style over 64-position chunks; the splits merge in
+// split flash-decoding style over DEC_CHUNK-position chunks; the splits merge in
 // attn_combine_kernel).  The grid holds about one wave: a CTA walks the row's
 // live splits sp, sp + gridDim.z, ...  Each split's K and V rows go to shared
 // memory in one round of 16-byte async copies, so a CTA waits on DRAM once per
@@ -281,6 +294,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
                     RowInfo ri, int layer, int n_layers, int max_seq, int n_heads, int n_kv, int hd,
                     float* __restrict__ part, int nsplit, float* __restrict__ kcw, float* __restrict__ vcw,
                     const float* __restrict__ rope) {
+  VTB_TL(12);
   // kcw / vcw non-null: decode step with RoPE + KV write fused in (rope_kv_kernel's
   // work): q is rotated in shared memory, and the split that holds the row's
   // position rotates its K and writes K and V to the cache and to its staged rows.
@@ -294,23 +308,23 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   const int G = GT ? GT : n_heads / n_kv;
   const int qd = n_heads * hd, kvd = n_kv * hd;
   const int pos = ri.pos[r], seq = ri.seq[r];  // host-staged before the step's first kernel
-  const int len = pos + 1, nsp = (len + ATT_CHUNK - 1) / ATT_CHUNK;
+  const int len = pos + 1, nsp = (len + DEC_CHUNK - 1) / DEC_CHUNK;
   if (sp >= nsp) {  // attn_combine_kernel reads only live splits
     asm volatile("griddepcontrol.wait;" ::: "memory");
     return;
   }
   const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
-  const int scf = G * ATT_CHUNK > slices * G * hd ? G * ATT_CHUNK : slices * G * hd;
+  const int scf = G * DEC_CHUNK > slices * G * hd ? G * DEC_CHUNK : slices * G * hd;
   const int ks = hd + ATT_PAD, h4 = hd / 4;
   float* qs = sm;           // [G][hd]
-  float* sc = sm + G * hd;  // [G][ATT_CHUNK]
-  float* kst = sc + scf;    // [ATT_CHUNK][ks]
-  float* vst = kst + ATT_CHUNK * ks;
+  float* sc = sm + G * hd;  // [G][DEC_CHUNK]
+  float* kst = sc + scf;    // [DEC_CHUNK][ks]
+  float* vst = kst + DEC_CHUNK * ks;
   const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
   // Stage split sp's K and V rows (all but the row this step writes itself).
   auto stage = [&](int spl) {
-    const int t0 = spl * ATT_CHUNK, n = min(len, t0 + ATT_CHUNK) - t0;
-    const int own = (kcw && spl == pos / ATT_CHUNK) ? pos - t0 : -1;
+    const int t0 = spl * DEC_CHUNK, n = min(len, t0 + DEC_CHUNK) - t0;
+    const int own = (kcw && spl == pos / DEC_CHUNK) ? pos - t0 : -1;
     for (int i = threadIdx.x; i < n * h4; i += ATT_THREADS) {
       const int t = i / h4, c4 = 4 * (i % h4);
       if (t != own) cp_async16(kst + t * ks + c4, kc + (lbase + t0 + t) * kvd + kvh * hd + c4);
@@ -323,13 +337,14 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   const bool early = kcw != nullptr;
-  float* csm = vst + ATT_CHUNK * ks;  // [hd]: (cos, sin) of each rotated pair at the row's position
+  float* csm = vst + DEC_CHUNK * ks;  // [hd]: (cos, sin) of each rotated pair at the row's position
   if (early) {
     stage(sp);
     for (int i = threadIdx.x; i < hd; i += blockDim.x) csm[i] = rope[(long long)pos * hd + i];
     __syncthreads();
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   const float inv_sqrt_hd = 1.0f / sqrtf((float)hd);
   const float* q = qkv + (long long)r * (qd + 2 * kvd) + kvh * G * hd;
   const int half = hd / 2;
@@ -365,7 +380,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
       qs[h * hd + i] = a - b;
       qs[h * hd + i + 1] = pp + qq;
     }
-    if (sp == pos / ATT_CHUNK) own_row(pos - sp * ATT_CHUNK);  // its loads overlap the q loads
+    if (sp == pos / DEC_CHUNK) own_row(pos - sp * DEC_CHUNK);  // its loads overlap the q loads
   } else {
     for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[i];
   }
@@ -373,16 +388,18 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float hm[64], hl[64];
   for (bool first = true; sp < nsp; sp += gridDim.z, first = false) {
-    const int t0 = sp * ATT_CHUNK, t1 = min(len, t0 + ATT_CHUNK), n = t1 - t0;
+    const int t0 = sp * DEC_CHUNK, t1 = min(len, t0 + DEC_CHUNK), n = t1 - t0;
     float* pr = part + (((long long)r * n_heads + kvh * G) * nsplit + sp) * (hd + 2);  // head stride nsplit*(hd+2)
-    const int own = (kcw && sp == pos / ATT_CHUNK) ? pos - t0 : -1;  // staged row this CTA writes itself
+    const int own = (kcw && sp == pos / DEC_CHUNK) ? pos - t0 : -1;  // staged row this CTA writes itself
     if (!(first && early)) stage(sp);
     if (own >= 0 && !first) own_row(own);  // (the first split's own row went in with q)
+    VTB_TL_MARK(0);
     asm volatile("cp.async.wait_group 1;" ::: "memory");  // K staged (V may still be in flight)
     __syncthreads();
-    // scores: two threads per position, each over alternate float4 columns of the staged K row
+    VTB_TL_MARK(1);
+    // scores: ATT_TPP threads per position, each over every ATT_TPP-th float4 column of the staged K row
     {
-      const int tt = threadIdx.x >> 1, hf = threadIdx.x & 1;
+      const int tt = threadIdx.x / ATT_TPP, hf = threadIdx.x % ATT_TPP;
       const float4* kr = reinterpret_cast<const float4*>(kst + tt * ks);
       const float4* q4 = reinterpret_cast<const float4*>(qs);
       if constexpr (GT > 0) {
@@ -391,7 +408,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
         for (int h = 0; h < GT; ++h) acc[h] = 0.f;
         if (tt < n) {
 #pragma unroll 4
-          for (int j = hf; j < h4; j += 2) {
+          for (int j = hf; j < h4; j += ATT_TPP) {
             const float4 kv = kr[j];
 #pragma unroll
             for (int h = 0; h < GT; ++h) {
@@ -401,20 +418,22 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
           }
         }
 #pragma unroll
-        for (int h = 0; h < GT; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+        for (int o = 1; o < ATT_TPP; o <<= 1)
+#pragma unroll
+          for (int h = 0; h < GT; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], o);
         if (tt < n && hf == 0)
 #pragma unroll
-          for (int h = 0; h < GT; ++h) sc[h * ATT_CHUNK + tt] = acc[h] * inv_sqrt_hd;
+          for (int h = 0; h < GT; ++h) sc[h * DEC_CHUNK + tt] = acc[h] * inv_sqrt_hd;
       } else {
         for (int h = 0; h < G; ++h) {
           float a = 0.f;
           if (tt < n)
-            for (int j = hf; j < h4; j += 2) {
+            for (int j = hf; j < h4; j += ATT_TPP) {
               const float4 kv = kr[j], b = q4[h * h4 + j];
               a += kv.x * b.x + kv.y * b.y + kv.z * b.z + kv.w * b.w;
             }
-          a += __shfl_xor_sync(0xffffffffu, a, 1);
-          if (tt < n && hf == 0) sc[h * ATT_CHUNK + tt] = a * inv_sqrt_hd;
+          for (int o = 1; o < ATT_TPP; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+          if (tt < n && hf == 0) sc[h * DEC_CHUNK + tt] = a * inv_sqrt_hd;
         }
       }
     }
@@ -422,13 +441,13 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     // per head: local max and exp-sum
     for (int h = warp; h < G; h += ATT_THREADS / 32) {
       float m = -INFINITY;
-      for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h * ATT_CHUNK + i]);
+      for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h * DEC_CHUNK + i]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       float l = 0.f;
       for (int i = lane; i < n; i += 32) {
-        const float e = expf(sc[h * ATT_CHUNK + i] - m);
-        sc[h * ATT_CHUNK + i] = e;
+        const float e = expf(sc[h * DEC_CHUNK + i] - m);
+        sc[h * DEC_CHUNK + i] = e;
         l += e;
       }
       l = warp_sum(l);
@@ -439,6 +458,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");  // V staged
     __syncthreads();
+    VTB_TL_MARK(2);
     // acc[h][d] = sum_t p[h][t] v[t][d]: thread (slice, d) reads staged v[t][d] once for every
     // head of the group; `slices` threads share a dimension, split the positions, add through smem.
     const int dd = threadIdx.x % hd, sl = threadIdx.x / hd;
@@ -451,7 +471,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
         for (int t = sl; t < n; t += slices) {
           const float v = vst[t * ks + dd];
 #pragma unroll
-          for (int h = 0; h < GT; ++h) acc[h] += sc[h * ATT_CHUNK + t] * v;
+          for (int h = 0; h < GT; ++h) acc[h] += sc[h * DEC_CHUNK + t] * v;
         }
       }
       __syncthreads();
@@ -474,7 +494,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     } else {
       for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
         const int h = i / hd, d = i % hd;
-        const float* ph = sc + h * ATT_CHUNK;
+        const float* ph = sc + h * DEC_CHUNK;
         float a = 0.f;
         for (int t = 0; t < n; ++t) a += ph[t] * vst[t * ks + d];
         float* p = pr + (long long)h * nsplit * (hd + 2);
@@ -485,6 +505,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
         }
       }
     }
+    VTB_TL_MARK(3);
     __syncthreads();  // the next split reuses the staging and score buffers
   }
 }
@@ -509,16 +530,19 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) 
 // computed once into shared memory; each dimension's sum then has independent loads.
 __global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ att, RowInfo ri, int n_heads,
                                     int hd, int nsplit) {
+  VTB_TL(13);
   asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ float wsm[];  // [nsplit]
   __shared__ float red[32];
   const int h = blockIdx.x, r = blockIdx.y;
-  const int na = min(nsplit, ri.pos[r] / ATT_CHUNK + 1);  // positions are staged before the step
+  const int na = min(nsplit, ri.pos[r] / DEC_CHUNK + 1);  // positions are staged before the step
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   const float* p = part + ((long long)r * n_heads + h) * nsplit * (hd + 2);
   float M = -INFINITY;
   for (int s = threadIdx.x; s < na; s += blockDim.x) M = fmaxf(M, p[s * (hd + 2)]);
   M = block_reduce(M, true, red);
+  VTB_TL_MARK(0);
   float L = 0.f;
   for (int s = threadIdx.x; s < na; s += blockDim.x) {
     const float e = expf(p[s * (hd + 2)] - M);
@@ -526,12 +550,23 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, float* __res
     L += p[s * (hd + 2) + 1] * e;
   }
   L = block_reduce(L, false, red);  // its barriers also publish wsm
+  VTB_TL_MARK(1);
   const float invL = 1.0f / L;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+  // blockDim / hd groups of threads split the splits, so each thread's loads
+  // are few and all in flight at once; the groups add up in order.
+  float* gsum = wsm + nsplit;  // [groups][hd]
+  const int groups = max(1, (int)blockDim.x / hd), g = threadIdx.x / hd, d = threadIdx.x % hd;
+  if (g < groups) {
     float a = 0.f;
-#pragma unroll 4
-    for (int s = 0; s < na; ++s) a += p[s * (hd + 2) + 2 + d] * wsm[s];
-    att[((long long)r * n_heads + h) * hd + d] = a * invL;
+#pragma unroll 8
+    for (int s = g; s < na; s += groups) a += p[s * (hd + 2) + 2 + d] * wsm[s];
+    gsum[g * hd + d] = a;
+  }
+  __syncthreads();
+  for (int dd = threadIdx.x; dd < hd; dd += blockDim.x) {
+    float a = 0.f;
+    for (int q = 0; q < groups; ++q) a += gsum[q * hd + dd];
+    att[((long long)r * n_heads + h) * hd + dd] = a * invL;
   }
 }
 
@@ -554,8 +589,10 @@ __global__ void __launch_bounds__(PA_THREADS)
 attn_prefill_kernel(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
                     RowInfo ri, int rows, int layer, int n_layers, int max_seq, int n_heads, int n_kv,
                     float* __restrict__ att) {
+  VTB_TL(14);
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   using P = PaSmem<HD>;
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                          // [64 qvec][QS]
@@ -694,8 +731,10 @@ attn_prefill_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
 // swiglu (math.zig:154-161): h = (g / (1 + e^-g)) * u.  gu per row is
 // [gate | up], or with `il` the fused weights' [gate 8 | up 8] row blocks.
 __global__ void swiglu_kernel(const float* __restrict__ gu, float* __restrict__ h, int ffn, int rows, int il) {
+  VTB_TL(15);
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  VTB_TL_WAITED();
   const long long n = (long long)rows * ffn;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / ffn, j = i % ffn;
@@ -719,6 +758,7 @@ __device__ __forceinline__ void argmax_merge(float& bv, int& bi, float ov, int o
 
 __global__ void argmax_partial_kernel(const float* __restrict__ logits, float* __restrict__ pv, int* __restrict__ pi,
                                       int n) {
+  VTB_TL(16);
   const int r = blockIdx.y, b = blockIdx.x;
   const int slice = (n + ARGMAX_PARTS - 1) / ARGMAX_PARTS, i0 = b * slice, i1 = min(n, i0 + slice);
   const float* l = logits + (long long)r * n;
@@ -743,6 +783,7 @@ __global__ void argmax_partial_kernel(const float* __restrict__ logits, float* _
 }
 
 __global__ void argmax_final_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int32_t* __restrict__ out) {
+  VTB_TL(17);
   const int r = blockIdx.x, lane = threadIdx.x;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
@@ -1152,7 +1193,7 @@ VtbCudaState* vtb_cuda_state_create(VtbCudaModel* m, int32_t n_seqs, int32_t max
       return nullptr;
     }
   }
-  s->nsplit = (c.max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
+  s->nsplit = (c.max_seq + DEC_CHUNK - 1) / DEC_CHUNK;
   const size_t R = max_rows, d = c.dim, hd = c.head_dim, qd = (size_t)m->H * hd, kvd = (size_t)m->KV * hd, f = m->F;
   const size_t qkvw = qd + 2 * kvd;
   const size_t kmax = d > f ? d : f;
@@ -1434,7 +1475,7 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
     // (3 resident per SM at these sizes), each walking its row's live splits.
     // Prefill rows (enqueued directly): one CTA per live split of the longest row.
     const int zdec = std::max(1, 3 * 148 / (KV * R));
-    const int z = s->decode_rows ? std::min(s->nsplit, zdec) : std::min(s->nsplit, s->max_pos / ATT_CHUNK + 1);
+    const int z = s->decode_rows ? std::min(s->nsplit, zdec) : std::min(s->nsplit, s->max_pos / DEC_CHUNK + 1);
     const dim3 agrid(KV, R, z);
     switch (hd <= ATT_THREADS && hd % 16 == 0 ? G : 0) {  // register path needs hd <= 128, hd % 16 == 0
   #define VTB_ATT(g)                                                                                               \
@@ -1451,7 +1492,9 @@ static cudaError_t enqueue_layer(VtbCudaState* s, int l) {
                        s->nsplit, kcw, vcw, (const float*)s->rope);
     }
     if (e) return e;
-    if ((e = pdl_launch(attn_combine_kernel, dim3(H, R), dim3(128), (size_t)s->nsplit * 4, st, (const float*)s->part,
+    // 256 threads: the split weights, then blockDim / hd groups of partial sums
+    if ((e = pdl_launch(attn_combine_kernel, dim3(H, R), dim3(256), (size_t)(s->nsplit + 256 + hd) * 4, st,
+                        (const float*)s->part,
                         s->att, ri, H, hd, s->nsplit)))
       return e;
   }

@@ -63,6 +63,7 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ w, float* __restrict_
 template <int Q>
 __global__ void embed_kernel(const uint8_t* __restrict__ table, const int32_t* __restrict__ ids, float* __restrict__ out,
                              int dim, int n_tok) {
+  VTB_TL(18);
   constexpr int EL = Fmt<Q>::elems, BB = Fmt<Q>::bytes;
   const long long rb = (long long)(dim / EL) * BB;
   const int t = blockIdx.y;
