@@ -274,7 +274,7 @@ static_assert(ATT_TPP * DEC_CHUNK == ATT_THREADS && (ATT_TPP & (ATT_TPP - 1)) ==
 __host__ __device__ inline int attn_smem_floats(int G, int hd) {
   const int slices = ATT_THREADS / hd > 0 ? ATT_THREADS / hd : 1;
   const int scf = G * DEC_CHUNK > slices * G * hd ? G * DEC_CHUNK : slices * G * hd;
-  return G * hd + scf + 2 * DEC_CHUNK * (hd + ATT_PAD) + hd;  // + the (cos, sin) pairs of the row's position
+  return G * hd + scf + 2 * DEC_CHUNK * (hd + ATT_PAD);
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -322,32 +322,49 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   float* vst = kst + DEC_CHUNK * ks;
   const long long lbase = ((long long)seq * n_layers + layer) * max_seq;
   // Stage split sp's K and V rows (all but the row this step writes itself).
+  // One bulk copy per K row and per V row (hd * 4 bytes each, 16-byte aligned
+  // rows), issued by warp 0 and counted on two mbarriers (K, V); the split's
+  // k-th staging completes phase k & 1 of both.
+  __shared__ __align__(8) uint64_t kvbar[2];
+  if (threadIdx.x == 0) {
+    mbar_init(&kvbar[0], 1);
+    mbar_init(&kvbar[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int lane0 = threadIdx.x & 31;
   auto stage = [&](int spl) {
+    if (threadIdx.x >= 32) return;
     const int t0 = spl * DEC_CHUNK, n = min(len, t0 + DEC_CHUNK) - t0;
     const int own = (kcw && spl == pos / DEC_CHUNK) ? pos - t0 : -1;
-    for (int i = threadIdx.x; i < n * h4; i += ATT_THREADS) {
-      const int t = i / h4, c4 = 4 * (i % h4);
-      if (t != own) cp_async16(kst + t * ks + c4, kc + (lbase + t0 + t) * kvd + kvh * hd + c4);
+    const unsigned bytes = (unsigned)((n - (own >= 0 ? 1 : 0)) * hd * 4);
+    if (lane0 == 0) {
+      mbar_expect_tx(&kvbar[0], bytes);
+      mbar_expect_tx(&kvbar[1], bytes);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    for (int i = threadIdx.x; i < n * h4; i += ATT_THREADS) {
-      const int t = i / h4, c4 = 4 * (i % h4);
-      if (t != own) cp_async16(vst + t * ks + c4, vc + (lbase + t0 + t) * kvd + kvh * hd + c4);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    __syncwarp();
+    for (int t = lane0; t < n; t += 32)
+      if (t != own) {
+        const long long src = (lbase + t0 + t) * kvd + kvh * hd;
+        bulk_g2s(kst + t * ks, kc + src, (unsigned)(hd * 4), &kvbar[0]);
+        bulk_g2s(vst + t * ks, vc + src, (unsigned)(hd * 4), &kvbar[1]);
+      }
   };
   const bool early = kcw != nullptr;
-  float* csm = vst + DEC_CHUNK * ks;  // [hd]: (cos, sin) of each rotated pair at the row's position
-  if (early) {
-    stage(sp);
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) csm[i] = rope[(long long)pos * hd + i];
-    __syncthreads();
-  }
+  // (cos, sin) of the rotated pairs at the row's position.  With ATT_THREADS a
+  // multiple of hd / 2 every pair a thread rotates (q heads and the own K row)
+  // is pair threadIdx.x % (hd / 2): one load, issued before the staging copies
+  // so it does not queue behind them.
+  const int half = hd / 2;
+  const float2* cs2 = reinterpret_cast<const float2*>(rope + (long long)pos * hd);
+  const bool cs_one = ATT_THREADS % half == 0;
+  float2 cs_mine = make_float2(1.f, 0.f);
+  if (kcw && cs_one) cs_mine = cs2[threadIdx.x % half];
+  if (early) stage(sp);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   VTB_TL_WAITED();
   const float inv_sqrt_hd = 1.0f / sqrtf((float)hd);
   const float* q = qkv + (long long)r * (qd + 2 * kvd) + kvh * G * hd;
-  const int half = hd / 2;
   // The row's own K / V (this step's QKV output): rotated K and V go to the
   // cache and to the staged rows of the split that holds `pos`.
   auto own_row = [&](int own) {
@@ -356,7 +373,8 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     const long long slot = (lbase + pos) * kvd + kvh * hd;
     for (int p = threadIdx.x; p < half; p += blockDim.x) {
       const int i = 2 * p;
-      const float c = csm[i], sn = csm[i + 1];
+      const float2 t = cs_one ? cs_mine : cs2[p];
+      const float c = t.x, sn = t.y;
       const float2 xk = *reinterpret_cast<const float2*>(kr + i);
       const float a = xk.x * c, b = xk.y * sn, pp = xk.x * sn, qq = xk.y * c;
       const float k0 = a - b, k1 = pp + qq;
@@ -375,7 +393,8 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
     for (int p = threadIdx.x; p < G * half; p += blockDim.x) {
       const int h = p / half, i = 2 * (p % half);
       const float2 xq = *reinterpret_cast<const float2*>(q + h * hd + i);
-      const float c = csm[i], sn = csm[i + 1];
+      const float2 t = cs_one ? cs_mine : cs2[i / 2];
+      const float c = t.x, sn = t.y;
       const float a = xq.x * c, b = xq.y * sn, pp = xq.x * sn, qq = xq.y * c;
       qs[h * hd + i] = a - b;
       qs[h * hd + i + 1] = pp + qq;
@@ -387,14 +406,15 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float hm[64], hl[64];
-  for (bool first = true; sp < nsp; sp += gridDim.z, first = false) {
+  unsigned kvphase = 0;
+  for (bool first = true; sp < nsp; sp += gridDim.z, first = false, kvphase ^= 1u) {
     const int t0 = sp * DEC_CHUNK, t1 = min(len, t0 + DEC_CHUNK), n = t1 - t0;
     float* pr = part + (((long long)r * n_heads + kvh * G) * nsplit + sp) * (hd + 2);  // head stride nsplit*(hd+2)
     const int own = (kcw && sp == pos / DEC_CHUNK) ? pos - t0 : -1;  // staged row this CTA writes itself
     if (!(first && early)) stage(sp);
     if (own >= 0 && !first) own_row(own);  // (the first split's own row went in with q)
     VTB_TL_MARK(0);
-    asm volatile("cp.async.wait_group 1;" ::: "memory");  // K staged (V may still be in flight)
+    mbar_wait_bounded(&kvbar[0], kvphase);  // K staged (V may still be in flight)
     __syncthreads();
     VTB_TL_MARK(1);
     // scores: ATT_TPP threads per position, each over every ATT_TPP-th float4 column of the staged K row
@@ -456,7 +476,7 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
         hl[h] = l;
       }
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");  // V staged
+    mbar_wait_bounded(&kvbar[1], kvphase);  // V staged
     __syncthreads();
     VTB_TL_MARK(2);
     // acc[h][d] = sum_t p[h][t] v[t][d]: thread (slice, d) reads staged v[t][d] once for every
@@ -506,7 +526,10 @@ attn_partial_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
       }
     }
     VTB_TL_MARK(3);
-    __syncthreads();  // the next split reuses the staging and score buffers
+    // the next split reuses the staging and score buffers: the bulk copies (async
+    // proxy) may overwrite what was just read only after every thread's reads
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
   }
 }
 
