@@ -775,6 +775,29 @@ def run_profile_case(case: str) -> None:
         st.prefill(np.arange(3, 131))
         for i in range(5):
             st.step([5 + i], want_logits=False)
+    elif case == "sampler":  # device sampler: 20 launches per (vocabulary, rows, config), D2H beside it
+        for rows, n in ((1, 32000), (1, 128256), (32, 128256)):
+            lg = torch.randn(rows, n, device="cuda") * 3
+            u = np.random.default_rng(0).random(rows, dtype=np.float32)
+            for cfg in ((0.0, 0, 0.0), (0.8, 0, 0.0), (0.8, 40, 0.0), (0.8, 0, 0.9), (0.7, 50, 0.95)):
+                bufs = [lg.clone() for _ in range(20)]
+                for b in bufs[:3]:
+                    ops.sample(b, *cfg, u)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for b in bufs[3:]:
+                    ops.sample(b, *cfg, u)
+                e1.record()
+                torch.cuda.synchronize()
+                print(f"rows {rows} n {n} cfg {cfg}: {e0.elapsed_time(e1) / 17 * 1000:.1f} us per call (host-paced)")
+            h = torch.empty(rows, n, pin_memory=True)
+            e0.record()
+            for _ in range(17):
+                h.copy_(lg, non_blocking=True)
+            e1.record()
+            torch.cuda.synchronize()
+            print(f"rows {rows} n {n}: D2H of the logits {e0.elapsed_time(e1) / 17 * 1000:.1f} us")
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()
@@ -783,7 +806,7 @@ def run_profile_case(case: str) -> None:
 
 
 PROFILE_CASES = ["gemv", "gemv_chain", "gemv_q6k", "gemv_q8", "gemm", "gemm_precise", "gemm_b32", "gemm_b32_q4k", "decode", "decode8b",
-                 "decode8b_b32"]
+                 "decode8b_b32", "sampler"]
 
 
 def main():

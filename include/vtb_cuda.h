@@ -318,6 +318,37 @@ int vtb_cuda_step(VtbCudaState *s, const int32_t *tokens, float *logits, int32_t
 int vtb_cuda_prefill(VtbCudaState *s, int32_t seq, const int32_t *tokens, int32_t n, float *logits,
                      int32_t *argmax);
 
+/* ---- token sampling on the device (Sampler.sample, src/runtime/sampler.zig:44-104) ----
+ * Same fields, meaning and layout as the reference's VtbSamplerConfig
+ * (include/vantablack.h:46-51).  temperature 0 = greedy argmax; top_k 0 =
+ * off; top_p 0 or >= 1 = off.  The PRNG stays with the caller: `u` holds one
+ * uniform draw in [0, 1) per row (what prng.random().float(f32) returns at
+ * sampler.zig:92), so `seed` is not read here.  Logits are rewritten in place
+ * with the pipeline's probabilities, as the reference mutates them.  Tokens
+ * equal the reference's for the same logits and draw unless the draw falls
+ * within a few ulp of a cumulative-probability boundary (the sums are formed
+ * in another order); argmax, the top-k cut and the nucleus set are exact.
+ * Logits must be finite or -inf.  rows <= 256, n <= 2^24. */
+typedef struct VtbCudaSamplerConfig {
+  float temperature;
+  size_t top_k;
+  float top_p;
+  uint64_t seed;
+} VtbCudaSamplerConfig;
+
+/* logits: device [rows][ld] f32 (first n of each row used), u: host [rows]
+ * (may be NULL when temperature == 0), tokens: device [rows] int32. */
+int vtb_cuda_sample(float *logits, int64_t rows, int64_t n, int64_t ld, const VtbCudaSamplerConfig *cfg,
+                    const float *u, int32_t *tokens, void *stream);
+
+/* Sample rows [0, rows) of the state's logits after vtb_cuda_step /
+ * vtb_cuda_final_step (one row per sequence) or vtb_cuda_prefill (row 0),
+ * and copy the rows' tokens to the host: 4 bytes per sequence cross PCIe
+ * instead of the f32[vocab] row that finalize_token would copy for the
+ * reference's host-side Sampler.sample (stream.zig:82, 96). */
+int vtb_cuda_state_sample(VtbCudaState *s, int32_t rows, const VtbCudaSamplerConfig *cfg, const float *u,
+                          int32_t *tokens);
+
 /* ------------------------------------------------------------------ */
 /* Tensor parallelism (NCCL over NVLink/NVSwitch; no counterpart in the   */
 /* reference, which is single-device)                                   */

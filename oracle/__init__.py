@@ -66,6 +66,7 @@ def _load():
         "vtbo_geglu": (None, [_f32p, _f32p, _sz]),
         "vtbo_add_into": (None, [_f32p, _f32p, _sz]),
         "vtbo_argmax": (_sz, [_f32p, _sz]),
+        "vtbo_sample": (C.c_uint32, [_f32p, _sz, C.c_float, _sz, C.c_float, C.c_float]),
         "vtbo_model_create": (C.c_void_p, [C.c_void_p, C.c_void_p, _u8p, C.c_int, _f32p, _u8p, C.c_int]),
         "vtbo_model_destroy": (None, [C.c_void_p]),
         "vtbo_model_set_q8_activations": (None, [C.c_void_p, C.c_int]),
@@ -229,6 +230,14 @@ def add_into(a, b):
 def argmax(x) -> int:
     x = np.ascontiguousarray(x, np.float32)
     return lib.vtbo_argmax(_p(x, _f32p), x.size)
+
+
+def sample(logits, temperature: float, top_k: int, top_p: float, u: float):
+    """Sampler.sample (sampler.zig:44-104) with the draw ``u`` supplied.
+    Returns (token, logits after the in-place pipeline)."""
+    a = np.ascontiguousarray(logits, dtype=np.float32).copy()
+    t = lib.vtbo_sample(_p(a, _f32p), a.size, float(temperature), int(top_k), float(top_p), float(u))
+    return int(t), a
 
 
 class _Config(C.Structure):

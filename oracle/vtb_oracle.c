@@ -597,6 +597,72 @@ size_t vtbo_argmax(const float *x, size_t n) {
     return bi;
 }
 
+/* ---------------- token sampler ---------------- */
+/*
+ * Sampler.sample, src/runtime/sampler.zig:44-104, with the PRNG draw taken
+ * as an argument: `u` stands for `self.prng.random().float(f32)` (:92), so
+ * the rest of the pipeline can be compared draw for draw.  The index sorts
+ * (:58, :70) are std.mem.sort, a stable sort, by descending logit: restated
+ * as qsort with the index as the tie-break, which orders the same.
+ * `logits` is mutated in place, as in the reference.
+ */
+static const float *g_sort_keys;
+static int desc_stable(const void *a, const void *b) {
+    size_t i = *(const size_t *)a, j = *(const size_t *)b;
+    float x = g_sort_keys[i], y = g_sort_keys[j];
+    if (x > y) return -1;
+    if (y > x) return 1;
+    return (i > j) - (i < j);
+}
+
+uint32_t vtbo_sample(float *logits, size_t n, float temperature, size_t top_k, float top_p, float u) {
+    if (temperature == 0.0f) return (uint32_t)vtbo_argmax(logits, n); /* :45-47 */
+    const float inv_t = 1.0f / temperature;                             /* :50-51 */
+    for (size_t i = 0; i < n; i++) logits[i] *= inv_t;
+    size_t *idx = NULL;
+    if ((top_k > 0 && top_k < n) || (top_p > 0.0f && top_p < 1.0f)) {
+        idx = (size_t *)malloc(n * sizeof *idx);
+        if (!idx) return 0;
+    }
+    if (top_k > 0 && top_k < n) { /* :54-63 */
+        for (size_t i = 0; i < n; i++) idx[i] = i;
+        g_sort_keys = logits;
+        qsort(idx, n, sizeof *idx, desc_stable);
+        const float threshold = logits[idx[top_k - 1]];
+        for (size_t i = 0; i < n; i++)
+            if (logits[i] < threshold) logits[i] = -INFINITY;
+    }
+    vtbo_softmax(logits, n); /* :65 */
+    if (top_p > 0.0f && top_p < 1.0f) { /* :68-89 */
+        for (size_t i = 0; i < n; i++) idx[i] = i;
+        g_sort_keys = logits;
+        qsort(idx, n, sizeof *idx, desc_stable);
+        float cumulative = 0.0f;
+        size_t cutoff = n;
+        for (size_t r = 0; r < n; r++) {
+            cumulative += logits[idx[r]];
+            if (cumulative >= top_p) { cutoff = r + 1; break; }
+        }
+        for (size_t r = cutoff; r < n; r++) logits[idx[r]] = 0.0f;
+        float sum = 0.0f;
+        for (size_t i = 0; i < n; i++) sum += logits[i];
+        if (sum > 0.0f) {
+            const float inv = 1.0f / sum;
+            for (size_t i = 0; i < n; i++) logits[i] *= inv;
+        }
+    }
+    free(idx);
+    float acc = 0.0f; /* :92-97 */
+    for (size_t i = 0; i < n; i++) {
+        acc += logits[i];
+        if (u <= acc) return (uint32_t)i;
+    }
+    size_t last = 0; /* :98-103 */
+    for (size_t i = 0; i < n; i++)
+        if (logits[i] > 0.0f) last = i;
+    return (uint32_t)last;
+}
+
 /* ---------------- Llama forward ---------------- */
 struct vtbo_model {
     vtbo_config c;

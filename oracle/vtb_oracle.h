@@ -85,6 +85,8 @@ void vtbo_swiglu(float *gate, const float *up, size_t n);
 void vtbo_geglu(float *gate, const float *up, size_t n);
 void vtbo_add_into(float *a, const float *b, size_t n);
 size_t vtbo_argmax(const float *x, size_t n);
+/* Sampler.sample (sampler.zig:44-104) with the uniform draw u in [0, 1) supplied. */
+uint32_t vtbo_sample(float *logits, size_t n, float temperature, size_t top_k, float top_p, float u);
 
 /* Llama forward (forward.zig / prefill.zig / kv_cache.zig). */
 typedef struct {

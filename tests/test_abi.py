@@ -62,3 +62,21 @@ def test_capabilities_slot_without_a_device(lib):
     assert (c.supports_fused_qkv, c.supports_kquant_gpu, c.supports_mlx_q4, c.unified_memory) == (1, 1, 0, 0)
     assert b"b200" in c.name
     assert lib.vtb_cuda_capabilities(None, None) == -1
+
+
+def test_sampler_argument_checks_without_launch(lib):
+    """vtb_cuda_sample / vtb_cuda_state_sample reject bad configurations on the host."""
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    u = (ctypes.c_float * 1)(0.5)
+    cfg = _lib.SamplerConfig(-1.0, 0, 0.0, 0)  # negative temperature
+    assert lib.vtb_cuda_sample(p, 1, 8, 8, ctypes.byref(cfg), u, p, None) == -1
+    cfg = _lib.SamplerConfig(float("nan"), 0, 0.0, 0)
+    assert lib.vtb_cuda_sample(p, 1, 8, 8, ctypes.byref(cfg), u, p, None) == -1
+    cfg = _lib.SamplerConfig(1.0, 0, 0.9, 0)
+    assert lib.vtb_cuda_sample(p, 0, 8, 8, ctypes.byref(cfg), u, p, None) == -1    # no rows
+    assert lib.vtb_cuda_sample(p, 257, 8, 8, ctypes.byref(cfg), u, p, None) == -1  # above 256 rows
+    assert lib.vtb_cuda_sample(p, 1, 8, 4, ctypes.byref(cfg), u, p, None) == -1    # stride below n
+    assert lib.vtb_cuda_sample(p, 1, 8, 8, ctypes.byref(cfg), None, p, None) == -1  # no draws
+    assert lib.vtb_cuda_sample(p, 1, 8, 8, None, u, p, None) == -1
+    assert lib.vtb_cuda_state_sample(None, 1, ctypes.byref(cfg), u, p) == -1

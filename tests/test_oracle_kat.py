@@ -178,3 +178,36 @@ def test_q8_0_quantizer_rule():
     q = np.sign(v) * np.floor(np.abs(v) + np.float32(0.5))  # round half away from zero
     assert np.array_equal(qs.reshape(-1, 32), q.astype(np.int8))
     assert np.abs(qs).max() <= 127
+
+
+def test_sampler_greedy_kat():  # sampler.zig:113-119
+    assert O.sample([0.1, 0.5, 2.0, 0.3, 1.2], 0.0, 0, 0.0, 0.7)[0] == 2
+
+
+def test_sampler_deterministic_kat():  # sampler.zig:121-130 (same draw, same token)
+    a = O.sample([1.0, 2.0, 3.0, 4.0, 5.0], 1.0, 0, 0.0, 0.42)[0]
+    b = O.sample([1.0, 2.0, 3.0, 4.0, 5.0], 1.0, 0, 0.0, 0.42)[0]
+    assert a == b
+
+
+def test_sampler_top_k1_is_greedy_kat():  # sampler.zig:132-138, for any draw
+    for u in (1e-7, 0.3, 0.999999):  # u = 0 would stop at index 0 (u <= acc = 0), as in the reference
+        assert O.sample([0.1, 0.5, 2.0, 0.3, 1.2], 1.0, 1, 0.0, u)[0] == 2
+
+
+def test_sampler_pipeline_by_hand():
+    """Temperature, top-k ties, nucleus cut and the CDF walk against a float64
+    restatement of sampler.zig:49-97 on a case whose boundaries are far from u."""
+    logits = np.array([1.0, 3.0, 3.0, 0.5, 2.0, -1.0], np.float32)
+    tok, p = O.sample(logits, 0.5, 4, 0.8, 0.7)
+    z = logits.astype(np.float64) / 0.5
+    thr = np.sort(z)[::-1][3]
+    z[z < thr] = -np.inf
+    q = np.exp(z - z.max()); q /= q.sum()
+    order = sorted(range(6), key=lambda i: (-q[i], i))
+    c = np.cumsum(q[order]); cut = int(np.argmax(c >= 0.8)) + 1
+    for i in order[cut:]:
+        q[i] = 0
+    q /= q.sum()
+    assert np.allclose(p, q, atol=1e-6)
+    assert tok == int(np.argmax(np.cumsum(q) >= 0.7))

@@ -80,6 +80,8 @@ SIGNATURES = {
     "vtb_cuda_finalize_token": (_int, [_vp, _vp, _vp]),
     "vtb_cuda_step": (_int, [_vp, _vp, _vp, _vp]),
     "vtb_cuda_prefill": (_int, [_vp, _i32, _vp, _i32, _vp, _vp]),
+    "vtb_cuda_sample": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "vtb_cuda_state_sample": (_int, [_vp, _i32, _vp, _vp, _vp]),
     "vtb_cuda_tp_unique_id": (_int, [_vp]),
     "vtb_cuda_tp_init": (_vp, [_int, _int, _int, _vp]),
     "vtb_cuda_tp_destroy": (None, [_vp]),
@@ -101,6 +103,11 @@ SIGNATURES = {
     "vtb_cuda_model_create_gguf": (_vp, [_vp, _vp, _i32]),
     "vtb_cuda_model_create_gguf_tp": (_vp, [_vp, _vp, _vp, _i32]),
 }
+
+
+class SamplerConfig(C.Structure):
+    """VtbCudaSamplerConfig: the reference's VtbSamplerConfig (include/vantablack.h:46-51)."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_size_t), ("top_p", C.c_float), ("seed", C.c_uint64)]
 
 
 class VtbError(RuntimeError):

@@ -13,3 +13,4 @@
 #include "model.cu"
 #include "gguf.cu"
 #include "noalloc.cu"
+#include "sampler.cu"

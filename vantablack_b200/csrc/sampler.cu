@@ -1,0 +1,488 @@
+// sampler.cu -- token sampling on the device: Sampler.sample
+// (src/runtime/sampler.zig:44-104) over logits that never leave HBM, so a
+// decode step reads back one int32 per sequence instead of f32[vocab].
+//
+// Pipeline per row (one 1024-thread CTA per row, logits rewritten in place as
+// the reference does):
+//   temperature == 0     -> argmax, first index of the maximum (math.zig:190-201)
+//   scale by 1/T         (sampler.zig:50-51; 1/T computed on the host in f32)
+//   top-k                (:54-63) the k-th largest value found by a 4-pass radix
+//                        select on order-preserving 32-bit keys (exact, equal to
+//                        the value at sorted position k-1); values below it
+//                        become probability 0, as -inf does through the softmax
+//   softmax              (math.zig:136-150) expf, block-reduced sum, 1/sum
+//   top-p                (:68-89) the nucleus cut located by a second radix walk
+//                        over the probabilities' bit patterns, descending, with
+//                        per-bucket sums in 2^-31 fixed point (integer adds, so
+//                        the cut is the same on every run); ties at the cut
+//                        value are kept in ascending index order, which is the
+//                        stable sort's order; then renormalise
+//   CDF walk             (:92-103) first index with u <= running sum, from a
+//                        scan over contiguous per-warp chunks (coalesced loads,
+//                        shuffle scans); if u is never reached, the last index
+//                        with nonzero mass
+//
+// The uniform draw u (the reference's prng.random().float(f32), :92) is an
+// argument: the caller owns the generator.  Sums are formed in a different
+// order than the reference's sequential loops, so probabilities agree to a
+// few ulp and the token agrees unless u falls within that distance of a CDF
+// boundary; argmax, the top-k threshold and the set of kept ties are exact.
+#include "common.cuh"
+
+namespace vtb {
+
+constexpr int SMP_THREADS = 1024;
+constexpr int SMP_MAX_ROWS = 256;
+constexpr float SMP_FX = 2147483648.0f;  // 2^31: fixed-point scale of the nucleus sums (total mass <= 1 fits u32)
+
+struct SampleArgs {
+  float inv_t;
+  int greedy;
+  int top_k;    // 0: off
+  float top_p;  // applied when use_p
+  int use_p;
+  float u[SMP_MAX_ROWS];
+};
+
+// Order-preserving key of a float (larger float -> larger key); -0 folds onto
+// +0 so that they compare equal, as the reference's float comparisons do.
+__device__ __forceinline__ uint32_t smp_key(float f) {
+  uint32_t b = __float_as_uint(f);
+  if (f == 0.f) b = 0u;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float smp_unkey(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+struct SmpShared {
+  uint32_t cnt[256];
+  uint32_t sum[256];
+  float red[32];
+  int redi[32];
+  uint32_t prefix, mask, remaining;
+  unsigned long long above;
+  int nocut;
+  float bcast;
+  int bcasti;
+};
+
+__device__ __forceinline__ float smp_block_sum(float v, SmpShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) sh.red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = sh.red[lane];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) sh.bcast = v;
+  }
+  __syncthreads();
+  return sh.bcast;
+}
+
+__device__ __forceinline__ float smp_block_max(float v, SmpShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) sh.red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = sh.red[lane];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) sh.bcast = v;
+  }
+  __syncthreads();
+  return sh.bcast;
+}
+
+// Block minimum (MIN = true) or maximum of an int.
+template <bool MIN>
+__device__ __forceinline__ int smp_block_int(int v, SmpShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const int w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = MIN ? min(v, w) : max(v, w);
+  }
+  if (lane == 0) sh.redi[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = sh.redi[lane];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const int w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = MIN ? min(v, w) : max(v, w);
+    }
+    if (lane == 0) sh.bcasti = v;
+  }
+  __syncthreads();
+  return sh.bcasti;
+}
+
+// One radix level, descending.  Warp 0 picks the highest bin at which the
+// running total (COUNT: sh.cnt against sh.remaining; else sh.sum added to
+// sh.above against target) is reached, and narrows prefix/mask to it; when
+// no bin reaches the target it sets sh.nocut.
+template <bool COUNT>
+__device__ __forceinline__ void smp_pick_bin(SmpShared& sh, int shift, unsigned long long target) {
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    // lane l owns bins 255-8l down to 248-8l
+    unsigned long long s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += COUNT ? (unsigned long long)sh.cnt[255 - 8 * lane - j] : sh.sum[255 - 8 * lane - j];
+    unsigned long long c = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long w = __shfl_up_sync(0xffffffffu, c, o);
+      if (lane >= o) c += w;
+    }
+    const unsigned long long base = COUNT ? 0ull : sh.above;
+    const unsigned long long need = COUNT ? (unsigned long long)sh.remaining : target;
+    const unsigned ball = __ballot_sync(0xffffffffu, base + c >= need);
+    if (ball == 0u) {
+      if (lane == 0) sh.nocut = 1;
+    } else if (lane == __ffs(ball) - 1) {
+      unsigned long long run = c - s;  // total of the higher lanes' bins
+      int b = 255 - 8 * lane;
+      for (int j = 0; j < 8; ++j, --b) {
+        const unsigned long long v = COUNT ? (unsigned long long)sh.cnt[b] : sh.sum[b];
+        if (base + run + v >= need) break;
+        run += v;
+      }
+      if (COUNT) sh.remaining -= (uint32_t)run;
+      else sh.above += run;
+      sh.prefix |= (uint32_t)b << shift;
+      sh.mask |= 255u << shift;
+    }
+  }
+  __syncthreads();
+}
+
+template <int V>
+__device__ __forceinline__ void smp_ld(const float* p, float (&x)[V]) {
+  if constexpr (V == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    x[0] = t.x; x[1] = t.y; x[2] = t.z; x[3] = t.w;
+  } else {
+    x[0] = *p;
+  }
+}
+template <int V>
+__device__ __forceinline__ void smp_st(float* p, const float (&x)[V]) {
+  if constexpr (V == 4) *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+  else *p = x[0];
+}
+
+// V = 4: rows of a multiple of 4 floats on 16-byte boundaries, read as float4;
+// V = 1 otherwise.  The row keeps the raw logits until the softmax pass; 1/T
+// and 1/sum are re-applied on the fly (the same f32 products each time) so
+// the passes before it only read.
+template <int V>
+__global__ void __launch_bounds__(SMP_THREADS, 1)
+sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_constant__ SampleArgs a,
+              int32_t* __restrict__ tokens) {
+  __shared__ SmpShared sh;
+  __shared__ float ftot[32];
+  float* L = logits + (long long)blockIdx.x * ld;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nu = n / V;  // units of V floats
+
+  if (a.greedy) {  // argmax: largest value, first index on ties
+    float bv = -INFINITY;
+    int bi = n;
+    for (int u = tid; u < nu; u += SMP_THREADS) {
+      float x[V];
+      smp_ld<V>(L + u * V, x);
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        if (bi == n || x[k] > bv) { bv = x[k]; bi = u * V + k; }  // ascending: this thread's first maximum
+    }
+    const float m = smp_block_max(bv, sh);
+    const int idx = smp_block_int<true>((bv == m && bi < n) ? bi : n, sh);
+    if (tid == 0) tokens[blockIdx.x] = idx < n ? idx : 0;
+    return;
+  }
+
+  // Maximum of the scaled logits (masking keeps it, so it is the softmax's).
+  const float inv_t = a.inv_t;
+  float mx = -INFINITY;
+  for (int u = tid; u < nu; u += SMP_THREADS) {
+    float x[V];
+    smp_ld<V>(L + u * V, x);
+#pragma unroll
+    for (int k = 0; k < V; ++k) mx = fmaxf(mx, x[k] * inv_t);
+  }
+  mx = smp_block_max(mx, sh);
+
+  // top-k threshold: the k-th largest scaled value.
+  float thr = -INFINITY;
+  const bool use_k = a.top_k > 0 && a.top_k < n;
+  if (use_k) {
+    if (tid == 0) { sh.prefix = 0u; sh.mask = 0u; sh.remaining = (uint32_t)a.top_k; sh.nocut = 0; }
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += SMP_THREADS) sh.cnt[b] = 0u;
+      __syncthreads();
+      const uint32_t pre = sh.prefix, msk = sh.mask;
+      for (int u = tid; u < nu; u += SMP_THREADS) {
+        float x[V];
+        smp_ld<V>(L + u * V, x);
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+          const uint32_t key = smp_key(x[k] * inv_t);
+          if ((key & msk) == pre) atomicAdd(&sh.cnt[(key >> shift) & 255u], 1u);
+        }
+      }
+      __syncthreads();
+      smp_pick_bin<true>(sh, shift, 0ull);
+    }
+    thr = smp_unkey(sh.prefix);
+  }
+
+  // softmax numerators (masked entries are exp(-inf) = 0 in the reference).
+  float s = 0.f;
+  for (int u = tid; u < nu; u += SMP_THREADS) {
+    float x[V];
+    smp_ld<V>(L + u * V, x);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float v = x[k] * inv_t;
+      x[k] = (use_k && v < thr) ? 0.f : expf(v - mx);
+      s += x[k];
+    }
+    smp_st<V>(L + u * V, x);
+  }
+  const float inv = 1.0f / smp_block_sum(s, sh);  // its barriers publish the numerators
+
+  // Warp w owns the contiguous units [w*cw, w*cw + cw), walked 32 units (one
+  // coalesced load per lane) at a time, so index order is (step, lane, k).
+  const int cw = ((nu + SMP_THREADS - 1) / SMP_THREADS) * 32;
+  const int w0 = min(nu, warp * cw), w1 = min(nu, w0 + cw);
+  float renorm = 1.f;
+  bool use_renorm = false;
+  if (a.use_p) {  // nucleus over p = e * inv
+    const unsigned long long target = (unsigned long long)ceil((double)a.top_p * (double)SMP_FX);
+    if (tid == 0) { sh.prefix = 0u; sh.mask = 0u; sh.above = 0ull; sh.nocut = 0; }
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += SMP_THREADS) { sh.cnt[b] = 0u; sh.sum[b] = 0u; }
+      __syncthreads();
+      if (sh.nocut) break;
+      const uint32_t pre = sh.prefix, msk = sh.mask;
+      for (int u = tid; u < nu; u += SMP_THREADS) {
+        float x[V];
+        smp_ld<V>(L + u * V, x);
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+          const float p = x[k] * inv;
+          const uint32_t key = __float_as_uint(p);  // p >= +0: the raw bits order like the values
+          if ((key & msk) == pre) {
+            const uint32_t b = (key >> shift) & 255u;
+            atomicAdd(&sh.cnt[b], 1u);
+            atomicAdd(&sh.sum[b], __float2uint_rn(p * SMP_FX));
+          }
+        }
+      }
+      __syncthreads();
+      smp_pick_bin<false>(sh, shift, target);
+    }
+    const bool nocut = sh.nocut != 0;
+    const uint32_t kstar = sh.prefix;
+    // Ties at the cut value to keep: the fewest that reach the target.
+    long long keep_ties = 0;
+    if (!nocut) {
+      const unsigned long long vfx = __float2uint_rn(__uint_as_float(kstar) * SMP_FX);
+      const unsigned long long rest = target - sh.above;  // > 0 by construction
+      keep_ties = vfx ? (long long)((rest + vfx - 1) / vfx) : 1;
+      if (keep_ties < 1) keep_ties = 1;
+    }
+    // Rank of this warp's first tie among all ties, in index order.
+    int my_ties = 0;
+    if (!nocut)
+      for (int j = w0; j < w1; j += 32) {
+        const int u = j + lane;
+        if (u < w1) {
+          float x[V];
+          smp_ld<V>(L + u * V, x);
+#pragma unroll
+          for (int k = 0; k < V; ++k) my_ties += __float_as_uint(x[k] * inv) == kstar;
+        }
+      }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) my_ties += __shfl_xor_sync(0xffffffffu, my_ties, o);
+    if (lane == 0) sh.redi[warp] = my_ties;
+    __syncthreads();
+    long long rank = 0;
+    for (int w = 0; w < warp; ++w) rank += sh.redi[w];
+    __syncthreads();
+    // Keep or zero each p; the row now holds the nucleus probabilities.
+    float kept = 0.f;
+    for (int j = w0; j < w1; j += 32) {
+      const int u = j + lane;
+      float x[V];
+      int tl = 0;
+      if (u < w1) {
+        smp_ld<V>(L + u * V, x);
+#pragma unroll
+        for (int k = 0; k < V; ++k) { x[k] *= inv; tl += __float_as_uint(x[k]) == kstar; }
+      }
+      int ex = tl;  // ties of the lower lanes of this step
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int w = __shfl_up_sync(0xffffffffu, ex, o);
+        if (lane >= o) ex += w;
+      }
+      const int step_ties = __shfl_sync(0xffffffffu, ex, 31);
+      ex -= tl;
+      if (u < w1) {
+        long long r = rank + ex;
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+          const uint32_t key = __float_as_uint(x[k]);
+          bool keep = true;
+          if (!nocut) {
+            keep = key > kstar;
+            if (key == kstar) keep = r++ < keep_ties;
+          }
+          if (!keep) x[k] = 0.f;
+          kept += x[k];
+        }
+        smp_st<V>(L + u * V, x);
+      }
+      rank += step_ties;
+    }
+    const float tot = smp_block_sum(kept, sh);  // its barriers publish the row
+    if (tot > 0.f) { use_renorm = true; renorm = 1.0f / tot; }
+  }
+
+  // CDF walk: final probabilities written back, warp totals, an exclusive
+  // scan over warps, then each warp scans its range until the sum reaches u.
+  float cs = 0.f;
+  int last = -1;
+  for (int j = w0; j < w1; j += 32) {
+    const int u = j + lane;
+    if (u < w1) {
+      float x[V];
+      smp_ld<V>(L + u * V, x);
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        if (!a.use_p) x[k] *= inv;
+        else if (use_renorm) x[k] *= renorm;
+        cs += x[k];
+        if (x[k] > 0.f) last = u * V + k;
+      }
+      smp_st<V>(L + u * V, x);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+  if (lane == 0) ftot[warp] = cs;
+  __syncthreads();  // also publishes the final row
+  float acc = 0.f;
+  for (int w = 0; w < warp; ++w) acc += ftot[w];
+  const float ud = a.u[blockIdx.x];
+  int cand = n;
+  for (int j = w0; j < w1; j += 32) {
+    const int u = j + lane;
+    float x[V];
+    float lt = 0.f;
+    if (u < w1) {
+      smp_ld<V>(L + u * V, x);
+#pragma unroll
+      for (int k = 0; k < V; ++k) lt += x[k];
+    }
+    float inc = lt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float w = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += w;
+    }
+    float run = acc + __shfl_up_sync(0xffffffffu, inc, 1);
+    if (lane == 0) run = acc;
+    int hit = -1;
+    if (u < w1) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        run += x[k];
+        if (hit < 0 && ud <= run) hit = k;
+      }
+    }
+    const unsigned hb = __ballot_sync(0xffffffffu, hit >= 0);
+    if (hb) {
+      const int fl = __ffs(hb) - 1;
+      cand = (j + fl) * V + __shfl_sync(0xffffffffu, hit, fl);
+      break;
+    }
+    acc += __shfl_sync(0xffffffffu, inc, 31);
+  }
+  cand = smp_block_int<true>(cand, sh);
+  last = smp_block_int<false>(last, sh);
+  if (tid == 0) tokens[blockIdx.x] = cand < n ? cand : (last >= 0 ? last : 0);
+}
+
+// Host side: argument checks happen in the extern "C" wrappers.
+cudaError_t launch_sample(float* logits, long long ld, int rows, int n, float temperature, long long top_k,
+                          float top_p, const float* u, int32_t* tokens, cudaStream_t st) {
+  SampleArgs a{};
+  a.greedy = temperature == 0.0f;
+  a.inv_t = a.greedy ? 1.0f : 1.0f / temperature;
+  a.top_k = (top_k > 0 && top_k < n) ? (int)top_k : 0;
+  a.top_p = top_p;
+  a.use_p = top_p > 0.0f && top_p < 1.0f;
+  for (int r = 0; r < rows; ++r) a.u[r] = u ? u[r] : 0.f;
+  const bool vec = n % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
+  if (vec) sample_kernel<4><<<rows, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+  else sample_kernel<1><<<rows, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+  return cudaGetLastError();
+}
+
+}  // namespace vtb
+
+using namespace vtb;
+
+static int check_sampler(const VtbCudaSamplerConfig* cfg, const float* u, int64_t rows, int64_t n) {
+  if (!cfg) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null sampler config");
+  if (!(cfg->temperature >= 0.0f) || !(cfg->top_p >= 0.0f))  // rejects NaN too
+    return set_err(VTB_CUDA_ERR_INVALID_ARG, "temperature and top_p must be >= 0");
+  if (rows < 1 || rows > SMP_MAX_ROWS) return set_err(VTB_CUDA_ERR_INVALID_ARG, "rows must be in [1, 256]");
+  if (n < 1 || n > (1 << 24)) return set_err(VTB_CUDA_ERR_INVALID_ARG, "n must be in [1, 2^24]");
+  if (cfg->temperature != 0.0f && !u) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null uniform draws");
+  return VTB_CUDA_OK;
+}
+
+extern "C" {
+
+int vtb_cuda_sample(float* logits, int64_t rows, int64_t n, int64_t ld, const VtbCudaSamplerConfig* cfg,
+                    const float* u, int32_t* tokens, void* stream) {
+  cudaGetLastError();
+  int rc = check_sampler(cfg, u, rows, n);
+  if (rc) return rc;
+  if (!logits || !tokens) return set_err(VTB_CUDA_ERR_INVALID_ARG, "null logits or tokens");
+  if (ld < n) return set_err(VTB_CUDA_ERR_INVALID_ARG, "row stride ld is below n");
+  return cuda_status(launch_sample(logits, ld, (int)rows, (int)n, cfg->temperature, (long long)cfg->top_k,
+                                   cfg->top_p, u, tokens, (cudaStream_t)stream));
+}
+
+int vtb_cuda_state_sample(VtbCudaState* s, int32_t rows, const VtbCudaSamplerConfig* cfg, const float* u,
+                          int32_t* tokens) {
+  cudaGetLastError();
+  if (!s || !tokens) return merr(VTB_CUDA_ERR_INVALID_ARG, "null argument");
+  const int64_t V = s->m->c.vocab_size;
+  int rc = check_sampler(cfg, u, rows, V);
+  if (rc) return rc;
+  if (rows > s->max_rows) return merr(VTB_CUDA_ERR_INVALID_ARG, "rows exceed the state's logits rows");
+  cudaSetDevice(s->m->device);
+  // s->amax / s->hamax are the argmax buffers (max_rows int32, device and pinned host).
+  cudaError_t e = launch_sample(s->logits, V, rows, (int)V, cfg->temperature, (long long)cfg->top_k, cfg->top_p,
+                                u, s->amax, s->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(s->hamax, s->amax, (size_t)rows * 4, cudaMemcpyDeviceToHost, s->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
+  if (e != cudaSuccess) return mcuda(e);
+  memcpy(tokens, s->hamax, (size_t)rows * 4);
+  return VTB_CUDA_OK;
+}
+
+}  // extern "C"

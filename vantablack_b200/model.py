@@ -367,6 +367,17 @@ class CudaState:
                                              _ptr(am)), "vtb_cuda_prefill")
         return lg, int(am[0])
 
+    def sample(self, temperature: float, top_k: int = 0, top_p: float = 0.0, u=None, rows: int | None = None):
+        """Sample the state's current logits on the device (vtb_cuda_state_sample):
+        one token per row, one uniform draw per row; only the tokens are read back."""
+        rows = self.n_seqs if rows is None else rows
+        cfg = _lib.SamplerConfig(float(temperature), int(top_k), float(top_p), 0)
+        ua = None if u is None else np.ascontiguousarray(np.atleast_1d(u), np.float32)
+        out = np.empty(rows, np.int32)
+        _lib.check(self.lib.vtb_cuda_state_sample(self.h, rows, C.byref(cfg), None if ua is None else _ptr(ua),
+                                                  _ptr(out)), "vtb_cuda_state_sample")
+        return out
+
     def generate_greedy(self, prompt, n_gen: int, use_prefill: bool = True):
         """Prompt then greedy decode of one sequence (n_seqs == 1)."""
         assert self.n_seqs == 1

@@ -6,6 +6,8 @@ tensors are flat ``torch.uint8`` CUDA tensors of packed GGUF blocks.
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
 from . import _lib
@@ -53,6 +55,27 @@ def embed(quant: int, table: torch.Tensor, ids: torch.Tensor, dim: int) -> torch
     _lib.check(lib.vtb_cuda_embed(quant, table.data_ptr(), ids.data_ptr(), out.data_ptr(), dim, ids.numel(),
                                   _stream()), "vtb_cuda_embed")
     return out
+
+
+def sample(logits: torch.Tensor, temperature: float, top_k: int = 0, top_p: float = 0.0, u=None) -> torch.Tensor:
+    """Sampler.sample (sampler.zig:44-104) per row of f32 logits [rows, n] on the
+    device, with one caller-supplied uniform draw per row; logits are rewritten
+    in place.  Returns int32 tokens [rows] on the device."""
+    import numpy as np
+    _dev(logits, "logits")
+    if logits.dtype != torch.float32:
+        raise ValueError("logits must be f32")
+    lg = logits if logits.dim() == 2 else logits.view(1, -1)
+    rows, n = lg.shape
+    cfg = _lib.SamplerConfig(float(temperature), int(top_k), float(top_p), 0)
+    ua = None if u is None else np.ascontiguousarray(np.atleast_1d(u), np.float32)
+    if ua is not None and ua.size != rows:
+        raise ValueError("one draw per row")
+    tok = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    _lib.check(lib.vtb_cuda_sample(lg.data_ptr(), rows, n, n, C.byref(cfg),
+                                   None if ua is None else ua.ctypes.data, tok.data_ptr(), _stream()),
+               "vtb_cuda_sample")
+    return tok
 
 
 def quantize_q8_0(x: torch.Tensor):
