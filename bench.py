@@ -775,6 +775,31 @@ def run_profile_case(case: str) -> None:
         st.prefill(np.arange(3, 131))
         for i in range(5):
             st.step([5 + i], want_logits=False)
+    elif case == "mlx":  # MLX 4-bit GEMV at 14336 x 4096 (G 64, bf16), 8 weight copies > L2, in a CUDA graph
+        m, k, g = 14336, 4096, 64
+        copies = []
+        for _ in range(8):
+            w, sc, bi = S.mlx_tensor(rng, m, k, 4, g, True)
+            copies.append(tuple(torch.from_numpy(a).cuda() for a in (w, sc, bi)))
+        x = torch.from_numpy(S.activations(rng, k)).cuda()
+        nbytes = sum(t.numel() for t in copies[0])
+        for c in copies:
+            ops.gemv_mlx(*c, x, m, k, 4, g, True)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for c in copies:
+                ops.gemv_mlx(*c, x, m, k, 4, g, True)
+        for _ in range(3):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000 / 80
+        print(f"MLX-Q4 GEMV {m}x{k}: {us:.2f} us per launch, {nbytes / us / 1e3:.0f} GB/s ({nbytes} bytes)")
     elif case == "sampler":  # device sampler: 20 launches per (vocabulary, rows, config), D2H beside it
         for rows, n in ((1, 32000), (1, 128256), (32, 128256)):
             lg = torch.randn(rows, n, device="cuda") * 3
@@ -806,7 +831,7 @@ def run_profile_case(case: str) -> None:
 
 
 PROFILE_CASES = ["gemv", "gemv_chain", "gemv_q6k", "gemv_q8", "gemm", "gemm_precise", "gemm_b32", "gemm_b32_q4k", "decode", "decode8b",
-                 "decode8b_b32", "sampler"]
+                 "decode8b_b32", "sampler", "mlx"]
 
 
 def main():

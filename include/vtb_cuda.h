@@ -318,6 +318,25 @@ int vtb_cuda_step(VtbCudaState *s, const int32_t *tokens, float *logits, int32_t
 int vtb_cuda_prefill(VtbCudaState *s, int32_t seq, const int32_t *tokens, int32_t n, float *logits,
                      int32_t *argmax);
 
+/* ---- MLX affine quantization (src/kernels/mlx.zig) ----
+ * w: [m][k / (32 / bits)] little-endian u32 words, 32 / bits values per word,
+ * low bits first; scales, biases: [m][k / group_size] f16 (scale_is_bf16 = 0)
+ * or bf16; weight = q * scale + bias.  bits in {2, 3, 4, 5, 6, 8}; group_size
+ * divides k and is a multiple of 32 / bits.  w, scales and biases may sit at
+ * any byte offset (safetensors shards); x must be 16-byte aligned.
+ * vtb_cuda_gemv_mlx: y[m] = W . x (matmul, mlx.zig:213-235, fp32 accumulation). */
+int vtb_cuda_gemv_mlx(const void *w, const void *scales, const void *biases, const float *x, float *y, int64_t m,
+                      int64_t k, int bits, int group_size, int scale_is_bf16, void *stream);
+/* out[rows][k] = dequantized rows, bit-exact with dequantRowDispatch (mlx.zig:261-279). */
+int vtb_cuda_dequant_mlx(const void *w, const void *scales, const void *biases, float *out, int64_t rows, int64_t k,
+                         int bits, int group_size, int scale_is_bf16, void *stream);
+/* Bridge one-shot, same arguments as vtb_metal_matmul_mlx_q4 (src/metal/bridge.h:217-229):
+ * weight, scales, biases and acts each as buffer + byte offset. */
+int vtb_cuda_matmul_mlx_q4(struct VtbCudaCtx *ctx, struct VtbCudaBuf *out_buf, struct VtbCudaBuf *weight_buf,
+                           size_t weight_offset, struct VtbCudaBuf *scales_buf, size_t scales_offset,
+                           struct VtbCudaBuf *biases_buf, size_t biases_offset, struct VtbCudaBuf *acts_buf,
+                           size_t acts_offset, size_t m, size_t k, uint32_t group_size, uint32_t scale_dtype_is_bf16);
+
 /* ---- token sampling on the device (Sampler.sample, src/runtime/sampler.zig:44-104) ----
  * Same fields, meaning and layout as the reference's VtbSamplerConfig
  * (include/vantablack.h:46-51).  temperature 0 = greedy argmax; top_k 0 =

@@ -66,6 +66,8 @@ def _load():
         "vtbo_geglu": (None, [_f32p, _f32p, _sz]),
         "vtbo_add_into": (None, [_f32p, _f32p, _sz]),
         "vtbo_argmax": (_sz, [_f32p, _sz]),
+        "vtbo_mlx_dequant": (C.c_int, [_f32p, _u8p, _u8p, _u8p, _sz, _sz, C.c_uint, _sz, C.c_int]),
+        "vtbo_mlx_matmul": (C.c_int, [_f32p, _u8p, _u8p, _u8p, _f32p, _sz, _sz, C.c_uint, _sz, C.c_int]),
         "vtbo_sample": (C.c_uint32, [_f32p, _sz, C.c_float, _sz, C.c_float, C.c_float]),
         "vtbo_model_create": (C.c_void_p, [C.c_void_p, C.c_void_p, _u8p, C.c_int, _f32p, _u8p, C.c_int]),
         "vtbo_model_destroy": (None, [C.c_void_p]),
@@ -230,6 +232,30 @@ def add_into(a, b):
 def argmax(x) -> int:
     x = np.ascontiguousarray(x, np.float32)
     return lib.vtbo_argmax(_p(x, _f32p), x.size)
+
+
+def mlx_dequant(w, scales, biases, rows: int, k: int, bits: int, group: int, bf16: bool) -> np.ndarray:
+    """dequantRow (mlx.zig:62-135) over `rows` rows -> f32 [rows, k]."""
+    out = np.empty((rows, k), np.float32)
+    rc = lib.vtbo_mlx_dequant(_p(out, _f32p), _p(np.ascontiguousarray(w, np.uint8), _u8p),
+                              _p(np.ascontiguousarray(scales, np.uint8), _u8p),
+                              _p(np.ascontiguousarray(biases, np.uint8), _u8p), rows, k, bits, group, int(bf16))
+    if rc:
+        raise ValueError("unsupported MLX arguments")
+    return out
+
+
+def mlx_matmul(w, scales, biases, x, m: int, k: int, bits: int, group: int, bf16: bool) -> np.ndarray:
+    """matmul (mlx.zig:213-235): y[m] = W . x."""
+    out = np.empty(m, np.float32)
+    xa = np.ascontiguousarray(x, np.float32)
+    rc = lib.vtbo_mlx_matmul(_p(out, _f32p), _p(np.ascontiguousarray(w, np.uint8), _u8p),
+                             _p(np.ascontiguousarray(scales, np.uint8), _u8p),
+                             _p(np.ascontiguousarray(biases, np.uint8), _u8p), _p(xa, _f32p), m, k, bits, group,
+                             int(bf16))
+    if rc:
+        raise ValueError("unsupported MLX arguments")
+    return out
 
 
 def sample(logits, temperature: float, top_k: int, top_p: float, u: float):

@@ -597,6 +597,89 @@ size_t vtbo_argmax(const float *x, size_t n) {
     return bi;
 }
 
+/* ---------------- MLX affine quantization (src/kernels/mlx.zig) ---------------- */
+/*
+ * Layout (mlx.zig:3-23): per row, k*bits/32 little-endian u32 words, each
+ * holding 32/bits values low bits first (the top 32 % bits bits unused);
+ * per group of G columns one scale and one bias, f16 or bf16 (mlx.zig:30-52);
+ * w = q * scale + bias.
+ */
+static uint16_t mlx_ld16(const uint8_t *p, size_t idx) { return (uint16_t)(p[2 * idx] | (p[2 * idx + 1] << 8)); }
+static float mlx_scale(const uint8_t *p, size_t idx, int bf16) { /* loadScale, mlx.zig:43-50 */
+    uint16_t b = mlx_ld16(p, idx);
+    if (bf16) {
+        uint32_t w = (uint32_t)b << 16;
+        float f;
+        memcpy(&f, &w, 4);
+        return f;
+    }
+    return vtbo_f16_to_f32(b);
+}
+static uint32_t mlx_ld32(const uint8_t *p, size_t idx) {
+    const uint8_t *q = p + 4 * idx;
+    return (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16) | ((uint32_t)q[3] << 24);
+}
+static int mlx_bits_ok(unsigned bits) { return bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8; }
+
+/* dequantRow / dequantRowQ4 (mlx.zig:62-135) for `rows` consecutive rows. */
+int vtbo_mlx_dequant(float *out, const uint8_t *w, const uint8_t *scales, const uint8_t *biases, size_t rows,
+                     size_t k, unsigned bits, size_t group, int bf16) {
+    if (!mlx_bits_ok(bits)) return -1;
+    const size_t el = 32 / bits, ng = k / group;
+    const uint32_t mask = (1u << bits) - 1u;
+    if (group == 0 || k % group || group % el) return -1;
+    for (size_t r = 0; r < rows; r++) {
+        const uint8_t *wr = w + r * (k / el) * 4, *sr = scales + r * ng * 2, *br = biases + r * ng * 2;
+        float *o = out + r * k;
+        size_t col = 0;
+        for (size_t g = 0; g < ng; g++) {
+            const float scale = mlx_scale(sr, g, bf16), bias = mlx_scale(br, g, bf16);
+            for (size_t c = 0; c < group; c += el) {
+                const uint32_t word = mlx_ld32(wr, (col + c) / el);
+                for (size_t i = 0; i < el; i++) {
+                    const uint32_t q = (word >> (i * bits)) & mask;
+                    float v = (float)q * scale;
+                    o[col + c + i] = v + bias;
+                }
+            }
+            col += group;
+        }
+    }
+    return 0;
+}
+
+/* matmul -> matmulGeneric / matmulQ4 (mlx.zig:139-330): per group
+ * total += scale * sum(q * x) + bias * sum(x), sequential f32. */
+int vtbo_mlx_matmul(float *out, const uint8_t *w, const uint8_t *scales, const uint8_t *biases, const float *x,
+                    size_t m, size_t k, unsigned bits, size_t group, int bf16) {
+    if (!mlx_bits_ok(bits)) return -1;
+    const size_t el = 32 / bits, ng = k / group;
+    const uint32_t mask = (1u << bits) - 1u;
+    if (group == 0 || k % group || group % el) return -1;
+    for (size_t r = 0; r < m; r++) {
+        const uint8_t *wr = w + r * (k / el) * 4, *sr = scales + r * ng * 2, *br = biases + r * ng * 2;
+        float total = 0.0f;
+        size_t col = 0;
+        for (size_t g = 0; g < ng; g++) {
+            const float scale = mlx_scale(sr, g, bf16), bias = mlx_scale(br, g, bf16);
+            float q_dot = 0.0f, x_sum = 0.0f;
+            for (size_t c = col; c < col + group; c += el) {
+                const uint32_t word = mlx_ld32(wr, c / el);
+                for (size_t i = 0; i < el; i++) {
+                    const uint32_t q = (word >> (i * bits)) & mask;
+                    const float xv = x[c + i];
+                    q_dot += (float)q * xv;
+                    x_sum += xv;
+                }
+            }
+            total += scale * q_dot + bias * x_sum;
+            col += group;
+        }
+        out[r] = total;
+    }
+    return 0;
+}
+
 /* ---------------- token sampler ---------------- */
 /*
  * Sampler.sample, src/runtime/sampler.zig:44-104, with the PRNG draw taken

@@ -87,6 +87,12 @@ void vtbo_add_into(float *a, const float *b, size_t n);
 size_t vtbo_argmax(const float *x, size_t n);
 /* Sampler.sample (sampler.zig:44-104) with the uniform draw u in [0, 1) supplied. */
 uint32_t vtbo_sample(float *logits, size_t n, float temperature, size_t top_k, float top_p, float u);
+/* MLX affine quantization (mlx.zig): dequantRow for `rows` rows, and matmul. bits in {2,3,4,5,6,8};
+ * bf16 != 0: scales/biases are bf16, else f16.  Return -1 on unsupported arguments. */
+int vtbo_mlx_dequant(float *out, const uint8_t *w, const uint8_t *scales, const uint8_t *biases, size_t rows,
+                     size_t k, unsigned bits, size_t group, int bf16);
+int vtbo_mlx_matmul(float *out, const uint8_t *w, const uint8_t *scales, const uint8_t *biases, const float *x,
+                    size_t m, size_t k, unsigned bits, size_t group, int bf16);
 
 /* Llama forward (forward.zig / prefill.zig / kv_cache.zig). */
 typedef struct {

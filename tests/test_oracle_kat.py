@@ -211,3 +211,56 @@ def test_sampler_pipeline_by_hand():
     q /= q.sum()
     assert np.allclose(p, q, atol=1e-6)
     assert tok == int(np.argmax(np.cumsum(q) >= 0.7))
+
+
+def _mlx_q4_nibbles_0_15():
+    w0 = sum(i << (4 * i) for i in range(8))
+    w1 = sum((i + 8) << (4 * i) for i in range(8))
+    return np.frombuffer(np.array([w0, w1], "<u4").tobytes(), np.uint8)
+
+
+def test_mlx_dequant_q4_kat():  # mlx.zig:339-367: scale 1, bias 0 recovers the nibbles
+    w = _mlx_q4_nibbles_0_15()
+    one, zero = np.array([0x00, 0x3C], np.uint8), np.array([0, 0], np.uint8)
+    assert np.array_equal(O.mlx_dequant(w, one, zero, 1, 16, 4, 16, False)[0], np.arange(16, dtype=np.float32))
+
+
+def test_mlx_matmul_q4_kat():  # mlx.zig:369-405
+    w = _mlx_q4_nibbles_0_15()
+    s, b = np.array([0x00, 0x38], np.uint8), np.array([0x00, 0x34], np.uint8)  # f16 0.5, 0.25
+    assert abs(O.mlx_matmul(w, s, b, np.ones(16, np.float32), 1, 16, 4, 16, False)[0] - 64.0) <= 1e-4
+    alt = np.where(np.arange(16) % 2 == 0, 1.0, -1.0).astype(np.float32)
+    assert abs(O.mlx_matmul(w, s, b, alt, 1, 16, 4, 16, False)[0] + 4.0) <= 1e-4
+
+
+def test_mlx_matmul_q8_kat():  # mlx.zig:407-434
+    w = np.frombuffer(np.array([0x03020100, 0x07060504], "<u4").tobytes(), np.uint8)
+    one, zero = np.array([0x00, 0x3C], np.uint8), np.array([0, 0], np.uint8)
+    assert abs(O.mlx_matmul(w, one, zero, np.ones(8, np.float32), 1, 8, 8, 8, False)[0] - 28.0) <= 1e-4
+
+
+def test_mlx_dispatch_q4_q8_agree_kat():  # mlx.zig:436-459
+    one, zero = np.array([0x00, 0x3C], np.uint8), np.array([0, 0], np.uint8)
+    w4 = np.frombuffer(np.array([sum(i << (4 * i) for i in range(8))], "<u4").tobytes(), np.uint8)
+    w8 = np.arange(8, dtype=np.uint8)
+    x = np.ones(8, np.float32)
+    assert O.mlx_matmul(w4, one, zero, x, 1, 8, 4, 8, False)[0] == O.mlx_matmul(w8, one, zero, x, 1, 8, 8, 8, False)[0] == 28.0
+
+
+def test_mlx_matmul_runtime_fixture():  # forward.zig:853-960: every nibble 3, f16 scale 0.5, bias 0.25, x = e0
+    m, k = 4, 64
+    w = np.full(m * k // 2, 0x33, np.uint8)
+    s = np.tile(np.array([0x00, 0x38], np.uint8), m)
+    b = np.tile(np.array([0x00, 0x34], np.uint8), m)
+    x = np.zeros(k, np.float32); x[0] = 1.0
+    assert np.array_equal(O.mlx_matmul(w, s, b, x, m, k, 4, 64, False), np.full(m, 1.75, np.float32))
+    # bf16 variant (forward.zig:968-1040): scale bf16 0.5 = 0x3F00, bias bf16 -1.0 = 0xBF80 -> 3 * 0.5 - 1
+    s16 = np.tile(np.array([0x00, 0x3F], np.uint8), m)
+    b16 = np.tile(np.array([0x80, 0xBF], np.uint8), m)
+    assert np.array_equal(O.mlx_matmul(w, s16, b16, x, m, k, 4, 64, True), np.full(m, 0.5, np.float32))
+
+
+def test_mlx_unsupported_bits():
+    with pytest.raises(ValueError):
+        O.mlx_matmul(np.zeros(16, np.uint8), np.zeros(2, np.uint8), np.zeros(2, np.uint8), np.zeros(8, np.float32),
+                     1, 8, 7, 8, False)

@@ -80,6 +80,10 @@ SIGNATURES = {
     "vtb_cuda_finalize_token": (_int, [_vp, _vp, _vp]),
     "vtb_cuda_step": (_int, [_vp, _vp, _vp, _vp]),
     "vtb_cuda_prefill": (_int, [_vp, _i32, _vp, _i32, _vp, _vp]),
+    "vtb_cuda_gemv_mlx": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _int, _vp]),
+    "vtb_cuda_dequant_mlx": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _int, _vp]),
+    "vtb_cuda_matmul_mlx_q4": (_int, [_vp, _vp, _vp, _sz, _vp, _sz, _vp, _sz, _vp, _sz, _sz, _sz, C.c_uint32,
+                                      C.c_uint32]),
     "vtb_cuda_sample": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
     "vtb_cuda_state_sample": (_int, [_vp, _i32, _vp, _vp, _vp]),
     "vtb_cuda_tp_unique_id": (_int, [_vp]),

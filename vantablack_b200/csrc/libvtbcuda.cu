@@ -14,3 +14,4 @@
 #include "gguf.cu"
 #include "noalloc.cu"
 #include "sampler.cu"
+#include "mlx.cu"

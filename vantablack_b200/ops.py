@@ -57,6 +57,28 @@ def embed(quant: int, table: torch.Tensor, ids: torch.Tensor, dim: int) -> torch
     return out
 
 
+def gemv_mlx(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, x: torch.Tensor, m: int, k: int,
+             bits: int, group: int, bf16: bool, w_off: int = 0) -> torch.Tensor:
+    """MLX affine GEMV (mlx.zig matmul): y[m] = W . x.  w, scales, biases are
+    flat uint8 CUDA tensors; w_off shifts the weight pointer by bytes."""
+    for t, nm in ((w, "w"), (scales, "scales"), (biases, "biases"), (x, "x")):
+        _dev(t, nm)
+    y = torch.empty(m, dtype=torch.float32, device=x.device)
+    _lib.check(lib.vtb_cuda_gemv_mlx(w.data_ptr() + w_off, scales.data_ptr(), biases.data_ptr(), x.data_ptr(),
+                                     y.data_ptr(), m, k, bits, group, int(bf16), _stream()), "vtb_cuda_gemv_mlx")
+    return y
+
+
+def dequant_mlx(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, rows: int, k: int, bits: int,
+                group: int, bf16: bool, w_off: int = 0) -> torch.Tensor:
+    for t, nm in ((w, "w"), (scales, "scales"), (biases, "biases")):
+        _dev(t, nm)
+    out = torch.empty(rows, k, dtype=torch.float32, device=w.device)
+    _lib.check(lib.vtb_cuda_dequant_mlx(w.data_ptr() + w_off, scales.data_ptr(), biases.data_ptr(), out.data_ptr(),
+                                        rows, k, bits, group, int(bf16), _stream()), "vtb_cuda_dequant_mlx")
+    return out
+
+
 def sample(logits: torch.Tensor, temperature: float, top_k: int = 0, top_p: float = 0.0, u=None) -> torch.Tensor:
     """Sampler.sample (sampler.zig:44-104) per row of f32 logits [rows, n] on the
     device, with one caller-supplied uniform draw per row; logits are rewritten

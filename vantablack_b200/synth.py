@@ -74,3 +74,20 @@ def activations(rng: np.random.Generator, *shape: int) -> np.ndarray:
 
 def norm_weight(rng: np.random.Generator, n: int) -> np.ndarray:
     return (1.0 + 0.02 * rng.standard_normal(n)).astype(np.float32)
+
+
+def mlx_tensor(rng, m: int, k: int, bits: int, group: int, bf16: bool):
+    """Seeded MLX affine tensor (mlx.zig layout): uniform random u32 words
+    (k / (32 / bits) per row), scales |N(0,1)| * 2^-6 and biases N(0,1) * 2^-4,
+    stored as f16 or as bf16 (the top half of the f32).  Returns
+    (weight bytes, scale bytes, bias bytes)."""
+    words = rng.integers(0, 2**32, size=m * (k // (32 // bits)), dtype=np.uint64).astype("<u4")
+    ng = m * (k // group)
+    sc = np.abs(rng.standard_normal(ng)) * 2.0**-6
+    bi = rng.standard_normal(ng) * 2.0**-4
+    def enc(v):
+        if bf16:
+            return (v.astype(np.float32).view(np.uint32) >> 16).astype("<u2")
+        return v.astype(np.float16).view("<u2")
+    return (np.frombuffer(words.tobytes(), np.uint8).copy(), np.frombuffer(enc(sc).tobytes(), np.uint8).copy(),
+            np.frombuffer(enc(bi).tobytes(), np.uint8).copy())
