@@ -98,49 +98,60 @@ gemv_mlx_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ sc, c
 }
 
 // 4-bit rows on 16-byte boundaries with group % 32 == 0: a lane takes 32
-// consecutive weights of a row (one 16-byte load, inside one group) for each
-// of the warp's rows, so a group's scale and bias are read once per 32 weights
-// and the 32 activations once per 4 rows.  The next chunk's weights, scales
-// and biases are loaded before the current chunk is multiplied (two chunks of
-// loads in flight per lane), and the products run as packed f32x2 FMAs.
+// consecutive weights of a row (16 bytes, inside one group) for each of the
+// warp's 4 rows, so a group's scale and bias are read once per 32 weights and
+// the 32 activations once per 4 rows.  Weights stream through a per-warp
+// MLX_STAGES-deep ring of cp.async copies (each lane copies and later reads
+// only its own 16-byte slots, so the per-thread async-copy groups order
+// everything).  Nibbles become floats with one byte-permute each (low and
+// high nibble planes masked once per word, byte p placed under 0x4B000000),
+// and the products run as packed f32x2 FMAs.
+//
+// x is staged once per CTA in shared memory, float4 slot i of 32-column chunk
+// c stored at c*8 + (i ^ (c & 7)): a warp reading eight float4 of 32 different
+// chunks then needs 4 wavefronts per load (the minimum for 512 bytes) instead
+// of one per lane, which is what direct global loads of 128 contiguous bytes
+// per lane cost.  The chunk sums of x are computed once there as well.
+constexpr int MLX_STAGES = 3;
+constexpr int MLX_RING = MLX_WARPS * MLX_STAGES * MLX_ROWS * 32 * 16;  // bytes per CTA
+
+__device__ __forceinline__ size_t mlx_q4_smem(int k) { return ((size_t)k + k / 32 + 3) / 4 * 16 + MLX_RING; }
+static size_t mlx_q4_smem_host(int k) { return ((size_t)k + k / 32 + 3) / 4 * 16 + MLX_RING; }
+
+__device__ __forceinline__ void mlx_cp16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void mlx_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void mlx_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 template <bool H2>
-__device__ __forceinline__ void mlx_q4_fetch(const uint8_t* __restrict__ w, const uint8_t* __restrict__ sc,
-                                             const uint8_t* __restrict__ bi, int r0, int nr, long long row_bytes,
-                                             int ng, int ch, int g, int bf16, uint4 (&wv)[MLX_ROWS],
-                                             float (&s)[MLX_ROWS], float (&b)[MLX_ROWS]) {
-#pragma unroll
-  for (int r = 0; r < MLX_ROWS; ++r) {
-    if (r < nr) {
-      wv[r] = __ldg(reinterpret_cast<const uint4*>(w + (long long)(r0 + r) * row_bytes) + ch);
-      const long long gi = (long long)(r0 + r) * ng + g;
-      if constexpr (H2) {
-        const uint32_t sb = __ldg(reinterpret_cast<const unsigned short*>(sc) + gi);
-        const uint32_t bb = __ldg(reinterpret_cast<const unsigned short*>(bi) + gi);
-        s[r] = bf16 ? __uint_as_float(sb << 16) : __half2float(__ushort_as_half((unsigned short)sb));
-        b[r] = bf16 ? __uint_as_float(bb << 16) : __half2float(__ushort_as_half((unsigned short)bb));
-      } else {
-        s[r] = mlx_half(sc, gi, bf16);
-        b[r] = mlx_half(bi, gi, bf16);
-      }
-    }
+__device__ __forceinline__ void mlx_sb(const uint8_t* __restrict__ sc, const uint8_t* __restrict__ bi, long long gi,
+                                       int bf16, float& s, float& b) {
+  if constexpr (H2) {
+    const uint32_t sb = __ldg(reinterpret_cast<const unsigned short*>(sc) + gi);
+    const uint32_t bb = __ldg(reinterpret_cast<const unsigned short*>(bi) + gi);
+    s = bf16 ? __uint_as_float(sb << 16) : __half2float(__ushort_as_half((unsigned short)sb));
+    b = bf16 ? __uint_as_float(bb << 16) : __half2float(__ushort_as_half((unsigned short)bb));
+  } else {
+    s = mlx_half(sc, gi, bf16);
+    b = mlx_half(bi, gi, bf16);
   }
 }
 
-// x is staged once per CTA in shared memory, float4 slot i of 32-column chunk
-// c stored at c*8 + (i ^ (c & 7)): a warp reading eight float4 of 32 different
-// chunks then needs 4 wavefronts per load (the minimum for 512 bytes) instead of
-// one per lane, which is what direct global loads of 128 contiguous bytes per
-// lane cost.  The chunk sums of x are computed once there as well.
 template <bool H2>
-__global__ void __launch_bounds__(MLX_WARPS * 32, 2)
+__global__ void __launch_bounds__(MLX_WARPS * 32)
 gemv_mlx_q4_vec_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ sc,
                        const uint8_t* __restrict__ bi, const float* __restrict__ x, float* __restrict__ y, int m,
                        int k, int group, int gshift, int bf16) {
-  extern __shared__ __align__(16) float xsm[];  // [k] swizzled, then [k / 32] chunk sums
-  const int lane = threadIdx.x & 31;
+  extern __shared__ __align__(16) float xsm[];  // [k] swizzled x, [k / 32] chunk sums, then the weight rings
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nch = k / 32, ng = k / group;
   float4* x4 = reinterpret_cast<float4*>(xsm);
   float* csum = xsm + k;
+  uint8_t* ring = reinterpret_cast<uint8_t*>(xsm) + (mlx_q4_smem(k) - MLX_RING) +
+                  warp * (MLX_STAGES * MLX_ROWS * 32 * 16);
+  const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring) + lane * 16;
   for (int q = threadIdx.x; q < k / 4; q += blockDim.x) {
     const int c = q >> 3, i = q & 7;
     x4[c * 8 + (i ^ (c & 7))] = __ldg(reinterpret_cast<const float4*>(x) + q);
@@ -158,49 +169,65 @@ gemv_mlx_q4_vec_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict_
   __syncthreads();
   const long long row_bytes = (long long)k / 2;
   const f2 magic = pk(8388608.0f, 8388608.0f);
-  for (int r0 = (blockIdx.x * MLX_WARPS + (threadIdx.x >> 5)) * MLX_ROWS; r0 < m;
-       r0 += gridDim.x * MLX_WARPS * MLX_ROWS) {
-    const int nr = min(MLX_ROWS, m - r0);
+  const int T = lane < nch ? (nch - lane + 31) / 32 : 0;  // this lane's chunks per row
+  // This warp's rows: an even share of m over all the grid's warps (the grid is
+  // one wave), walked MLX_ROWS at a time.
+  const long long nw = (long long)gridDim.x * MLX_WARPS, gw = (long long)blockIdx.x * MLX_WARPS + warp;
+  const int row_end = (int)((gw + 1) * m / nw);
+  for (int r0 = (int)(gw * m / nw); r0 < row_end; r0 += MLX_ROWS) {
+    const int nr = min(MLX_ROWS, row_end - r0);
+    auto issue = [&](int t) {
+      const int ch = lane + 32 * t, st = t % MLX_STAGES;
+#pragma unroll
+      for (int r = 0; r < MLX_ROWS; ++r)
+        if (r < nr)
+          mlx_cp16(ring_s + (uint32_t)((st * MLX_ROWS + r) * 32 * 16),
+                   w + (long long)(r0 + r) * row_bytes + (long long)ch * 16);
+    };
+#pragma unroll
+    for (int t = 0; t < MLX_STAGES - 1; ++t) {
+      if (t < T) issue(t);
+      mlx_cp_commit();
+    }
     float acc[MLX_ROWS] = {0.f, 0.f, 0.f, 0.f};
-    uint4 wv[MLX_ROWS];
-    float s[MLX_ROWS], b[MLX_ROWS];
-    auto grp = [&](int c) { return gshift >= 0 ? ((c * 32) >> gshift) : (c * 32) / group; };
-    if (lane < nch) mlx_q4_fetch<H2>(w, sc, bi, r0, nr, row_bytes, ng, lane, grp(lane), bf16, wv, s, b);
-    for (int ch = lane; ch < nch; ch += 32) {
-      uint4 wn[MLX_ROWS];
-      float sn[MLX_ROWS], bn[MLX_ROWS];
-      const int cn = ch + 32;
-      if (cn < nch) mlx_q4_fetch<H2>(w, sc, bi, r0, nr, row_bytes, ng, cn, grp(cn), bf16, wn, sn, bn);
+    for (int t = 0; t < T; ++t) {
+      if (t + MLX_STAGES - 1 < T) issue(t + MLX_STAGES - 1);
+      mlx_cp_commit();
+      const int ch = lane + 32 * t, st = t % MLX_STAGES;
+      const int g = gshift >= 0 ? ((ch * 32) >> gshift) : (ch * 32) / group;
+      float s[MLX_ROWS], b[MLX_ROWS];
+#pragma unroll
+      for (int r = 0; r < MLX_ROWS; ++r)
+        if (r < nr) mlx_sb<H2>(sc, bi, (long long)(r0 + r) * ng + g, bf16, s[r], b[r]);
       f2 xv[16];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float4 t = x4[ch * 8 + (i ^ (ch & 7))];
-        xv[2 * i] = pk(t.x, t.y);
-        xv[2 * i + 1] = pk(t.z, t.w);
+        const float4 v = x4[ch * 8 + (i ^ (ch & 7))];
+        xv[2 * i] = pk(v.x, v.y);
+        xv[2 * i + 1] = pk(v.z, v.w);
       }
       const float xs = csum[ch];
+      mlx_cp_wait<MLX_STAGES - 1>();  // this lane's copies of chunk t have landed
 #pragma unroll
       for (int r = 0; r < MLX_ROWS; ++r) {
         if (r < nr) {
-          const uint32_t wd[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
+          const uint4 wv = *reinterpret_cast<const uint4*>(ring + ((st * MLX_ROWS + r) * 32 + lane) * 16);
+          const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
           f2 qd = pk(0.f, 0.f);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-              const f2 q = sub2(pk(__uint_as_float(0x4B000000u | ((wd[j] >> (4 * i)) & 15u)),
-                                   __uint_as_float(0x4B000000u | ((wd[j] >> (4 * i + 4)) & 15u))),
-                                magic);
-              qd = fma2(q, xv[4 * j + i / 2], qd);
-            }
+          for (int j = 0; j < 4; ++j) {
+            // byte p of lo / hi = the nibble of column 2p / 2p + 1 of this word
+            const uint32_t lo = wd[j] & 0x0F0F0F0Fu, hi = (wd[j] >> 4) & 0x0F0F0F0Fu;
+            qd = fma2(sub2(pk(byte_magic<0>(lo), byte_magic<0>(hi)), magic), xv[4 * j + 0], qd);
+            qd = fma2(sub2(pk(byte_magic<1>(lo), byte_magic<1>(hi)), magic), xv[4 * j + 1], qd);
+            qd = fma2(sub2(pk(byte_magic<2>(lo), byte_magic<2>(hi)), magic), xv[4 * j + 2], qd);
+            qd = fma2(sub2(pk(byte_magic<3>(lo), byte_magic<3>(hi)), magic), xv[4 * j + 3], qd);
+          }
           acc[r] = fmaf(s[r], hsum(qd), fmaf(b[r], xs, acc[r]));
         }
       }
-      if (cn < nch) {
-#pragma unroll
-        for (int r = 0; r < MLX_ROWS; ++r) { wv[r] = wn[r]; s[r] = sn[r]; b[r] = bn[r]; }
-      }
     }
+    mlx_cp_wait<0>();  // nothing of this row group may still be in flight when the ring is reused
 #pragma unroll
     for (int r = 0; r < MLX_ROWS; ++r) {
       float v = acc[r];
@@ -241,14 +268,19 @@ static cudaError_t launch_mlx_bits(bool gemv, const void* w, const void* sc, con
     if ((group & (group - 1)) == 0) gshift = __builtin_ctz((unsigned)group);
     const long long per_cta = MLX_WARPS * MLX_ROWS;
     const int grid = (int)std::min<long long>((rows + per_cta - 1) / per_cta, 148ll * 16);
-    const size_t vsmem = ((size_t)k + k / 32) * 4;
+    const size_t vsmem = mlx_q4_smem_host(k);
     if (BITS == 4 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && group % 32 == 0 && k % 32 == 0 &&
-        vsmem <= 100 * 1024) {
+        vsmem <= 200 * 1024) {
       const bool h2 = ((reinterpret_cast<uintptr_t>(sc) | reinterpret_cast<uintptr_t>(bi)) & 1u) == 0;
-      const int vgrid = std::min(grid, 148 * 2);  // two resident CTAs per SM; the rest by grid stride
-      const cudaError_t e = h2 ? ensure_smem_attr<gemv_mlx_q4_vec_kernel<true>>(current_device(), 100 * 1024)
-                               : ensure_smem_attr<gemv_mlx_q4_vec_kernel<false>>(current_device(), 100 * 1024);
+      const int dev = current_device();
+      cudaError_t e = h2 ? ensure_smem_attr<gemv_mlx_q4_vec_kernel<true>>(dev, (int)vsmem)
+                         : ensure_smem_attr<gemv_mlx_q4_vec_kernel<false>>(dev, (int)vsmem);
       if (e != cudaSuccess) return e;
+      const int per_sm = h2 ? ctas_per_sm<gemv_mlx_q4_vec_kernel<true>>(dev, MLX_WARPS * 32, (int)vsmem)
+                            : ctas_per_sm<gemv_mlx_q4_vec_kernel<false>>(dev, MLX_WARPS * 32, (int)vsmem);
+      // One wave of CTAs, each warp an even share of the rows (at least MLX_ROWS rows per warp).
+      const long long need = (rows + MLX_WARPS * MLX_ROWS - 1) / (MLX_WARPS * MLX_ROWS);
+      const int vgrid = (int)std::min<long long>(need, (long long)sm_count(dev) * std::max(per_sm, 1));
       if (h2) gemv_mlx_q4_vec_kernel<true><<<vgrid, MLX_WARPS * 32, vsmem, st>>>(W, S, B, x, y, (int)rows, k, group, gshift, bf16);
       else gemv_mlx_q4_vec_kernel<false><<<vgrid, MLX_WARPS * 32, vsmem, st>>>(W, S, B, x, y, (int)rows, k, group, gshift, bf16);
     } else if (al) gemv_mlx_kernel<BITS, true><<<grid, MLX_WARPS * 32, 0, st>>>(W, S, B, x, y, (int)rows, k, group, gshift, bf16);
