@@ -163,3 +163,20 @@ def test_sample_odd_vocab(case):
     probs = d.cpu().numpy()
     for r in range(rows):
         check_row(lg[r], t, k, p, float(u[r]), int(tok[r]), probs[r])
+
+
+@pytest.mark.parametrize("rows,n", [(24, 128256), (2, 100001)])
+@pytest.mark.parametrize("case", [(0.0, 0, 0.0), (0.7, 50, 0.95), (1.0, 0, 0.9)])
+def test_sample_cluster_shapes(rows, n, case):
+    """Rows spread over 4 CTAs (24 rows of 128256) and over 8 CTAs with
+    scalar loads (an odd vocabulary): the same bar as one CTA per row."""
+    t, k, p = case
+    rng = np.random.default_rng(rows * 7 + n % 97 + k)
+    lg = (rng.standard_normal((rows, n)) * 3.0).astype(np.float32)
+    u = rng.random(rows, dtype=np.float32)
+    d = torch.from_numpy(lg).cuda()
+    tok = ops.sample(d, t, k, p, u).cpu().numpy()
+    ops.check_device_error()
+    probs = d.cpu().numpy()
+    for r in range(0, rows, 5 if rows > 8 else 1):
+        check_row(lg[r], t, k, p, float(u[r]), int(tok[r]), probs[r])

@@ -2,8 +2,11 @@
 // (src/runtime/sampler.zig:44-104) over logits that never leave HBM, so a
 // decode step reads back one int32 per sequence instead of f32[vocab].
 //
-// Pipeline per row (one 1024-thread CTA per row, logits rewritten in place as
-// the reference does):
+// Pipeline per row (a cluster of C 1024-thread CTAs per row, C = 8, 4 or 1
+// by row count and length; each CTA owns a contiguous slice; reductions,
+// histograms and prefix sums are folded across the cluster through
+// distributed shared memory between cluster barriers, in rank order so every
+// CTA holds the same bits; logits rewritten in place as the reference does):
 //   temperature == 0     -> argmax, first index of the maximum (math.zig:190-201)
 //   scale by 1/T         (sampler.zig:50-51; 1/T computed on the host in f32)
 //   top-k                (:54-63) the k-th largest value found by a 4-pass radix
@@ -27,7 +30,11 @@
 // order than the reference's sequential loops, so probabilities agree to a
 // few ulp and the token agrees unless u falls within that distance of a CDF
 // boundary; argmax, the top-k threshold and the set of kept ties are exact.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace vtb {
 
@@ -56,15 +63,19 @@ __device__ __forceinline__ float smp_unkey(uint32_t k) {
 }
 
 struct SmpShared {
-  uint32_t cnt[256];
+  uint32_t cnt[256];  // this CTA's radix histogram (read by the whole cluster)
   uint32_t sum[256];
   float red[32];
   int redi[32];
-  uint32_t prefix, mask, remaining;
+  float pub_f;        // this CTA's contribution to a cluster reduction
+  int pub_i;
+  long long pub_l;
+  uint32_t prefix, mask, remaining;  // radix walk state, identical in every CTA of the cluster
   unsigned long long above;
   int nocut;
-  float bcast;
-  int bcasti;
+  float bcast, cbf;
+  int bcasti, cbi;
+  long long cbl;
 };
 
 __device__ __forceinline__ float smp_block_sum(float v, SmpShared& sh) {
@@ -123,18 +134,57 @@ __device__ __forceinline__ int smp_block_int(int v, SmpShared& sh) {
   return sh.bcasti;
 }
 
-// One radix level, descending.  Warp 0 picks the highest bin at which the
-// running total (COUNT: sh.cnt against sh.remaining; else sh.sum added to
-// sh.above against target) is reached, and narrows prefix/mask to it; when
-// no bin reaches the target it sets sh.nocut.
-template <bool COUNT>
-__device__ __forceinline__ void smp_pick_bin(SmpShared& sh, int shift, unsigned long long target) {
+// Cluster-wide combination of a CTA-uniform value: every CTA publishes its
+// value, then each CTA folds all of them in rank order (ranks [0, upto) for a
+// prefix), so every CTA gets the same bits.  Two cluster barriers: one before
+// the reads, one before a slot can be rewritten.
+enum SmpOp { SMP_SUM, SMP_MAX, SMP_MIN };
+template <int C>
+__device__ __forceinline__ void smp_csync(cg::cluster_group& cl) {
+  if constexpr (C == 1) __syncthreads();
+  else cl.sync();
+}
+
+template <int C, SmpOp OP, typename T>
+__device__ __forceinline__ T smp_cluster(T v, T& pub, T& out, cg::cluster_group& cl, int upto = C) {
+  if constexpr (C == 1) return (OP == SMP_SUM && upto == 0) ? T(0) : v;  // one CTA: nothing to fold
+  if (threadIdx.x == 0) pub = v;
+  cl.sync();
+  if (threadIdx.x == 0) {
+    T acc = OP == SMP_SUM ? T(0) : *cl.map_shared_rank(&pub, 0);
+    for (int r = OP == SMP_SUM ? 0 : 1; r < upto; ++r) {
+      const T o = *cl.map_shared_rank(&pub, r);
+      acc = OP == SMP_SUM ? acc + o : (OP == SMP_MAX ? (o > acc ? o : acc) : (o < acc ? o : acc));
+    }
+    out = acc;
+  }
+  cl.sync();
+  return out;
+}
+
+// One radix level over the cluster's merged histograms, descending.  Warp 0
+// of every CTA sums the CTAs' bins (integers: any order gives the same
+// totals), picks the highest bin at which the running total (COUNT: counts
+// against sh.remaining; else sums added to sh.above against target) is
+// reached and narrows prefix/mask to it; with no such bin it sets sh.nocut.
+// The caller's cluster barriers bracket it.
+template <int C, bool COUNT>
+__device__ __forceinline__ void smp_pick_bin(SmpShared& sh, int shift, unsigned long long target,
+                                             cg::cluster_group& cl) {
   const int lane = threadIdx.x & 31;
   if (threadIdx.x < 32) {
     // lane l owns bins 255-8l down to 248-8l
+    unsigned long long v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0;
+    for (int r = 0; r < C; ++r) {
+      const uint32_t* rc = C == 1 ? (COUNT ? sh.cnt : sh.sum) : cl.map_shared_rank(COUNT ? sh.cnt : sh.sum, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += rc[255 - 8 * lane - j];
+    }
     unsigned long long s = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s += COUNT ? (unsigned long long)sh.cnt[255 - 8 * lane - j] : sh.sum[255 - 8 * lane - j];
+    for (int j = 0; j < 8; ++j) s += v[j];
     unsigned long long c = s;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -148,12 +198,12 @@ __device__ __forceinline__ void smp_pick_bin(SmpShared& sh, int shift, unsigned 
       if (lane == 0) sh.nocut = 1;
     } else if (lane == __ffs(ball) - 1) {
       unsigned long long run = c - s;  // total of the higher lanes' bins
-      int b = 255 - 8 * lane;
-      for (int j = 0; j < 8; ++j, --b) {
-        const unsigned long long v = COUNT ? (unsigned long long)sh.cnt[b] : sh.sum[b];
-        if (base + run + v >= need) break;
-        run += v;
+      int j = 0;
+      for (; j < 7; ++j) {
+        if (base + run + v[j] >= need) break;
+        run += v[j];
       }
+      const int b = 255 - 8 * lane - j;
       if (COUNT) sh.remaining -= (uint32_t)run;
       else sh.above += run;
       sh.prefix |= (uint32_t)b << shift;
@@ -178,48 +228,55 @@ __device__ __forceinline__ void smp_st(float* p, const float (&x)[V]) {
   else *p = x[0];
 }
 
-// V = 4: rows of a multiple of 4 floats on 16-byte boundaries, read as float4;
-// V = 1 otherwise.  The row keeps the raw logits until the softmax pass; 1/T
-// and 1/sum are re-applied on the fly (the same f32 products each time) so
-// the passes before it only read.
-template <int V>
-__global__ void __launch_bounds__(SMP_THREADS, 1)
+// A cluster of C CTAs (C SMs) samples one row: CTA `rank` owns the
+// contiguous units [u0, u1) (units of V floats; V = 4 for rows of a multiple
+// of 4 floats on 16-byte boundaries, read as float4).  Index order is (rank,
+// warp, step, lane, element), so the scans below walk the row in order.  The
+// row keeps the raw logits until the softmax pass; 1/T and 1/sum are
+// re-applied on the fly (the same f32 products each time).
+template <int V, int C>
+__global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(SMP_THREADS, 1)
 sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_constant__ SampleArgs a,
               int32_t* __restrict__ tokens) {
   __shared__ SmpShared sh;
   __shared__ float ftot[32];
-  float* L = logits + (long long)blockIdx.x * ld;
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = (int)cl.block_rank(), row = blockIdx.x / C;
+  float* L = logits + (long long)row * ld;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nu = n / V;  // units of V floats
+  const int nu = n / V;
+  const int u0 = (int)((long long)rank * nu / C), u1 = (int)((long long)(rank + 1) * nu / C);
 
   if (a.greedy) {  // argmax: largest value, first index on ties
     float bv = -INFINITY;
     int bi = n;
-    for (int u = tid; u < nu; u += SMP_THREADS) {
+    for (int u = u0 + tid; u < u1; u += SMP_THREADS) {
       float x[V];
       smp_ld<V>(L + u * V, x);
 #pragma unroll
       for (int k = 0; k < V; ++k)
         if (bi == n || x[k] > bv) { bv = x[k]; bi = u * V + k; }  // ascending: this thread's first maximum
     }
-    const float m = smp_block_max(bv, sh);
-    const int idx = smp_block_int<true>((bv == m && bi < n) ? bi : n, sh);
-    if (tid == 0) tokens[blockIdx.x] = idx < n ? idx : 0;
+    const float mc = smp_block_max(bv, sh);
+    const int ic = smp_block_int<true>((bv == mc && bi < n) ? bi : n, sh);
+    const float m = smp_cluster<C, SMP_MAX>(mc, sh.pub_f, sh.cbf, cl);
+    const int idx = smp_cluster<C, SMP_MIN>(mc == m ? ic : n, sh.pub_i, sh.cbi, cl);
+    if (rank == 0 && tid == 0) tokens[row] = idx < n ? idx : 0;
     return;
   }
 
   // Maximum of the scaled logits (masking keeps it, so it is the softmax's).
   const float inv_t = a.inv_t;
   float mx = -INFINITY;
-  for (int u = tid; u < nu; u += SMP_THREADS) {
+  for (int u = u0 + tid; u < u1; u += SMP_THREADS) {
     float x[V];
     smp_ld<V>(L + u * V, x);
 #pragma unroll
     for (int k = 0; k < V; ++k) mx = fmaxf(mx, x[k] * inv_t);
   }
-  mx = smp_block_max(mx, sh);
+  mx = smp_cluster<C, SMP_MAX>(smp_block_max(mx, sh), sh.pub_f, sh.cbf, cl);
 
-  // top-k threshold: the k-th largest scaled value.
+  // top-k threshold: the k-th largest scaled value of the whole row.
   float thr = -INFINITY;
   const bool use_k = a.top_k > 0 && a.top_k < n;
   if (use_k) {
@@ -228,7 +285,7 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
       for (int b = tid; b < 256; b += SMP_THREADS) sh.cnt[b] = 0u;
       __syncthreads();
       const uint32_t pre = sh.prefix, msk = sh.mask;
-      for (int u = tid; u < nu; u += SMP_THREADS) {
+      for (int u = u0 + tid; u < u1; u += SMP_THREADS) {
         float x[V];
         smp_ld<V>(L + u * V, x);
 #pragma unroll
@@ -237,15 +294,16 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
           if ((key & msk) == pre) atomicAdd(&sh.cnt[(key >> shift) & 255u], 1u);
         }
       }
-      __syncthreads();
-      smp_pick_bin<true>(sh, shift, 0ull);
+      smp_csync<C>(cl);  // every CTA's histogram is complete
+      smp_pick_bin<C, true>(sh, shift, 0ull, cl);
+      smp_csync<C>(cl);  // nobody reads a histogram any more
     }
     thr = smp_unkey(sh.prefix);
   }
 
   // softmax numerators (masked entries are exp(-inf) = 0 in the reference).
   float s = 0.f;
-  for (int u = tid; u < nu; u += SMP_THREADS) {
+  for (int u = u0 + tid; u < u1; u += SMP_THREADS) {
     float x[V];
     smp_ld<V>(L + u * V, x);
 #pragma unroll
@@ -256,12 +314,12 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
     }
     smp_st<V>(L + u * V, x);
   }
-  const float inv = 1.0f / smp_block_sum(s, sh);  // its barriers publish the numerators
+  const float inv = 1.0f / smp_cluster<C, SMP_SUM>(smp_block_sum(s, sh), sh.pub_f, sh.cbf, cl);
 
-  // Warp w owns the contiguous units [w*cw, w*cw + cw), walked 32 units (one
-  // coalesced load per lane) at a time, so index order is (step, lane, k).
-  const int cw = ((nu + SMP_THREADS - 1) / SMP_THREADS) * 32;
-  const int w0 = min(nu, warp * cw), w1 = min(nu, w0 + cw);
+  // Warp w owns the contiguous units [w0, w1) of this CTA's slice, walked 32
+  // units (one coalesced load per lane) at a time.
+  const int cw = ((u1 - u0 + SMP_THREADS - 1) / SMP_THREADS) * 32;
+  const int w0 = min(u1, u0 + warp * cw), w1 = min(u1, w0 + cw);
   float renorm = 1.f;
   bool use_renorm = false;
   if (a.use_p) {  // nucleus over p = e * inv
@@ -270,9 +328,9 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int b = tid; b < 256; b += SMP_THREADS) { sh.cnt[b] = 0u; sh.sum[b] = 0u; }
       __syncthreads();
-      if (sh.nocut) break;
+      if (sh.nocut) break;  // identical in every CTA
       const uint32_t pre = sh.prefix, msk = sh.mask;
-      for (int u = tid; u < nu; u += SMP_THREADS) {
+      for (int u = u0 + tid; u < u1; u += SMP_THREADS) {
         float x[V];
         smp_ld<V>(L + u * V, x);
 #pragma unroll
@@ -286,8 +344,9 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
           }
         }
       }
-      __syncthreads();
-      smp_pick_bin<false>(sh, shift, target);
+      smp_csync<C>(cl);
+      smp_pick_bin<C, false>(sh, shift, target, cl);
+      smp_csync<C>(cl);
     }
     const bool nocut = sh.nocut != 0;
     const uint32_t kstar = sh.prefix;
@@ -299,7 +358,7 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
       keep_ties = vfx ? (long long)((rest + vfx - 1) / vfx) : 1;
       if (keep_ties < 1) keep_ties = 1;
     }
-    // Rank of this warp's first tie among all ties, in index order.
+    // Rank of this warp's first tie among all ties of the row, in index order.
     int my_ties = 0;
     if (!nocut)
       for (int j = w0; j < w1; j += 32) {
@@ -315,10 +374,14 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
     for (int o = 16; o; o >>= 1) my_ties += __shfl_xor_sync(0xffffffffu, my_ties, o);
     if (lane == 0) sh.redi[warp] = my_ties;
     __syncthreads();
-    long long rank = 0;
-    for (int w = 0; w < warp; ++w) rank += sh.redi[w];
+    long long rank_in = 0, cta_ties = 0;
+    for (int w = 0; w < 32; ++w) {
+      if (w < warp) rank_in += sh.redi[w];
+      cta_ties += sh.redi[w];
+    }
     __syncthreads();
-    // Keep or zero each p; the row now holds the nucleus probabilities.
+    long long tie_rank = rank_in + smp_cluster<C, SMP_SUM>(cta_ties, sh.pub_l, sh.cbl, cl, rank);
+    // Keep or zero each p; the slice now holds the nucleus probabilities.
     float kept = 0.f;
     for (int j = w0; j < w1; j += 32) {
       const int u = j + lane;
@@ -338,7 +401,7 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
       const int step_ties = __shfl_sync(0xffffffffu, ex, 31);
       ex -= tl;
       if (u < w1) {
-        long long r = rank + ex;
+        long long r = tie_rank + ex;
 #pragma unroll
         for (int k = 0; k < V; ++k) {
           const uint32_t key = __float_as_uint(x[k]);
@@ -352,14 +415,14 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
         }
         smp_st<V>(L + u * V, x);
       }
-      rank += step_ties;
+      tie_rank += step_ties;
     }
-    const float tot = smp_block_sum(kept, sh);  // its barriers publish the row
+    const float tot = smp_cluster<C, SMP_SUM>(smp_block_sum(kept, sh), sh.pub_f, sh.cbf, cl);
     if (tot > 0.f) { use_renorm = true; renorm = 1.0f / tot; }
   }
 
-  // CDF walk: final probabilities written back, warp totals, an exclusive
-  // scan over warps, then each warp scans its range until the sum reaches u.
+  // CDF walk: final probabilities written back, warp totals, the mass of the
+  // lower CTAs and warps, then each warp scans its range until the sum reaches u.
   float cs = 0.f;
   int last = -1;
   for (int j = w0; j < w1; j += 32) {
@@ -380,10 +443,14 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
 #pragma unroll
   for (int o = 16; o; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
   if (lane == 0) ftot[warp] = cs;
-  __syncthreads();  // also publishes the final row
-  float acc = 0.f;
-  for (int w = 0; w < warp; ++w) acc += ftot[w];
-  const float ud = a.u[blockIdx.x];
+  __syncthreads();  // also publishes this CTA's final slice
+  float cta_mass = 0.f, acc = 0.f;
+  for (int w = 0; w < 32; ++w) {
+    if (w == warp) acc = cta_mass;
+    cta_mass += ftot[w];
+  }
+  acc += smp_cluster<C, SMP_SUM>(cta_mass, sh.pub_f, sh.cbf, cl, rank);
+  const float ud = a.u[row];
   int cand = n;
   for (int j = w0; j < w1; j += 32) {
     const int u = j + lane;
@@ -418,9 +485,9 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
     }
     acc += __shfl_sync(0xffffffffu, inc, 31);
   }
-  cand = smp_block_int<true>(cand, sh);
-  last = smp_block_int<false>(last, sh);
-  if (tid == 0) tokens[blockIdx.x] = cand < n ? cand : (last >= 0 ? last : 0);
+  cand = smp_cluster<C, SMP_MIN>(smp_block_int<true>(cand, sh), sh.pub_i, sh.cbi, cl);
+  last = smp_cluster<C, SMP_MAX>(smp_block_int<false>(last, sh), sh.pub_i, sh.cbi, cl);
+  if (rank == 0 && tid == 0) tokens[row] = cand < n ? cand : (last >= 0 ? last : 0);
 }
 
 // Host side: argument checks happen in the extern "C" wrappers.
@@ -434,8 +501,23 @@ cudaError_t launch_sample(float* logits, long long ld, int rows, int n, float te
   a.use_p = top_p > 0.0f && top_p < 1.0f;
   for (int r = 0; r < rows; ++r) a.u[r] = u ? u[r] : 0.f;
   const bool vec = n % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
-  if (vec) sample_kernel<4><<<rows, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
-  else sample_kernel<1><<<rows, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+  // CTAs per row: as many as keep every row's cluster in one wave of the GPU
+  // and give each CTA at least 12k values (below that the cluster barriers
+  // cost more than the extra SMs' bandwidth returns).
+  const int sms = sm_count(current_device());
+  int C = 1;
+  if (rows * 8 <= sms && n >= 8 * 12288) C = 8;
+  else if (rows * 4 <= sms && n >= 4 * 12288) C = 4;
+  const dim3 grid(rows * C);
+  if (vec) {
+    if (C == 8) sample_kernel<4, 8><<<grid, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+    else if (C == 4) sample_kernel<4, 4><<<grid, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+    else sample_kernel<4, 1><<<grid, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+  } else {
+    if (C == 8) sample_kernel<1, 8><<<grid, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+    else if (C == 4) sample_kernel<1, 4><<<grid, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+    else sample_kernel<1, 1><<<grid, SMP_THREADS, 0, st>>>(logits, ld, n, a, tokens);
+  }
   return cudaGetLastError();
 }
 
