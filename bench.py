@@ -235,6 +235,97 @@ def time_graph(build, replays: int, stream):
     return e0.elapsed_time(e1) / replays
 
 
+def mlx_gemv(dev, hbm: float, cpu_threads: int) -> dict:
+    """MLX affine 4-bit GEMV (mlx.zig:283-330 matmulQ4; Metal matmul_mlx_q4,
+    bridge.m:245-291) at 14336 x 4096, group 64, bf16 scales: 8 weight copies
+    (264 MB > L2) in a CUDA graph; oracle parity and rate on 512 rows."""
+    import torch
+    import oracle as O
+    from vantablack_b200 import ops, synth as S
+    m, k, g = 14336, 4096, 64
+    rng = np.random.default_rng(3)
+    hw, hs, hb = S.mlx_tensor(rng, m, k, 4, g, True)
+    base = tuple(torch.from_numpy(a).to(dev) for a in (hw, hs, hb))
+    copies = [base] + [tuple(t.clone() for t in base) for _ in range(7)]
+    hx = S.activations(rng, k)
+    x = torch.from_numpy(hx).to(dev)
+    nbytes = hw.nbytes + hs.nbytes + hb.nbytes
+    stream = torch.cuda.Stream(device=dev)
+
+    def build():
+        for c in copies:
+            ops.gemv_mlx(*c, x, m, k, 4, g, True)
+    ms = time_graph(build, 10, stream)
+    gbs = nbytes * len(copies) / (ms / 1e3) / 1e9
+    y0 = ops.gemv_mlx(*base, x, m, k, 4, g, True).cpu().numpy()
+    rows = 512
+    O.set_threads(cpu_threads)
+    sw, ss = hw[:rows * k // 2], hs[:rows * (k // g) * 2]
+    sb = hb[:rows * (k // g) * 2]
+    ref = O.mlx_matmul(sw, ss, sb, hx, rows, k, 4, g, True)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 0.5:
+        O.mlx_matmul(sw, ss, sb, hx, rows, k, 4, g, True)
+        n += 1
+    cpu_s = (time.perf_counter() - t0) / n
+    ops.check_device_error()
+    return {"shape": f"{m}x{k}", "group": g, "scales": "bf16", "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4),
+            "us_per_launch": round(ms * 1e3 / len(copies), 2), "bytes_per_launch": nbytes,
+            "max_rel_err_vs_oracle": float(np.abs(y0[:rows] - ref).max() / np.abs(ref).max()),
+            "oracle_rows_checked": rows,
+            "cpu_gbs_single_thread": round((sw.nbytes + ss.nbytes + sb.nbytes) / cpu_s / 1e9, 2)}
+
+
+def sampler_leg(dev, cpu_threads: int) -> dict:
+    """Device sampler (Sampler.sample, sampler.zig:44-104) at the Llama-3-8B
+    vocabulary, batch 1 and 32: CUDA-event time per launch over 20 launches in
+    a CUDA graph (replays re-sample the rows the first replay rewrote), the
+    f32[vocab] read-back it replaces, and token parity with the oracle on
+    fresh rows with the same draws."""
+    import torch
+    import oracle as O
+    from vantablack_b200 import ops
+    V = 128256
+    stream = torch.cuda.Stream(device=dev)
+    gen = torch.Generator(device=dev).manual_seed(4)
+    out = {}
+    for rows in (1, 32):
+        lg = torch.randn(rows, V, device=dev, generator=gen) * 3
+        u = np.random.default_rng(rows).random(rows, dtype=np.float32)
+        for name, cfg in (("greedy", (0.0, 0, 0.0)), ("temp0.8", (0.8, 0, 0.0)),
+                          ("temp0.7_k50_p0.95", (0.7, 50, 0.95))):
+            bufs = [lg.clone() for _ in range(20)]
+
+            def build():
+                for b in bufs:
+                    ops.sample(b, *cfg, u)
+            ms = time_graph(build, 5, stream)
+            fresh = lg.clone()
+            tok = ops.sample(fresh, *cfg, u).cpu().numpy()
+            host = lg.cpu().numpy()
+            probs = fresh.cpu().numpy()
+            agree, checked = 0, 0
+            for r in range(min(rows, 4)):
+                otok, op = O.sample(host[r], *cfg, float(u[r]))
+                c = np.cumsum(op.astype(np.float64))
+                if cfg[0] == 0.0 or np.abs(c - u[r]).min() >= 1e-3:
+                    checked += 1
+                    agree += int(otok == int(tok[r]))
+            out[f"b{rows}_{name}"] = {"us_per_launch": round(ms * 1e3 / 20, 2), "tokens_equal_oracle": agree,
+                                      "rows_checked": checked}
+        h = torch.empty(rows, V, pin_memory=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(10):
+                h.copy_(lg, non_blocking=True)
+            e1.record(stream)
+            e1.synchronize()
+        out[f"b{rows}_logits_d2h_us"] = round(e0.elapsed_time(e1) * 1e3 / 10, 2)
+    ops.check_device_error()
+    return out
+
+
 def gemv_sweep(dev, hbm: float, cpu_threads: int) -> dict:
     """Q6_K / Q8_0 / Q8_0xQ8_0 / Q5_K GEMVs at the Llama-3-8B decode shapes
     (simd.zig:159-190, 406-434, 290-347; dot_i8 :40-62 for the int8 variant), each a PDL
@@ -664,6 +755,8 @@ def run_ours(args):
         leg("gemv_sweep", lambda: gemv_sweep(dev, hbm, cores))
         leg("prefill_gemm", lambda: prefill_gemm(dev, bf16, cores))
         leg("tinyllama", lambda: tinyllama(local, hbm, cores))
+        leg("mlx_q4_gemv", lambda: mlx_gemv(dev, hbm, cores))
+        leg("sampler", lambda: sampler_leg(dev, cores))
     if args.model_steps > 0:
         leg("llama3_8b", lambda: llama3_8b(rank, world, local, dist, args, hbm, cores))
 
