@@ -80,3 +80,16 @@ def test_sampler_argument_checks_without_launch(lib):
     assert lib.vtb_cuda_sample(p, 1, 8, 8, ctypes.byref(cfg), None, p, None) == -1  # no draws
     assert lib.vtb_cuda_sample(p, 1, 8, 8, None, u, p, None) == -1
     assert lib.vtb_cuda_state_sample(None, 1, ctypes.byref(cfg), u, p) == -1
+
+
+def test_mlx_argument_checks_without_launch(lib):
+    """MLX entry points reject unsupported widths and group sizes on the host."""
+    buf = ctypes.create_string_buffer(256)
+    p = (ctypes.addressof(buf) + 15) & ~15
+    assert lib.vtb_cuda_gemv_mlx(p, p, p, p, p, 4, 64, 7, 64, 0, None) == -8      # 7 bits
+    assert lib.vtb_cuda_gemv_mlx(p, p, p, p, p, 4, 64, 4, 48, 0, None) == -1      # group does not divide k
+    assert lib.vtb_cuda_gemv_mlx(p, p, p, p, p, 4, 60, 3, 15, 0, None) == -1      # group not a multiple of 10
+    assert lib.vtb_cuda_gemv_mlx(p, p, p, p + 4, p, 4, 64, 4, 64, 0, None) == -1  # x not 16-byte aligned
+    assert lib.vtb_cuda_gemv_mlx(None, p, p, p, p, 4, 64, 4, 64, 0, None) == -1
+    assert lib.vtb_cuda_dequant_mlx(p, p, p, None, 4, 64, 4, 64, 0, None) == -1
+    assert lib.vtb_cuda_matmul_mlx_q4(None, None, None, 0, None, 0, None, 0, None, 0, 4, 64, 64, 0) == -1

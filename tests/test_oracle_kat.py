@@ -264,3 +264,66 @@ def test_mlx_unsupported_bits():
     with pytest.raises(ValueError):
         O.mlx_matmul(np.zeros(16, np.uint8), np.zeros(2, np.uint8), np.zeros(2, np.uint8), np.zeros(8, np.float32),
                      1, 8, 7, 8, False)
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 5, 6, 8])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_mlx_oracle_vs_numpy(bits, bf16):
+    """The C restatement of mlx.zig against an independent numpy unpacking of
+    the same layout (u32 words, 32 // bits values low bits first, per-group
+    f16/bf16 scale and bias): dequant bit-exact, matmul within 1e-5."""
+    from vantablack_b200 import synth as S
+    el = 32 // bits
+    group = 64 if 64 % el == 0 else 32 * el  # a multiple of 32 / bits values
+    rng = np.random.default_rng(bits * 2 + bf16)
+    m, k = 7, 4 * group
+    w, sc, bi = S.mlx_tensor(rng, m, k, bits, group, bf16)
+    words = np.frombuffer(w.tobytes(), "<u4").reshape(m, k // el)
+    shifts = (np.arange(el, dtype=np.uint32) * bits)
+    q = ((words[:, :, None] >> shifts) & ((1 << bits) - 1)).reshape(m, k).astype(np.float32)
+    def dec(b):
+        h = np.frombuffer(b.tobytes(), "<u2").reshape(m, k // group)
+        return (h.astype(np.uint32) << 16).view(np.float32) if bf16 else h.view(np.float16).astype(np.float32)
+    s = np.repeat(dec(sc), group, axis=1)
+    b = np.repeat(dec(bi), group, axis=1)
+    want = q * s + b  # f32 multiply then add, as dequantRow does
+    got = O.mlx_dequant(w, sc, bi, m, k, bits, group, bf16)
+    assert np.array_equal(got.view(np.uint32), want.astype(np.float32).view(np.uint32))
+    x = rng.standard_normal(k).astype(np.float32)
+    y = O.mlx_matmul(w, sc, bi, x, m, k, bits, group, bf16)
+    ref = want.astype(np.float64) @ x.astype(np.float64)
+    assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_sampler_random_vs_float64():
+    """Sampler.sample on random logits against a float64 restatement: the kept
+    set and the token agree wherever rounding cannot decide them."""
+    rng = np.random.default_rng(17)
+    checked = 0
+    for trial in range(40):
+        n = int(rng.integers(50, 3000))
+        lg = (rng.standard_normal(n) * rng.uniform(0.5, 4)).astype(np.float32)
+        t = float(rng.uniform(0.3, 1.5))
+        k = int(rng.integers(0, n)) if trial % 3 else 0
+        p = float(rng.uniform(0.2, 0.99)) if trial % 2 else 0.0
+        u = float(rng.random())
+        tok, probs = O.sample(lg, t, k, p, u)
+        z = lg.astype(np.float64) * np.float32(1 / np.float32(t))
+        if 0 < k < n:
+            z[z < np.sort(z)[::-1][k - 1]] = -np.inf
+        q = np.exp(z - z.max()); q /= q.sum()
+        if 0 < p < 1:
+            order = sorted(range(n), key=lambda i: (-q[i], i))
+            c = np.cumsum(q[order])
+            if np.abs(c - p).min() < 1e-4:
+                continue
+            cut = int(np.argmax(c >= p)) + 1
+            q[np.asarray(order[cut:], dtype=int)] = 0
+            q /= q.sum()
+        cdf = np.cumsum(q)
+        if np.abs(cdf - u).min() < 1e-4:
+            continue
+        assert np.array_equal(probs > 0, q > 0)
+        assert tok == int(np.argmax(cdf >= u))
+        checked += 1
+    assert checked >= 25
