@@ -27,9 +27,12 @@
 //
 // The uniform draw u (the reference's prng.random().float(f32), :92) is an
 // argument: the caller owns the generator.  Sums are formed in a different
-// order than the reference's sequential loops, so probabilities agree to a
-// few ulp and the token agrees unless u falls within that distance of a CDF
-// boundary; argmax, the top-k threshold and the set of kept ties are exact.
+// order than the reference's sequential f32 loops (whose own rounding drifts
+// ~3e-4 relative over a 128k vocabulary; these sums sit closer to exact), so
+// probabilities agree to that level, the nucleus set agrees except for
+// entries whose preceding mass is that close to top_p, and the token agrees
+// unless u falls that close to a CDF boundary; argmax and the top-k threshold
+// are exact.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
