@@ -68,6 +68,7 @@ __device__ __forceinline__ float smp_unkey(uint32_t k) {
 struct SmpShared {
   uint32_t cnt[256];  // this CTA's radix histogram (read by the whole cluster)
   uint32_t sum[256];
+  uint32_t merged[256];  // the cluster's histogram, folded here before a pick
   float red[32];
   int redi[32];
   float pub_f;        // this CTA's contribution to a cluster reduction
@@ -165,26 +166,32 @@ __device__ __forceinline__ T smp_cluster(T v, T& pub, T& out, cg::cluster_group&
   return out;
 }
 
-// One radix level over the cluster's merged histograms, descending.  Warp 0
-// of every CTA sums the CTAs' bins (integers: any order gives the same
-// totals), picks the highest bin at which the running total (COUNT: counts
-// against sh.remaining; else sums added to sh.above against target) is
-// reached and narrows prefix/mask to it; with no such bin it sets sh.nocut.
-// The caller's cluster barriers bracket it.
+// One radix level over the cluster's merged histograms, descending.  256
+// threads each fold one bin over the cluster's CTAs (integers: any order gives
+// the same totals); then warp 0 of every CTA picks the highest bin at which
+// the running total (COUNT: counts against sh.remaining; else sums added to
+// sh.above against target) is reached and narrows prefix/mask to it; with no
+// such bin it sets sh.nocut.  The caller's cluster barriers bracket it.
 template <int C, bool COUNT>
 __device__ __forceinline__ void smp_pick_bin(SmpShared& sh, int shift, unsigned long long target,
                                              cg::cluster_group& cl) {
   const int lane = threadIdx.x & 31;
+  const uint32_t* hist = COUNT ? sh.cnt : sh.sum;
+  if constexpr (C > 1) {
+    if (threadIdx.x < 256) {
+      uint32_t t = 0;
+#pragma unroll
+      for (int r = 0; r < C; ++r) t += cl.map_shared_rank(hist, r)[threadIdx.x];
+      sh.merged[threadIdx.x] = t;
+    }
+    __syncthreads();
+    hist = sh.merged;
+  }
   if (threadIdx.x < 32) {
     // lane l owns bins 255-8l down to 248-8l
     unsigned long long v[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = 0;
-    for (int r = 0; r < C; ++r) {
-      const uint32_t* rc = C == 1 ? (COUNT ? sh.cnt : sh.sum) : cl.map_shared_rank(COUNT ? sh.cnt : sh.sum, r);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] += rc[255 - 8 * lane - j];
-    }
+    for (int j = 0; j < 8; ++j) v[j] = hist[255 - 8 * lane - j];
     unsigned long long s = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) s += v[j];
@@ -329,7 +336,7 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
     const unsigned long long target = (unsigned long long)ceil((double)a.top_p * (double)SMP_FX);
     if (tid == 0) { sh.prefix = 0u; sh.mask = 0u; sh.above = 0ull; sh.nocut = 0; }
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = tid; b < 256; b += SMP_THREADS) { sh.cnt[b] = 0u; sh.sum[b] = 0u; }
+      for (int b = tid; b < 256; b += SMP_THREADS) sh.sum[b] = 0u;
       __syncthreads();
       if (sh.nocut) break;  // identical in every CTA
       const uint32_t pre = sh.prefix, msk = sh.mask;
@@ -340,11 +347,7 @@ sample_kernel(float* __restrict__ logits, long long ld, int n, const __grid_cons
         for (int k = 0; k < V; ++k) {
           const float p = x[k] * inv;
           const uint32_t key = __float_as_uint(p);  // p >= +0: the raw bits order like the values
-          if ((key & msk) == pre) {
-            const uint32_t b = (key >> shift) & 255u;
-            atomicAdd(&sh.cnt[b], 1u);
-            atomicAdd(&sh.sum[b], __float2uint_rn(p * SMP_FX));
-          }
+          if ((key & msk) == pre) atomicAdd(&sh.sum[(key >> shift) & 255u], __float2uint_rn(p * SMP_FX));
         }
       }
       smp_csync<C>(cl);
